@@ -1,0 +1,286 @@
+"""Drop-in for the reference's pybind module ``comfyui_turing_utils_kernel._C``.
+
+Same function names, argument names, defaults and checks as
+kernel/csrc/bindings.cpp:851-935; the work goes through the C ABI of
+libturing_b200.so (sm_100a kernels).  Outputs are allocated here with torch and
+written in place by the kernels, on PyTorch's current stream of the input's
+device (the reference's TorchOpContext, bindings.cpp:17-31).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream_of
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_cuda_2d(t: torch.Tensor, name: str) -> None:
+    # bindings.cpp:93-97
+    _check(t.is_cuda, f"{name} must be a CUDA tensor")
+    _check(t.dim() == 2, f"{name} must be 2D")
+    _check(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def _require_blackwell(device: torch.device, what: str) -> None:
+    major, _ = torch.cuda.get_device_capability(device)
+    _check(major == 10, f"{what} requires an sm_100 (B200) device for this build")
+
+
+def _as_f32_vec(t: torch.Tensor) -> torch.Tensor:
+    return t.reshape(-1).to(torch.float32).contiguous()
+
+
+# ------------------------------------------------------------------ linears
+
+def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=None,
+                       tile_policy=0):
+    """bindings.cpp:371-421."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = _as_f32_vec(activation_scale)
+    weight_scale = _as_f32_vec(weight_scale)
+    if bias is not None:
+        bias = _as_f32_vec(bias)
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check(activation.dtype == torch.int8 and weight.dtype == torch.int8,
+           "Turing INT8 linear activation and weight must be int8")
+    _check(activation.device == weight.device and activation.device == activation_scale.device
+           and activation.device == weight_scale.device,
+           "Turing INT8 linear tensors must use the same CUDA device")
+    _check(weight.size(1) == activation.size(1), "INT8 linear K dimensions must match")
+    _check(activation.size(1) % 16 == 0 and weight.size(0) % 8 == 0,
+           "Turing INT8 linear requires K%16=0 and N%8=0")
+    _check(activation_scale.numel() == activation.size(0),
+           "activation_scale must contain one value per row")
+    _check(weight_scale.numel() == weight.size(0),
+           "weight_scale must contain one value per output channel")
+    if bias is not None:
+        _check(bias.is_cuda and bias.device == activation.device
+               and bias.numel() == weight.size(0),
+               "bias must contain one value per output channel on the same CUDA device")
+    m, k = activation.shape
+    n = weight.size(0)
+    with torch.cuda.device(activation.device):
+        _require_blackwell(activation.device, "turing_int8_linear")
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=activation.device)
+        call("tb_int8_linear", ptr(activation), ptr(weight), ptr(activation_scale),
+             ptr(weight_scale), ptr(bias), ptr(out), m, n, k, n, int(tile_policy),
+             stream_of(activation))
+    return out
+
+
+def turing_int8_gemm_s32(activation, weight):
+    """Exact INT32 accumulators [M, N] (the INT32 GEMM the plugin pairs with
+    turing_dequantize_int8_bf16, dispatch.py:481-535)."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check(activation.dtype == torch.int8 and weight.dtype == torch.int8,
+           "INT8 GEMM activation and weight must be int8")
+    _check(weight.size(1) == activation.size(1), "INT8 GEMM K dimensions must match")
+    m, k = activation.shape
+    n = weight.size(0)
+    _check(k % 16 == 0 and n % 4 == 0, "INT8 GEMM requires K%16=0 and N%4=0")
+    with torch.cuda.device(activation.device):
+        _require_blackwell(activation.device, "turing_int8_gemm_s32")
+        acc = torch.empty((m, n), dtype=torch.int32, device=activation.device)
+        call("tb_int8_gemm_s32", ptr(activation), ptr(weight), ptr(acc), m, n, k, n,
+             stream_of(activation))
+    return acc
+
+
+def turing_codebook_w4a8_linear(activation, weight, activation_scale, group_scale,
+                                channel_scale, codebook, bias=None, group_size=16, chunk_rows=0,
+                                tile_policy=0):
+    """bindings.cpp:262-369.  On sm_100a every shape decodes through the bounded
+    staged workspace (the reference's inline CUTLASS iterator is an sm75 tile
+    policy; both forms are bit-exact with each other, validate_compatible.py:175-210)."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = _as_f32_vec(activation_scale)
+    group_scale = group_scale.contiguous()
+    channel_scale = _as_f32_vec(channel_scale)
+    codebook = _as_f32_vec(codebook)
+    if bias is not None:
+        bias = _as_f32_vec(bias)
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check_cuda_2d(group_scale, "group_scale")
+    _check(activation.dtype == torch.int8, "activation must be int8")
+    _check(weight.dtype == torch.int8, "weight must use packed int8 storage")
+    _check(group_scale.dtype == torch.uint8, "group_scale must contain raw float8_e4m3fn bytes")
+    dev = activation.device
+    _check(weight.device == dev and group_scale.device == dev and activation_scale.device == dev
+           and channel_scale.device == dev and codebook.device == dev,
+           "all codebook W4A8 tensors must use the same CUDA device")
+    m, k = activation.shape
+    n = weight.size(0)
+    _check(m > 0 and n > 0 and k > 0, "codebook W4A8 dimensions must be positive")
+    _check(k % 16 == 0 and n % 8 == 0,
+           "codebook W4A8 requires K divisible by 16 and N divisible by 8")
+    _check(weight.size(1) * 2 == k, "packed weight K must match activation K")
+    _check(group_size >= 4 and k % group_size == 0
+           and (16 % group_size == 0 or group_size % 16 == 0),
+           "unsupported codebook W4A8 group_size")
+    _check(group_scale.size(0) == n and group_scale.size(1) == k // group_size,
+           "group_scale must have shape [N, K/group_size]")
+    _check(activation_scale.numel() == m,
+           "activation_scale must contain one value per activation row")
+    _check(channel_scale.numel() == n, "channel_scale must contain one value per output channel")
+    _check(codebook.numel() == 16, "codebook must contain 16 float32 values")
+    if bias is not None:
+        _check(bias.is_cuda and bias.device == dev, "bias must use the activation CUDA device")
+        _check(bias.numel() == n, "bias must contain one value per output channel")
+    _check(chunk_rows >= -1, "chunk_rows must be -1, 0, or a positive multiple of 8")
+    inline_eligible = group_size == 16 and m > 8192 and chunk_rows <= 0
+    _check(chunk_rows != -1 or inline_eligible,
+           "forced inline codebook W4A8 requires group_size=16 and M>8192")
+    if chunk_rows <= 0:
+        chunk_rows = min(n, 4096)
+    else:
+        _check(chunk_rows % 8 == 0, "chunk_rows must be divisible by 8")
+        chunk_rows = min(n, chunk_rows)
+    with torch.cuda.device(dev):
+        _require_blackwell(dev, "turing_codebook_w4a8_linear")
+        workspace = torch.empty((chunk_rows, k), dtype=torch.int8, device=dev)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        call("tb_codebook_w4a8_linear", ptr(activation), ptr(weight), ptr(activation_scale),
+             ptr(group_scale), ptr(channel_scale), ptr(codebook), ptr(bias), ptr(workspace),
+             chunk_rows, ptr(out), m, n, k, int(group_size), 0, int(tile_policy),
+             stream_of(activation))
+    return out
+
+
+def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, output_columns=-1):
+    """bindings.cpp:423-467."""
+    accumulator = accumulator.contiguous()
+    activation_scale = _as_f32_vec(activation_scale)
+    weight_scale = _as_f32_vec(weight_scale)
+    _check_cuda_2d(accumulator, "accumulator")
+    _check(accumulator.dtype == torch.int32, "accumulator must be int32")
+    _check(activation_scale.is_cuda and weight_scale.is_cuda, "scales must be CUDA tensors")
+    _check(accumulator.device == activation_scale.device
+           and accumulator.device == weight_scale.device,
+           "accumulator and scales must use the same CUDA device")
+    rows, acc_cols = accumulator.shape
+    if output_columns < 0:
+        output_columns = acc_cols
+    _check(rows > 0 and acc_cols > 0, "INT8 BF16 epilogue dimensions must be positive")
+    _check(0 < output_columns <= acc_cols,
+           "output_columns must be positive and no larger than the accumulator width")
+    _check(activation_scale.numel() == rows,
+           "activation_scale must contain one value per accumulator row")
+    _check(weight_scale.numel() == 1 or weight_scale.numel() == output_columns,
+           "weight_scale must be scalar or contain one value per output column")
+    with torch.cuda.device(accumulator.device):
+        _require_blackwell(accumulator.device, "INT8 BF16 epilogue")
+        out = torch.empty((rows, output_columns), dtype=torch.bfloat16, device=accumulator.device)
+        call("tb_dequantize_int8_bf16", ptr(accumulator), acc_cols, ptr(activation_scale),
+             ptr(weight_scale), weight_scale.numel(), ptr(out), rows, output_columns,
+             stream_of(accumulator))
+    return out
+
+
+# ---------------------------------------------------------- ConvRot quantizers
+
+def _rowbuffer(input, group_size, swiglu, int4, gelu, forced_threads=0):
+    input = input.contiguous()
+    _check_cuda_2d(input, "input")
+    label = "BF16 GELU row-buffer" if gelu else "BF16 row-buffer"
+    _check(input.dtype == torch.bfloat16, f"{label} ConvRot input must be bfloat16")
+    _check(group_size == 256, f"{label} ConvRot only supports group_size=256")
+    rows, cols = input.shape
+    _check(not swiglu or cols % 2 == 0, "SwiGLU BF16 row-buffer ConvRot input width must be even")
+    hidden = cols // 2 if swiglu else cols
+    _check(rows > 0 and hidden > 0 and hidden % group_size == 0,
+           f"{label} ConvRot width must be positive and divisible by 256")
+    with torch.cuda.device(input.device):
+        _require_blackwell(input.device, f"{label} ConvRot")
+        out = torch.empty((rows, hidden // 2 if int4 else hidden), dtype=torch.int8,
+                          device=input.device)
+        scales = torch.empty((rows, 1), dtype=torch.float32, device=input.device)
+        s = stream_of(input)
+        if gelu:
+            call("tb_bf16_gelu_int4_convrot_quantize" if int4 else
+                 "tb_bf16_gelu_int8_convrot_quantize",
+                 ptr(input), rows, hidden, ptr(out), ptr(scales), s)
+        elif int4:
+            call("tb_bf16_int4_convrot_quantize", ptr(input), rows, hidden, int(bool(swiglu)),
+                 ptr(out), ptr(scales), s)
+        else:
+            call("tb_bf16_int8_convrot_quantize", ptr(input), rows, hidden, int(bool(swiglu)),
+                 int(forced_threads), ptr(out), ptr(scales), s)
+    return out, scales
+
+
+def turing_bf16_int8_convrot_quantize(input, group_size=256, swiglu=False, forced_threads=0):
+    """bindings.cpp:603-646."""
+    if forced_threads not in (0, 512, 768, 1024):
+        raise RuntimeError("forced_threads must be 0, 512, 768, or 1024")
+    return _rowbuffer(input, group_size, swiglu, False, False, forced_threads)
+
+
+def turing_bf16_int4_convrot_quantize(input, group_size=256, swiglu=False):
+    """bindings.cpp:648-688."""
+    return _rowbuffer(input, group_size, swiglu, True, False)
+
+
+def turing_bf16_gelu_int8_convrot_quantize(input, group_size=256):
+    return _rowbuffer(input, group_size, False, False, True)
+
+
+def turing_bf16_gelu_int4_convrot_quantize(input, group_size=256):
+    return _rowbuffer(input, group_size, False, True, True)
+
+
+def _staged(input, group_size, act, int4):
+    input = input.contiguous()
+    _check_cuda_2d(input, "input")
+    _check(input.dtype in (torch.float16, torch.bfloat16), "input must be float16 or bfloat16")
+    label = "SwiGLU" if act == 1 else "GELU"
+    _check(group_size == 256, f"{label} staged ConvRot only supports group_size=256")
+    rows, cols = input.shape
+    if act == 1:
+        _check(cols % 2 == 0, "SwiGLU input width must be even")
+    hidden = cols // 2 if act == 1 else cols
+    _check(rows > 0, f"{label} staged ConvRot requires at least one row")
+    _check(hidden > 0 and hidden % group_size == 0,
+           f"activated {label} width must be positive and divisible by 256")
+    with torch.cuda.device(input.device):
+        _require_blackwell(input.device, f"{label} staged ConvRot")
+        rotated = torch.empty((rows, hidden), dtype=input.dtype, device=input.device)
+        partial = torch.empty((rows, hidden // group_size), dtype=torch.float32,
+                              device=input.device)
+        out = torch.empty((rows, hidden // 2 if int4 else hidden), dtype=torch.int8,
+                          device=input.device)
+        scales = torch.empty((rows, 1), dtype=torch.float32, device=input.device)
+        name = {(1, False): "tb_swiglu_int8_convrot_quantize",
+                (1, True): "tb_swiglu_int4_convrot_quantize",
+                (2, False): "tb_gelu_int8_convrot_quantize",
+                (2, True): "tb_gelu_int4_convrot_quantize"}[(act, bool(int4))]
+        call(name, ptr(input), _lib.dtype_code(input), rows, hidden, ptr(rotated), ptr(partial),
+             ptr(out), ptr(scales), stream_of(input))
+    return out, scales
+
+
+def turing_swiglu_int8_convrot_quantize(input, group_size=256):
+    return _staged(input, group_size, 1, False)
+
+
+def turing_swiglu_int4_convrot_quantize(input, group_size=256):
+    return _staged(input, group_size, 1, True)
+
+
+def turing_gelu_int8_convrot_quantize(input, group_size=256):
+    return _staged(input, group_size, 2, False)
+
+
+def turing_gelu_int4_convrot_quantize(input, group_size=256):
+    return _staged(input, group_size, 2, True)

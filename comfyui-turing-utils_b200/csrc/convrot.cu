@@ -1,0 +1,486 @@
+// ConvRot activation quantizer for sm_100a: 256-wide block-Hadamard rotation
+// followed by per-token symmetric INT8 (or packed INT4) quantization, with
+// optional fused SwiGLU / tanh-GELU on the load.
+//
+// Semantics follow the reference kernels bit for bit
+// (kernel/csrc/turing/convrot_quant.cu:104-156 FHT and activations,
+//  :350-444 BF16 row-buffer kernel, :158-291 staged kernels):
+//   * the 256-point transform is applied as four radix-4 stages S = 1, 4, 16,
+//     64, each output computed as 0.5 * (((x0 +- x1) +- x2) +- x3) in that
+//     order, in fp32 with round-to-nearest and no contraction;
+//   * the row absmax is taken over the fp32 rotated values, the stored value
+//     is bf16 (fp16 for fp16 inputs of the staged form);
+//   * scale = max(min(amax, dtype_max) / 127, 1e-30) (row-buffer form) or
+//     max(min(amax, dtype_max) * (1/127), 1e-30) (staged form); INT4 uses 7
+//     and 1e-10;
+//   * INT8 code = clamp(rint(round_dtype(v / round_dtype(scale))), -128, 127)
+//     with an IEEE divide; INT4 code = clamp(rint(v * (1/scale)), -7, 7),
+//     two per byte, low nibble = even column.
+//
+// B200 layout: one half-warp owns a 256-group, 16 consecutive elements per
+// lane (two 16-byte loads).  Stages S=1 and S=4 run in registers; the group
+// is transposed through a bank-conflict-free shared buffer so that lane l
+// holds elements l + 16 j; stages S=16 and S=64 then also run in registers.
+// The rotated row is kept as bf16 in shared memory (never in HBM) until the
+// row scale is known; the quantized codes leave as 16-byte coalesced stores.
+#include "tb_capi_internal.h"
+#include "tb_tu.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kGroup = 256;
+constexpr int kTbufStride = 272;  // floats per half-warp transpose buffer (256 + 16 pad)
+
+enum Act { kActNone = 0, kActSwiGLU = 1, kActGelu = 2 };
+
+template <typename T>
+__device__ __forceinline__ float elem_to_f32(uint32_t bits16);
+template <>
+__device__ __forceinline__ float elem_to_f32<__nv_bfloat16>(uint32_t b) {
+  return bf16_bits_to_f32(b);
+}
+template <>
+__device__ __forceinline__ float elem_to_f32<__half>(uint32_t b) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t f32_to_elem_bits(float v);
+template <>
+__device__ __forceinline__ uint32_t f32_to_elem_bits<__nv_bfloat16>(float v) {
+  return f32_to_bf16_bits(v);
+}
+template <>
+__device__ __forceinline__ uint32_t f32_to_elem_bits<__half>(float v) {
+  return __half_as_ushort(__float2half_rn(v));
+}
+
+template <typename T>
+__device__ __forceinline__ float round_to_elem(float v) {
+  return elem_to_f32<T>(f32_to_elem_bits<T>(v));
+}
+
+template <typename T>
+__device__ __forceinline__ float dtype_finite_max();
+template <>
+__device__ __forceinline__ float dtype_finite_max<__nv_bfloat16>() {
+  return 3.38953139e38f;
+}
+template <>
+__device__ __forceinline__ float dtype_finite_max<__half>() {
+  return 65504.0f;
+}
+
+// Activations exactly as written in the reference so that nvcc forms the same
+// expression tree (convrot_quant.cu:137-156).
+__device__ __forceinline__ float swiglu_value(float gate, float up) {
+  return (gate / (1.0f + expf(-gate))) * up;
+}
+
+template <typename T>
+__device__ __forceinline__ float gelu_value(float x) {
+  constexpr float kAlpha = 0.7978845608028654f;
+  constexpr float kBeta = 0.044715f;
+  const float activated = 0.5f * x * (1.0f + tanhf(kAlpha * (x + kBeta * x * x * x)));
+  return round_to_elem<T>(activated);
+}
+
+// One radix-4 butterfly in the reference's operation order.
+__device__ __forceinline__ void butterfly4(float& x0, float& x1, float& x2, float& x3) {
+  const float s01 = __fadd_rn(x0, x1);
+  const float d01 = __fsub_rn(x0, x1);
+  const float y0 = __fmul_rn(0.5f, __fsub_rn(__fadd_rn(s01, x2), x3));
+  const float y1 = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(s01, x2), x3));
+  const float y2 = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(d01, x2), x3));
+  // (-x0 + x1) + x2 == x2 - (x0 - x1) exactly (negation is exact).
+  const float y3 = __fmul_rn(0.5f, __fadd_rn(__fsub_rn(x2, d01), x3));
+  x0 = y0;
+  x1 = y1;
+  x2 = y2;
+  x3 = y3;
+}
+
+// Stage on 4 consecutive registers (S=1 in layout A, S=16 in layout B).
+__device__ __forceinline__ void stage_contig(float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) butterfly4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// Stage on registers 4 apart (S=4 in layout A, S=64 in layout B).
+__device__ __forceinline__ void stage_strided(float (&v)[16]) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) butterfly4(v[p], v[p + 4], v[p + 8], v[p + 12]);
+}
+
+// Loads the 16 activated fp32 inputs of lane l (elements col..col+15).
+template <typename T, int ACT>
+__device__ __forceinline__ void load16(const T* __restrict__ row_in, int k, int col,
+                                       float (&v)[16]) {
+  const uint4* p = reinterpret_cast<const uint4*>(row_in + col);
+  uint4 a = __ldg(p);
+  uint4 b = __ldg(p + 1);
+  uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float x[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    x[2 * i] = elem_to_f32<T>(w[i] & 0xffffu);
+    x[2 * i + 1] = elem_to_f32<T>(w[i] >> 16);
+  }
+  if constexpr (ACT == kActSwiGLU) {
+    const uint4* q = reinterpret_cast<const uint4*>(row_in + k + col);
+    uint4 c = __ldg(q);
+    uint4 d = __ldg(q + 1);
+    uint32_t u[8] = {c.x, c.y, c.z, c.w, d.x, d.y, d.z, d.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[2 * i] = swiglu_value(x[2 * i], elem_to_f32<T>(u[i] & 0xffffu));
+      v[2 * i + 1] = swiglu_value(x[2 * i + 1], elem_to_f32<T>(u[i] >> 16));
+    }
+  } else if constexpr (ACT == kActGelu) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_value<T>(x[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = x[i];
+  }
+}
+
+// Full 256-point rotation of one group held by a half-warp.  On entry lane l
+// holds elements 16 l + j in v[j]; on exit it holds elements l + 16 j.
+__device__ __forceinline__ void rotate_group(float (&v)[16], float* __restrict__ tbuf, int l) {
+  stage_contig(v);   // S = 1
+  stage_strided(v);  // S = 4
+  const int swz = (l >> 1) & 3;
+  float4* row = reinterpret_cast<float4*>(tbuf + 16 * l);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    row[c ^ swz] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  }
+  __syncwarp();
+  const int c_read = l >> 2, w_read = l & 3;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int swz_j = (j >> 1) & 3;
+    v[j] = tbuf[16 * j + 4 * (c_read ^ swz_j) + w_read];
+  }
+  __syncwarp();
+  stage_contig(v);   // S = 16
+  stage_strided(v);  // S = 64
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+struct RowQuantParams {
+  const void* input;
+  int8_t* output;
+  float* scales;
+  void* rotated;          // staged form: [rows, k] T scratch
+  float* partial_absmax;  // staged form: [rows, k/256]
+  int rows;
+  int k;
+  int rows_per_cta;
+};
+
+template <typename T, bool INT4, bool STAGED_SCALE>
+__device__ __forceinline__ float row_scale_from_amax(float amax) {
+  constexpr float qmax = INT4 ? 7.0f : 127.0f;
+  constexpr float floor_v = INT4 ? 1.0e-10f : 1.0e-30f;
+  const float clipped = fminf(amax, dtype_finite_max<T>());
+  if constexpr (STAGED_SCALE) {
+    return fmaxf(__fmul_rn(clipped, 1.0f / qmax), floor_v);
+  } else {
+    return fmaxf(__fdiv_rn(clipped, qmax), floor_v);
+  }
+}
+
+// Quantizes 16 consecutive rotated elements (bits in `h`) and stores them.
+template <typename T, bool INT4>
+__device__ __forceinline__ void quantize16_store(const uint32_t (&h)[8], float scale,
+                                                 float rounded_scale, float inv_scale,
+                                                 int8_t* __restrict__ dst) {
+  if constexpr (INT4) {
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float lo = elem_to_f32<T>(h[i] & 0xffffu);
+      const float hi = elem_to_f32<T>(h[i] >> 16);
+      // clamp-then-round equals round-then-clamp for integer bounds, and
+      // fmaxf(NaN, -7) = -7 reproduces the reference's NaN path.
+      const int ql = __float2int_rn(fminf(7.0f, fmaxf(-7.0f, __fmul_rn(lo, inv_scale))));
+      const int qh = __float2int_rn(fminf(7.0f, fmaxf(-7.0f, __fmul_rn(hi, inv_scale))));
+      const uint32_t byte = (static_cast<uint32_t>(ql) & 0xfu) |
+                            ((static_cast<uint32_t>(qh) & 0xfu) << 4);
+      packed[i >> 2] |= byte << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+  } else {
+    uint32_t out[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t bits = (i & 1) ? (h[i >> 1] >> 16) : (h[i >> 1] & 0xffffu);
+      const float v = elem_to_f32<T>(bits);
+      const float d = round_to_elem<T>(__fdiv_rn(v, rounded_scale));
+      const int q = __float2int_rn(fminf(127.0f, fmaxf(-128.0f, d)));
+      out[i >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << (8 * (i & 3));
+    }
+    (void)scale;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
+// Single-pass kernel: rows_per_cta rows per CTA, rotated bf16 row buffer in
+// shared memory.  Shared layout: [rows_per_cta * k] row buffer (T bits),
+// [halfwarps * kTbufStride] f32 transpose buffers, [rows_per_cta] u32 amax.
+template <typename T, int ACT, bool INT4, bool STAGED_SCALE>
+__global__ void __launch_bounds__(512) convrot_rowbuffer_kernel(RowQuantParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int R = p.rows_per_cta;
+  const int k = p.k;
+  const int groups = k / kGroup;
+  const int halfwarps = blockDim.x >> 4;
+  uint16_t* rowbuf = reinterpret_cast<uint16_t*>(smem);
+  float* tbuf_all = reinterpret_cast<float*>(smem + static_cast<size_t>(R) * k * 2);
+  unsigned int* row_amax =
+      reinterpret_cast<unsigned int*>(tbuf_all + static_cast<size_t>(halfwarps) * kTbufStride);
+
+  const int tid = threadIdx.x;
+  const int hw = tid >> 4;
+  const int l = tid & 15;
+  const int row0 = blockIdx.x * R;
+  const int rows_here = min(R, p.rows - row0);
+  const int in_width = ACT == kActSwiGLU ? 2 * k : k;
+  const T* in = static_cast<const T*>(p.input);
+  float* tbuf = tbuf_all + hw * kTbufStride;
+
+  for (int r = tid; r < R; r += blockDim.x) row_amax[r] = 0u;
+  __syncthreads();
+
+  // Items (row, group) are taken two per warp so both half-warps of a warp
+  // run the same number of iterations (the transpose and the shuffles below
+  // are warp-collective); an odd last item leaves one half-warp idle.
+  const int items = rows_here * groups;
+  for (int base = 2 * (hw >> 1); base < items; base += halfwarps) {
+    const int item = base + (hw & 1);
+    const bool active = item < items;
+    const int r = active ? item / groups : 0;
+    const int g = active ? item - r * groups : 0;
+    const T* row_in = in + static_cast<int64_t>(row0 + r) * in_width;
+    float v[16];
+    load16<T, ACT>(row_in, k, g * kGroup + 16 * l, v);
+    rotate_group(v, tbuf, l);
+    float amax = 0.0f;
+    uint16_t* dst = rowbuf + static_cast<size_t>(r) * k + g * kGroup + l;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      amax = fmaxf(amax, fabsf(v[j]));
+      if (active) dst[16 * j] = static_cast<uint16_t>(f32_to_elem_bits<T>(v[j]));
+    }
+    // Non-negative floats order like their bit patterns.
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
+    if (active && l == 0) atomicMax(&row_amax[r], __float_as_uint(amax));
+  }
+  __syncthreads();
+
+  // Phase 2: quantize the buffered rows with coalesced 16-element chunks.
+  const int chunks_per_row = k / 16;
+  const int chunks = rows_here * chunks_per_row;
+  for (int c = tid; c < chunks; c += blockDim.x) {
+    const int r = c / chunks_per_row;
+    const int col = (c - r * chunks_per_row) * 16;
+    const float amax = __uint_as_float(row_amax[r]);
+    const float scale = row_scale_from_amax<T, INT4, STAGED_SCALE>(amax);
+    const float rounded_scale = round_to_elem<T>(scale);
+    const float inv_scale = __frcp_rn(scale);
+    const uint4* src = reinterpret_cast<const uint4*>(rowbuf + static_cast<size_t>(r) * k + col);
+    uint4 a = src[0], b = src[1];
+    uint32_t h[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const int64_t row = row0 + r;
+    int8_t* dst = INT4 ? p.output + row * (k / 2) + col / 2 : p.output + row * k + col;
+    quantize16_store<T, INT4>(h, scale, rounded_scale, inv_scale, dst);
+    if (col == 0) p.scales[row] = scale;
+  }
+}
+
+// Staged form, pass 1: rotate, write the rotated T values to the global
+// scratch and one fp32 absmax per (row, group) (convrot_quant.cu:158-211).
+template <typename T, int ACT>
+__global__ void __launch_bounds__(256) convrot_staged_rotate_kernel(RowQuantParams p) {
+  __shared__ __align__(16) float tbuf_all[16 * kTbufStride];
+  const int k = p.k;
+  const int groups = k / kGroup;
+  const int64_t total = static_cast<int64_t>(p.rows) * groups;
+  const int hw = threadIdx.x >> 4;
+  const int l = threadIdx.x & 15;
+  float* tbuf = tbuf_all + hw * kTbufStride;
+  const int in_width = ACT == kActSwiGLU ? 2 * k : k;
+  const T* in = static_cast<const T*>(p.input);
+  uint16_t* rot = static_cast<uint16_t*>(p.rotated);
+  // Two items per warp per iteration (see convrot_rowbuffer_kernel).
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * 16 + 2 * (hw >> 1); base < total;
+       base += static_cast<int64_t>(gridDim.x) * 16) {
+    const int64_t item = base + (hw & 1);
+    const bool active = item < total;
+    const int64_t row = active ? item / groups : 0;
+    const int g = active ? static_cast<int>(item - row * groups) : 0;
+    float v[16];
+    load16<T, ACT>(in + row * in_width, k, g * kGroup + 16 * l, v);
+    rotate_group(v, tbuf, l);
+    float amax = 0.0f;
+    uint16_t* dst = rot + row * k + g * kGroup + l;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      amax = fmaxf(amax, fabsf(v[j]));
+      if (active) dst[16 * j] = static_cast<uint16_t>(f32_to_elem_bits<T>(v[j]));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o, 16));
+    if (active && l == 0) p.partial_absmax[row * groups + g] = amax;
+  }
+}
+
+// Staged form, pass 2: per row, reduce the partial absmax and quantize from
+// the rotated scratch (convrot_quant.cu:213-291).  One CTA per row.
+template <typename T, bool INT4>
+__global__ void __launch_bounds__(256) convrot_staged_quant_kernel(RowQuantParams p) {
+  __shared__ float warp_max_s[8];
+  const int k = p.k;
+  const int groups = k / kGroup;
+  const int64_t row = blockIdx.x;
+  float amax = 0.0f;
+  for (int g = threadIdx.x; g < groups; g += blockDim.x)
+    amax = fmaxf(amax, p.partial_absmax[row * groups + g]);
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) warp_max_s[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.0f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) amax = fmaxf(amax, warp_max_s[w]);
+  const float scale = row_scale_from_amax<T, INT4, true>(amax);
+  const float rounded_scale = round_to_elem<T>(scale);
+  const float inv_scale = __frcp_rn(scale);
+  if (threadIdx.x == 0) p.scales[row] = scale;
+  const uint16_t* rot = static_cast<const uint16_t*>(p.rotated) + row * k;
+  for (int col = threadIdx.x * 16; col < k; col += blockDim.x * 16) {
+    const uint4* src = reinterpret_cast<const uint4*>(rot + col);
+    uint4 a = __ldg(src), b = __ldg(src + 1);
+    uint32_t h[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    int8_t* dst = INT4 ? p.output + row * (k / 2) + col / 2 : p.output + row * k + col;
+    quantize16_store<T, INT4>(h, scale, rounded_scale, inv_scale, dst);
+  }
+}
+
+struct RowbufferLaunch {
+  int rows_per_cta;
+  int threads;
+  size_t smem;
+};
+
+RowbufferLaunch plan_rowbuffer(int k) {
+  const int groups = k / kGroup;
+  int R = groups >= 32 ? 1 : 32 / groups;
+  while (R > 1 && static_cast<size_t>(R) * k * 2 > 64 * 1024) R >>= 1;
+  const int items = R * groups;
+  int halfwarps = items < 32 ? items : 32;
+  int threads = halfwarps * 16;
+  threads = (threads + 31) / 32 * 32;
+  halfwarps = threads / 16;
+  RowbufferLaunch L;
+  L.rows_per_cta = R;
+  L.threads = threads;
+  L.smem = static_cast<size_t>(R) * k * 2 + static_cast<size_t>(halfwarps) * kTbufStride * 4 +
+           static_cast<size_t>(R) * 4;
+  return L;
+}
+
+template <typename T, int ACT, bool INT4, bool STAGED_SCALE>
+void launch_rowbuffer_t(const void* input, int rows, int k, int8_t* out, float* scales,
+                        cudaStream_t stream) {
+  RowbufferLaunch L = plan_rowbuffer(k);
+  RowQuantParams p{};
+  p.input = input;
+  p.output = out;
+  p.scales = scales;
+  p.rows = rows;
+  p.k = k;
+  p.rows_per_cta = L.rows_per_cta;
+  auto kernel = convrot_rowbuffer_kernel<T, ACT, INT4, STAGED_SCALE>;
+  if (L.smem > 48 * 1024) {
+    TB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(L.smem)));
+  }
+  const int grid = (rows + L.rows_per_cta - 1) / L.rows_per_cta;
+  kernel<<<grid, L.threads, L.smem, stream>>>(p);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+template <typename T, int ACT, bool INT4>
+void launch_staged_t(const void* input, int rows, int k, void* rotated, float* partial,
+                     int8_t* out, float* scales, cudaStream_t stream) {
+  RowQuantParams p{};
+  p.input = input;
+  p.output = out;
+  p.scales = scales;
+  p.rotated = rotated;
+  p.partial_absmax = partial;
+  p.rows = rows;
+  p.k = k;
+  const int64_t items = static_cast<int64_t>(rows) * (k / kGroup);
+  int64_t blocks = (items + 15) / 16;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+  if (blocks > cap) blocks = cap;
+  convrot_staged_rotate_kernel<T, ACT><<<static_cast<int>(blocks), 256, 0, stream>>>(p);
+  TB_CUDA_CHECK(cudaGetLastError());
+  convrot_staged_quant_kernel<T, INT4><<<rows, 256, 0, stream>>>(p);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace
+
+// Shared dispatcher for both forms.  dtype: TB_DTYPE_BF16 or TB_DTYPE_F16
+// (fp16 only for the staged form, as in the reference).
+void convrot_quantize_impl(const void* input, int dtype, int64_t rows64, int64_t k64, int act,
+                           int int4, int staged, void* rotated, float* partial, int8_t* out,
+                           float* scales, cudaStream_t stream) {
+  TB_REQUIRE(rows64 > 0 && k64 > 0 && k64 % kGroup == 0,
+             "ConvRot width must be positive and divisible by 256");
+  TB_REQUIRE(rows64 <= INT32_MAX && k64 <= INT32_MAX,
+             "ConvRot dimensions exceed the CUDA kernel range");
+  TB_REQUIRE(act >= 0 && act <= 2, "ConvRot activation must be 0 (none), 1 (SwiGLU) or 2 (GELU)");
+  TB_REQUIRE(dtype == TB_DTYPE_BF16 || (staged && dtype == TB_DTYPE_F16),
+             "ConvRot input must be bfloat16 (float16 only for the staged form)");
+  TB_REQUIRE(input != nullptr && out != nullptr && scales != nullptr,
+             "ConvRot input, output and scales must be non-null");
+  const int rows = static_cast<int>(rows64), k = static_cast<int>(k64);
+  TB_REQUIRE(!staged || (rotated != nullptr && partial != nullptr),
+             "staged ConvRot requires rotated and partial_absmax scratch");
+  TB_REQUIRE(static_cast<size_t>(k) * 2 + 32 * kTbufStride * 4 + 64 <= 227 * 1024 || staged,
+             "ConvRot row does not fit in shared memory; use the staged form");
+
+#define TB_CONVROT_CASE(T, ACT)                                                             \
+  if (staged) {                                                                             \
+    if (int4) launch_staged_t<T, ACT, true>(input, rows, k, rotated, partial, out, scales,  \
+                                            stream);                                        \
+    else launch_staged_t<T, ACT, false>(input, rows, k, rotated, partial, out, scales,      \
+                                        stream);                                            \
+  } else {                                                                                  \
+    if (int4) launch_rowbuffer_t<T, ACT, true, false>(input, rows, k, out, scales, stream); \
+    else launch_rowbuffer_t<T, ACT, false, false>(input, rows, k, out, scales, stream);     \
+  }
+  if (dtype == TB_DTYPE_BF16) {
+    if (act == kActNone) { TB_CONVROT_CASE(__nv_bfloat16, kActNone) }
+    else if (act == kActSwiGLU) { TB_CONVROT_CASE(__nv_bfloat16, kActSwiGLU) }
+    else { TB_CONVROT_CASE(__nv_bfloat16, kActGelu) }
+  } else {
+    if (act == kActNone) { TB_CONVROT_CASE(__half, kActNone) }
+    else if (act == kActSwiGLU) { TB_CONVROT_CASE(__half, kActSwiGLU) }
+    else { TB_CONVROT_CASE(__half, kActGelu) }
+  }
+#undef TB_CONVROT_CASE
+}
+
+}  // namespace tb

@@ -1,0 +1,158 @@
+// Memory-bound kernels of the linear path:
+//   * INT32 -> BF16 dequant epilogue (kernel/csrc/turing/bf16_epilogue.cu:46-143):
+//       out = bf16_rn((acc * a_s[row]) * w_s[col]), w_s scalar or per column;
+//   * grouped-codebook W4 -> INT8 decode (kernel/csrc/turing/w4a8.cu:907-973):
+//       w8 = clamp(rint(codebook[idx] * e4m3(group_scale)), -127, 127).
+// Both move 16-byte vectors per thread with grid-stride loops sized to the SM
+// count.
+#include <cuda_fp8.h>
+
+#include "tb_capi_internal.h"
+#include "tb_tu.cuh"
+
+namespace tb {
+namespace {
+
+template <bool SCALAR_W>
+__global__ void __launch_bounds__(256) dequant_vec8_kernel(const int32_t* __restrict__ acc,
+                                                           int64_t acc_stride,
+                                                           const float* __restrict__ a_s,
+                                                           const float* __restrict__ w_s,
+                                                           __nv_bfloat16* __restrict__ out,
+                                                           int rows, int cols) {
+  const int vpr = cols / 8;
+  const int64_t total = static_cast<int64_t>(rows) * vpr;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(v / vpr);
+    const int col = static_cast<int>(v - static_cast<int64_t>(row) * vpr) * 8;
+    const int32_t* src = acc + static_cast<int64_t>(row) * acc_stride + col;
+    const int4 x0 = __ldg(reinterpret_cast<const int4*>(src));
+    const int4 x1 = __ldg(reinterpret_cast<const int4*>(src + 4));
+    const float xs = __ldg(a_s + row);
+    float w[8];
+    if (SCALAR_W) {
+      const float s = __ldg(w_s);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[j] = s;
+    } else {
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(w_s + col));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(w_s + col + 4));
+      w[0] = s0.x; w[1] = s0.y; w[2] = s0.z; w[3] = s0.w;
+      w[4] = s1.x; w[5] = s1.y; w[6] = s1.z; w[7] = s1.w;
+    }
+    const int a[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fmul_rn(__fmul_rn(static_cast<float>(a[j]), xs), w[j]);
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * cols + col) =
+        make_uint4(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]), pack_bf16x2(r[4], r[5]),
+                   pack_bf16x2(r[6], r[7]));
+  }
+}
+
+template <bool SCALAR_W>
+__global__ void __launch_bounds__(256) dequant_scalar_kernel(const int32_t* __restrict__ acc,
+                                                             int64_t acc_stride,
+                                                             const float* __restrict__ a_s,
+                                                             const float* __restrict__ w_s,
+                                                             uint16_t* __restrict__ out, int rows,
+                                                             int cols) {
+  const int64_t total = static_cast<int64_t>(rows) * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / cols);
+    const int col = static_cast<int>(i - static_cast<int64_t>(row) * cols);
+    const float v = __fmul_rn(__fmul_rn(static_cast<float>(acc[static_cast<int64_t>(row) * acc_stride + col]),
+                                        a_s[row]),
+                              w_s[SCALAR_W ? 0 : col]);
+    out[i] = f32_to_bf16_bits(v);
+  }
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+__device__ __forceinline__ uint32_t decode_byte(float cb, float s) {
+  const int q = __float2int_rn(cb * s);
+  return static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(max(-127, min(127, q)))));
+}
+
+// One thread decodes 16 columns (8 packed bytes) of one weight row.
+__global__ void __launch_bounds__(256) codebook_decode_kernel(
+    const int8_t* __restrict__ packed, const uint8_t* __restrict__ group_scale,
+    const float* __restrict__ codebook, int8_t* __restrict__ out, int rows, int k,
+    int group_size) {
+  __shared__ float cb[16];
+  if (threadIdx.x < 16) cb[threadIdx.x] = codebook[threadIdx.x];
+  __syncthreads();
+  const int vpr = k / 16;
+  const int gpr = k / group_size;
+  const int64_t total = static_cast<int64_t>(rows) * vpr;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(v / vpr);
+    const int col = static_cast<int>(v - static_cast<int64_t>(row) * vpr) * 16;
+    const uint2 pk = __ldg(reinterpret_cast<const uint2*>(packed + static_cast<int64_t>(row) * (k / 2) + col / 2));
+    const uint8_t* gs = group_scale + static_cast<int64_t>(row) * gpr;
+    uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const uint32_t byte = ((e < 8 ? pk.x : pk.y) >> (8 * ((e >> 1) & 3))) & 0xffu;
+      const uint32_t code = (e & 1) ? (byte >> 4) : (byte & 0xfu);
+      const float s = e4m3_to_f32(__ldg(gs + (col + e) / group_size));
+      words[e >> 2] |= decode_byte(cb[code], s) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * k + col) =
+        make_uint4(words[0], words[1], words[2], words[3]);
+  }
+}
+
+int grid_for(int64_t work_items, int threads) {
+  int64_t blocks = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+}  // namespace
+
+void dequant_launch(const int32_t* acc, int64_t acc_stride, const float* a_s, const float* w_s,
+                    bool scalar_w, void* out, int rows, int cols, cudaStream_t stream) {
+  const bool vec = cols % 8 == 0 && acc_stride % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(acc) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+                   (scalar_w || (reinterpret_cast<uintptr_t>(w_s) & 15u) == 0);
+  if (vec) {
+    const int grid = grid_for(static_cast<int64_t>(rows) * (cols / 8), 256);
+    if (scalar_w)
+      dequant_vec8_kernel<true><<<grid, 256, 0, stream>>>(acc, acc_stride, a_s, w_s,
+                                                          static_cast<__nv_bfloat16*>(out), rows, cols);
+    else
+      dequant_vec8_kernel<false><<<grid, 256, 0, stream>>>(acc, acc_stride, a_s, w_s,
+                                                           static_cast<__nv_bfloat16*>(out), rows, cols);
+  } else {
+    const int grid = grid_for(static_cast<int64_t>(rows) * cols, 256);
+    if (scalar_w)
+      dequant_scalar_kernel<true><<<grid, 256, 0, stream>>>(acc, acc_stride, a_s, w_s,
+                                                            static_cast<uint16_t*>(out), rows, cols);
+    else
+      dequant_scalar_kernel<false><<<grid, 256, 0, stream>>>(acc, acc_stride, a_s, w_s,
+                                                             static_cast<uint16_t*>(out), rows, cols);
+  }
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
+                            const float* codebook, int8_t* out, int rows, int k, int group_size,
+                            cudaStream_t stream) {
+  const int grid = grid_for(static_cast<int64_t>(rows) * (k / 16), 256);
+  codebook_decode_kernel<<<grid, 256, 0, stream>>>(packed, group_scale, codebook, out, rows, k,
+                                                   group_size);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace tb

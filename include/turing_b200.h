@@ -1,0 +1,180 @@
+/*
+ * turing_b200.h — C ABI of libturing_b200.so, the sm_100a (B200) implementation
+ * of the comfyui-turing-utils quantized DiT path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream) and returns a
+ * status code.  On failure the message is available from tb_last_error()
+ * (thread-local) and nothing was launched.  Buffers are owned by the caller:
+ * outputs and workspaces are allocated by the binding and written in place, as
+ * in the reference (kernel/csrc/bindings.cpp:206-210, 350-353, 409-410).
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the reference project root).  The reference's native interface is the C++
+ * ABI in kernel/csrc/kernel_api.h (functions taking `Tensor` PODs,
+ * kernel/csrc/tensor_bridge.h:83-236) and the Sage entry points in
+ * kernel/csrc/turing/sage/fused.h and attn_cuda_sm75.h; here each `Tensor`
+ * becomes a pointer plus the sizes the kernel needs.
+ */
+#ifndef TURING_B200_H
+#define TURING_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define TB_OK 0
+#define TB_ERR_INVALID 1     /* argument / shape error (reference: TORCH_CHECK) */
+#define TB_ERR_CUDA 2        /* CUDA runtime error at launch */
+#define TB_ERR_UNSUPPORTED 3 /* device is not sm_100 */
+#define TB_ERR_INTERNAL 4
+
+/* 16-bit floating-point input types. */
+#define TB_DTYPE_BF16 0
+#define TB_DTYPE_F16 1
+
+/* Tensor layouts of the Sage entry points (reference: tensor_layout 0/1,
+ * kernel/csrc/turing/sage/qk_int_sv_f16_cuda_sm75.cu:1059-1101). */
+#define TB_LAYOUT_NHD 0
+#define TB_LAYOUT_HND 1
+
+typedef void *tb_stream_t;
+
+/* Exported symbols (the library is built with hidden default visibility). */
+#if defined(__GNUC__)
+#define TB_API __attribute__((visibility("default")))
+#else
+#define TB_API
+#endif
+
+/* ABI version of this header (bumped on any signature change). */
+TB_API int tb_abi_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+TB_API const char *tb_last_error(void);
+
+/* Reads and clears the device-side watchdog word of the current device: 0 if
+ * no kernel of this library hit a wait limit since the last call.  No
+ * counterpart in the reference (its kernels have no bounded waits). */
+TB_API int tb_device_error(int *code_out);
+
+/* ------------------------------------------------ ConvRot quantizers ---- */
+
+/* BF16 row-buffer ConvRot INT8 quantizer: input bf16 [rows, swiglu ? 2*hidden :
+ * hidden], output int8 [rows, hidden], scales fp32 [rows].  forced_threads is
+ * validated (0/512/768/1024) for signature parity; the kernel sizes its own
+ * CTA.  Replaces kernel_api.h:66-70 turing_bf16_int8_convrot_quantize
+ * (binding checks kernel/csrc/bindings.cpp:603-646). */
+TB_API int tb_bf16_int8_convrot_quantize(const void *input, int64_t rows, int64_t hidden, int swiglu,
+                                  int forced_threads, int8_t *output, float *scales,
+                                  tb_stream_t stream);
+
+/* As above with packed INT4 output int8 [rows, hidden/2] (low nibble = even
+ * column).  Replaces kernel_api.h:72-76 (bindings.cpp:649-688). */
+TB_API int tb_bf16_int4_convrot_quantize(const void *input, int64_t rows, int64_t hidden, int swiglu,
+                                  int8_t *output, float *scales, tb_stream_t stream);
+
+/* tanh-GELU fused row-buffer quantizers, input bf16 [rows, hidden].
+ * Replace kernel_api.h:78-81 and 83-86 (bindings.cpp:690-741). */
+TB_API int tb_bf16_gelu_int8_convrot_quantize(const void *input, int64_t rows, int64_t hidden,
+                                       int8_t *output, float *scales, tb_stream_t stream);
+TB_API int tb_bf16_gelu_int4_convrot_quantize(const void *input, int64_t rows, int64_t hidden,
+                                       int8_t *output, float *scales, tb_stream_t stream);
+
+/* Staged (two-pass) ConvRot quantizers with caller-owned scratch:
+ * rotated [rows, hidden] of the input dtype and partial_absmax fp32
+ * [rows, hidden/256].  dtype TB_DTYPE_BF16 or TB_DTYPE_F16.
+ * Replace kernel_api.h:44-48, 50-54, 56-60, 62-64 (bindings.cpp:469-601). */
+TB_API int tb_swiglu_int8_convrot_quantize(const void *input, int dtype, int64_t rows, int64_t hidden,
+                                    void *rotated, float *partial_absmax, int8_t *output,
+                                    float *scales, tb_stream_t stream);
+TB_API int tb_swiglu_int4_convrot_quantize(const void *input, int dtype, int64_t rows, int64_t hidden,
+                                    void *rotated, float *partial_absmax, int8_t *output,
+                                    float *scales, tb_stream_t stream);
+TB_API int tb_gelu_int8_convrot_quantize(const void *input, int dtype, int64_t rows, int64_t hidden,
+                                  void *rotated, float *partial_absmax, int8_t *output,
+                                  float *scales, tb_stream_t stream);
+TB_API int tb_gelu_int4_convrot_quantize(const void *input, int dtype, int64_t rows, int64_t hidden,
+                                  void *rotated, float *partial_absmax, int8_t *output,
+                                  float *scales, tb_stream_t stream);
+
+/* --------------------------------------------------- GEMM + epilogue ---- */
+
+/* W8A8 linear: out[m, n] = bf16(((float)sum_k act[m,k] w[n,k] * a_s[m]) * w_s[n]
+ * + bias[n]).  act int8 [m, k], weight int8 [n, k] (K-contiguous rows),
+ * activation_scale fp32 [m], weight_scale fp32 [n], bias fp32 [n] or NULL,
+ * output bf16 [m, ldo].  Requires k % 16 == 0 and n % 8 == 0.
+ * Replaces kernel_api.h:29-35 turing_int8_linear (bindings.cpp:371-421,
+ * w4a8.cu:1185-1219). */
+TB_API int tb_int8_linear(const int8_t *activation, const int8_t *weight, const float *activation_scale,
+                   const float *weight_scale, const float *bias, void *output, int64_t m,
+                   int64_t n, int64_t k, int64_t ldo, int tile_policy, tb_stream_t stream);
+
+/* Grouped-codebook W4A8 linear: weight = packed 4-bit codebook indices
+ * [n, k/2], group_scale = raw E4M3 bytes [n, k/group_size], channel_scale
+ * fp32 [n], codebook fp32 [16].  Weight row w8 = clamp(rint(codebook[idx] *
+ * e4m3(group_scale)), -127, 127).  workspace int8 [workspace_rows, k] (the
+ * staged decode chunk) may be NULL when inline_decode != 0.
+ * Replaces kernel_api.h:15-27 turing_codebook_w4a8_linear
+ * (w4a8.cu:1088-1183, bindings.cpp:262-369). */
+TB_API int tb_codebook_w4a8_linear(const int8_t *activation, const int8_t *weight_packed,
+                            const float *activation_scale, const uint8_t *group_scale,
+                            const float *channel_scale, const float *codebook, const float *bias,
+                            int8_t *workspace, int64_t workspace_rows, void *output, int64_t m,
+                            int64_t n, int64_t k, int64_t group_size, int inline_decode,
+                            int tile_policy, tb_stream_t stream);
+
+/* INT32 accumulator GEMM: acc[m, n] = sum_k act[m,k] * w[n,k] (exact int32),
+ * acc row stride acc_stride (elements).  Replaces the INT32 cuBLAS GEMM that
+ * the plugin feeds into turing_dequantize_int8_bf16
+ * (comfyui_turing_utils/quantization/dispatch.py:481-535); also the
+ * accumulator dump used by the bit-exact tests. */
+TB_API int tb_int8_gemm_s32(const int8_t *activation, const int8_t *weight, int32_t *accumulator,
+                     int64_t m, int64_t n, int64_t k, int64_t acc_stride, tb_stream_t stream);
+
+/* INT32 -> BF16 dequant epilogue: out[r, c] = bf16((acc[r, c] * a_s[r]) * w_s[c])
+ * (w_s scalar when weight_scale_numel == 1).  Replaces kernel_api.h:37-40
+ * turing_dequantize_int8_bf16 (bf16_epilogue.cu:147-218). */
+TB_API int tb_dequantize_int8_bf16(const int32_t *accumulator, int64_t acc_stride,
+                            const float *activation_scale, const float *weight_scale,
+                            int64_t weight_scale_numel, void *output, int64_t rows, int64_t cols,
+                            tb_stream_t stream);
+
+/* ----------------------------------------------------- Sage quantizers -- */
+
+/* Per-tile INT8 quantization of Q or K.  input [B, H, L, D] (layout HND) or
+ * [B, L, H, D] (NHD), last dim contiguous, element strides stride_b / stride_h
+ * / stride_l; output int8 contiguous with the input's shape; scale fp32
+ * [B, H, ceil(L / tile)] contiguous.  mean: optional bf16/f16 [B, H, D]
+ * smoothing mean subtracted before quantization (NULL = none).
+ *   tb_quant_per_block_int8: tile = block_size tokens (K, 64) — replaces
+ *     fused.h:27-32 quant_per_block_int8_cuda (fused.cu:983-1067).
+ *   tb_quant_per_warp_int8: tile = warp_block_size tokens inside block_size
+ *     blocks (Q, 64/16), scale [B, H, ceil(L/block)*(block/warp)] — replaces
+ *     fused.h:35-41 quant_per_warp_int8_cuda (fused.cu:1070-1150). */
+TB_API int tb_quant_per_block_int8(const void *input, int dtype, int8_t *output, float *scale, int64_t B,
+                            int64_t H, int64_t L, int64_t D, int64_t stride_b, int64_t stride_h,
+                            int64_t stride_l, int block_size, int layout, const void *mean,
+                            tb_stream_t stream);
+TB_API int tb_quant_per_warp_int8(const void *input, int dtype, int8_t *output, float *scale, int64_t B,
+                           int64_t H, int64_t L, int64_t D, int64_t stride_b, int64_t stride_h,
+                           int64_t stride_l, int block_size, int warp_block_size, int layout,
+                           tb_stream_t stream);
+
+/* Token mean for K smoothing: mean [B, H, D] of the input dtype, accumulated in
+ * fp64 and rounded to fp32 then to the input dtype.  Produces the `mean` that
+ * the reference's QuantInt8Kernel<..., sub_mean=true> consumes
+ * (fused.cu:97-128); the reference has no kernel that computes it. */
+TB_API int tb_token_mean(const void *input, int dtype, void *mean, int64_t B, int64_t H, int64_t L,
+                  int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_l, int layout,
+                  tb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURING_B200_H */

@@ -1,0 +1,432 @@
+/*
+ * CPU ORACLE — TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement of the arithmetic of the comfyui-turing-utils quantized
+ * DiT path (ConvRot activation quantizer, INT8 GEMM accumulate + dequant
+ * epilogue, W4 / codebook-W4 weight decode, Sage Q/K INT8 quantizer).  Only the
+ * test suite, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm load this file; the product path never does.
+ *
+ * Every function names the reference file:line it restates (paths are relative
+ * to the reference project root).  Compile with -ffp-contract=off and without
+ * -ffast-math: the reference's `_C` extension is built without fast-math
+ * (kernel/setup.py:398-412), so its divides and adds are IEEE round-to-nearest
+ * and the order of every floating-point operation below matters.
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <stdint.h>
+#include <string.h>
+
+/* ---------------------------------------------------------------- bf16 --- */
+
+/* kernel/csrc/turing/convrot_quant.cu:293-305 (float_to_bf16_rn_bits) */
+static inline uint16_t f32_to_bf16_rn(float v) {
+    uint32_t bits;
+    memcpy(&bits, &v, 4);
+    if ((bits & 0x7fffffffu) > 0x7f800000u) return 0x7fffu;
+    uint16_t upper = (uint16_t)(bits >> 16);
+    uint32_t rem = bits << 16;
+    if (rem > 0x80000000u || (rem == 0x80000000u && (upper & 1u))) ++upper;
+    return upper;
+}
+
+static inline float bf16_to_f32(uint16_t h) {
+    uint32_t bits = ((uint32_t)h) << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* IEEE binary16 <-> binary32 (round to nearest even), used for FP16 inputs of
+ * the staged quantizer (convrot_quant.cu:33-54) and for E4M3 decode. */
+static inline float f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    int exp = (h >> 10) & 0x1f;
+    uint32_t mant = h & 0x3ffu;
+    uint32_t bits;
+    if (exp == 0) {
+        if (mant == 0) {
+            bits = sign;
+        } else {
+            int e = -1;
+            do { mant <<= 1; ++e; } while (!(mant & 0x400u));
+            mant &= 0x3ffu;
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | (mant << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (mant << 13);
+    } else {
+        bits = sign | ((uint32_t)(exp - 15 + 127) << 23) | (mant << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static inline uint16_t f32_to_f16_rn(float v) {
+    uint32_t bits;
+    memcpy(&bits, &v, 4);
+    uint32_t sign = (bits >> 16) & 0x8000u;
+    uint32_t absb = bits & 0x7fffffffu;
+    if (absb > 0x7f800000u) return (uint16_t)(sign | 0x7e00u);
+    if (absb >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* rounds to inf */
+    if (absb < 0x38800000u) {                                   /* subnormal f16 */
+        if (absb < 0x33000000u) return (uint16_t)sign;           /* < 2^-25 -> 0 */
+        int e = (int)(absb >> 23);
+        uint32_t m = (absb & 0x7fffffu) | 0x800000u;
+        int shift = 126 - e; /* q = m * 2^(e-126): value in units of 2^-24 */
+        uint32_t q = m >> shift;
+        uint32_t r = m & ((1u << shift) - 1u);
+        uint32_t half = 1u << (shift - 1);
+        if (r > half || (r == half && (q & 1u))) ++q;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t e = (absb >> 23) - 112;
+    uint32_t m = absb & 0x7fffffu;
+    uint32_t q = (e << 10) | (m >> 13);
+    uint32_t r = m & 0x1fffu;
+    if (r > 0x1000u || (r == 0x1000u && (q & 1u))) ++q;
+    return (uint16_t)(sign | q);
+}
+
+/* E4M3 (OCP fp8, no infinities, 0x7f/0xff NaN) -> float.  Every finite E4M3
+ * value is exact in half and float, so this equals the reference's
+ * __nv_cvt_fp8_to_halfraw(value, __NV_E4M3) -> __half2float
+ * (kernel/csrc/turing/w4a8.cu:77-80). */
+float orc_e4m3_to_f32(uint8_t v) {
+    int sign = v >> 7;
+    int exp = (v >> 3) & 0xf;
+    int mant = v & 7;
+    float out;
+    if (exp == 15 && mant == 7) {
+        out = NAN;
+    } else if (exp == 0) {
+        out = ldexpf((float)mant, -9);
+    } else {
+        out = ldexpf((float)(8 + mant), exp - 10);
+    }
+    return sign ? -out : out;
+}
+
+/* ------------------------------------------------------------- ConvRot --- */
+
+#define GROUP 256
+
+/* One radix-4 stage of the 256-point block Hadamard, in the reference's exact
+ * per-output operation order: kernel/csrc/turing/convrot_quant.cu:104-116
+ * (fht_stage) and :385-391 (the S=1 stage fused with the load). */
+static void fht_stage(const float *src, float *dst, int S) {
+    for (int lane = 0; lane < 64; ++lane) {
+        int base = (lane % S) + (lane / S) * (4 * S);
+        float x0 = src[base], x1 = src[base + S], x2 = src[base + 2 * S], x3 = src[base + 3 * S];
+        dst[base] = 0.5f * (x0 + x1 + x2 - x3);
+        dst[base + S] = 0.5f * (x0 + x1 - x2 + x3);
+        dst[base + 2 * S] = 0.5f * (x0 - x1 + x2 + x3);
+        dst[base + 3 * S] = 0.5f * (-x0 + x1 + x2 + x3);
+    }
+}
+
+/* Rotate one 256-group of fp32 inputs: stages S = 1, 4, 16, 64 in that order
+ * (convrot_quant.cu:384-403).  Returns the fp32 rotated values in y. */
+static void fht256(const float *x, float *y) {
+    float a[GROUP], b[GROUP];
+    fht_stage(x, a, 1);
+    fht_stage(a, b, 4);
+    fht_stage(b, a, 16);
+    fht_stage(a, y, 64);
+}
+
+/* SwiGLU load: convrot_quant.cu:137-143.  expf is the C library's, so this
+ * can differ from CUDA's expf in the last place; tests of the fused variants
+ * therefore allow rare +-1 code differences (documented in the tests). */
+static inline float swiglu_f(float gate, float up) {
+    return (gate / (1.0f + expf(-gate))) * up;
+}
+
+/* tanh-GELU load rounded to the input dtype: convrot_quant.cu:145-156.  The
+ * inner x + beta*x^3 is written as the FMA that nvcc's default contraction
+ * forms from the reference expression. */
+static inline float gelu_f(float x, int fp16_input) {
+    const float kAlpha = 0.7978845608028654f;
+    const float kBeta = 0.044715f;
+    float inner = fmaf(kBeta * x * x, x, x);
+    float act = 0.5f * x * (1.0f + tanhf(kAlpha * inner));
+    return fp16_input ? f16_to_f32(f32_to_f16_rn(act)) : bf16_to_f32(f32_to_bf16_rn(act));
+}
+
+/* ConvRot activation quantizer.
+ *   input : [rows, act==1 ? 2k : k] of bf16 (in_fp16=0) or fp16 (in_fp16=1)
+ *   act   : 0 none, 1 SwiGLU (gate = first half, up = second half), 2 tanh-GELU
+ *   int4  : 0 -> out int8 [rows, k];  1 -> packed int4 [rows, k/2] (low = even col)
+ *   staged: 0 -> BF16 row-buffer kernel (convrot_quant.cu:350-444)
+ *           1 -> staged two-kernel path (convrot_quant.cu:158-291)
+ *   scales: [rows] fp32
+ * The two forms differ only in how the per-row scale is formed
+ * (staged: min(amax,max)*(1/127); row-buffer: min(amax,max)/127) and in the
+ * staged path's FP16 scratch for FP16 inputs.
+ */
+void orc_convrot_quantize(const uint16_t *input, int64_t rows, int64_t k, int act, int int4,
+                          int staged, int in_fp16, int8_t *out, float *scales) {
+    const int64_t in_width = act == 1 ? 2 * k : k;
+    const int groups = (int)(k / GROUP);
+    float xin[GROUP], y[GROUP];
+    uint16_t *buf = (uint16_t *)malloc((size_t)k * sizeof(uint16_t));
+    for (int64_t row = 0; row < rows; ++row) {
+        const uint16_t *src = input + row * in_width;
+        float amax = 0.0f;
+        for (int g = 0; g < groups; ++g) {
+            for (int i = 0; i < GROUP; ++i) {
+                int64_t col = (int64_t)g * GROUP + i;
+                float v;
+                if (act == 1) {
+                    float gate = in_fp16 ? f16_to_f32(src[col]) : bf16_to_f32(src[col]);
+                    float up = in_fp16 ? f16_to_f32(src[k + col]) : bf16_to_f32(src[k + col]);
+                    v = swiglu_f(gate, up);
+                } else if (act == 2) {
+                    float x = in_fp16 ? f16_to_f32(src[col]) : bf16_to_f32(src[col]);
+                    v = gelu_f(x, in_fp16);
+                } else {
+                    v = in_fp16 ? f16_to_f32(src[col]) : bf16_to_f32(src[col]);
+                }
+                xin[i] = v;
+            }
+            fht256(xin, y);
+            for (int i = 0; i < GROUP; ++i) {
+                /* fht_store_bf16_absmax: store the rounded value, take the
+                 * absmax of the fp32 value (convrot_quant.cu:311-330). */
+                buf[(int64_t)g * GROUP + i] = in_fp16 ? f32_to_f16_rn(y[i]) : f32_to_bf16_rn(y[i]);
+                amax = fmaxf(amax, fabsf(y[i]));
+            }
+        }
+        const float fmax_in = in_fp16 ? 65504.0f : 3.38953139e38f;
+        const float qmax = int4 ? 7.0f : 127.0f;
+        const float floor_v = int4 ? 1.0e-10f : 1.0e-30f;
+        float clipped = fminf(amax, fmax_in);
+        float scale = staged ? fmaxf(clipped * (1.0f / qmax), floor_v)
+                             : fmaxf(clipped / qmax, floor_v);
+        scales[row] = scale;
+        if (int4) {
+            /* convrot_quant.cu:418-433 / :280-290 */
+            const float inv = 1.0f / scale;
+            int8_t *dst = out + row * (k / 2);
+            for (int64_t pc = 0; pc < k / 2; ++pc) {
+                float lo_v = in_fp16 ? f16_to_f32(buf[2 * pc]) : bf16_to_f32(buf[2 * pc]);
+                float hi_v = in_fp16 ? f16_to_f32(buf[2 * pc + 1]) : bf16_to_f32(buf[2 * pc + 1]);
+                float lo = nearbyintf(lo_v * inv);
+                float hi = nearbyintf(hi_v * inv);
+                lo = fminf(7.0f, fmaxf(-7.0f, lo));
+                hi = fminf(7.0f, fmaxf(-7.0f, hi));
+                uint8_t lb = (uint8_t)((int8_t)lo) & 0x0f;
+                uint8_t hb = (uint8_t)((int8_t)hi) & 0x0f;
+                dst[pc] = (int8_t)(lb | (hb << 4));
+            }
+        } else {
+            /* convrot_quant.cu:417,434-442 / :69-73,242-247 */
+            float rs = in_fp16 ? f16_to_f32(f32_to_f16_rn(scale)) : bf16_to_f32(f32_to_bf16_rn(scale));
+            int8_t *dst = out + row * k;
+            for (int64_t c = 0; c < k; ++c) {
+                float v = in_fp16 ? f16_to_f32(buf[c]) : bf16_to_f32(buf[c]);
+                float d = v / rs;
+                d = in_fp16 ? f16_to_f32(f32_to_f16_rn(d)) : bf16_to_f32(f32_to_bf16_rn(d));
+                float q = nearbyintf(d);
+                q = fminf(127.0f, fmaxf(-128.0f, q));
+                dst[c] = (int8_t)q;
+            }
+        }
+    }
+    free(buf);
+}
+
+/* Rotated bf16 values only (the staged kernel's `rotated` scratch,
+ * convrot_quant.cu:158-211), for diagnostics. */
+void orc_convrot_rotate_bf16(const uint16_t *input, int64_t rows, int64_t k, uint16_t *out,
+                             float *group_absmax) {
+    const int groups = (int)(k / GROUP);
+    float xin[GROUP], y[GROUP];
+    for (int64_t row = 0; row < rows; ++row) {
+        for (int g = 0; g < groups; ++g) {
+            float am = 0.0f;
+            for (int i = 0; i < GROUP; ++i) xin[i] = bf16_to_f32(input[row * k + (int64_t)g * GROUP + i]);
+            fht256(xin, y);
+            for (int i = 0; i < GROUP; ++i) {
+                out[row * k + (int64_t)g * GROUP + i] = f32_to_bf16_rn(y[i]);
+                am = fmaxf(am, fabsf(y[i]));
+            }
+            group_absmax[row * groups + g] = am;
+        }
+    }
+}
+
+/* ------------------------------------------------------- INT8 GEMM ------- */
+
+/* acc[m, n] = sum_k A[m, k] * W[n, k] in exact integer arithmetic
+ * (kernel/csrc/turing/w4a8.cu:376-418: S8 x S8 -> S32, OpMultiplyAddSaturate;
+ * with |acc| <= 127*128*K no saturation occurs for K < 132,000). Rows given by
+ * row_index (so tests can sample rows of a large problem); n_rows rows out. */
+void orc_int8_gemm_rows(const int8_t *A, const int8_t *W, int64_t N, int64_t K,
+                        const int64_t *row_index, int64_t n_rows, int32_t *acc) {
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const int8_t *a = A + row_index[r] * K;
+        for (int64_t n = 0; n < N; ++n) {
+            const int8_t *w = W + n * K;
+            int32_t s = 0;
+            for (int64_t k = 0; k < K; ++k) s += (int32_t)a[k] * (int32_t)w[k];
+            acc[r * N + n] = s;
+        }
+    }
+}
+
+/* Dequantize epilogue: v = ((float)acc * a_s[m]) * w_s[n] (+ bias[n]) -> bf16 RNE.
+ * Operation order of kernel/csrc/turing/bf16_epilogue.cu:105-119 and of the
+ * GEMM EVT tree w4a8.cu:474-525 (multiply by the row scale, then the column
+ * scale, then add the bias).  The add is a separate rounding here (no FMA);
+ * the CUDA epilogue in this repository uses the same two-step form.
+ * w_scalar: weight_scale has one element (bf16_epilogue.cu:81-89). */
+void orc_dequant_bf16(const int32_t *acc, int64_t rows, int64_t cols, int64_t acc_stride,
+                      const float *a_s, const float *w_s, int w_scalar, const float *bias,
+                      uint16_t *out) {
+    for (int64_t m = 0; m < rows; ++m) {
+        for (int64_t n = 0; n < cols; ++n) {
+            float v = (float)acc[m * acc_stride + n] * a_s[m];
+            v = v * (w_scalar ? w_s[0] : w_s[n]);
+            if (bias) v = v + bias[n];
+            out[m * cols + n] = f32_to_bf16_rn(v);
+        }
+    }
+}
+
+/* ------------------------------------------------------ weight decode ---- */
+
+/* Legacy signed-nibble W4: low nibble = even k, sign extended
+ * (w4a8.cu:34-72, validate_compatible.py:28-40). packed [N, K/2] -> int8 [N, K]. */
+void orc_unpack_int4(const int8_t *packed, int64_t n, int64_t k, int8_t *out) {
+    for (int64_t r = 0; r < n; ++r) {
+        for (int64_t j = 0; j < k / 2; ++j) {
+            uint8_t b = (uint8_t)packed[r * (k / 2) + j];
+            int lo = b & 0xf, hi = b >> 4;
+            if (lo >= 8) lo -= 16;
+            if (hi >= 8) hi -= 16;
+            out[r * k + 2 * j] = (int8_t)lo;
+            out[r * k + 2 * j + 1] = (int8_t)hi;
+        }
+    }
+}
+
+/* Grouped-codebook W4 decode (w4a8.cu:907-973, iterator :209-223):
+ * w8[n,k] = clamp(rint_even(codebook[idx] * float(e4m3(group_scale[n, k/g]))), -127, 127).
+ * idx: low nibble = even column. */
+void orc_codebook_decode(const int8_t *packed, const uint8_t *group_scale, const float *codebook,
+                         int64_t n, int64_t k, int64_t group_size, int8_t *out) {
+    const int64_t gpr = k / group_size;
+    for (int64_t r = 0; r < n; ++r) {
+        for (int64_t c = 0; c < k; ++c) {
+            uint8_t b = (uint8_t)packed[r * (k / 2) + c / 2];
+            int code = (c & 1) ? (b >> 4) : (b & 0xf);
+            float s = orc_e4m3_to_f32(group_scale[r * gpr + c / group_size]);
+            float v = codebook[code] * s;
+            float q = nearbyintf(v);
+            if (q > 127.0f) q = 127.0f;
+            if (q < -127.0f) q = -127.0f;
+            out[r * k + c] = (int8_t)q;
+        }
+    }
+}
+
+/* ----------------------------------------------------------- Sage quant -- */
+
+/* cvt.rni.sat.s8.f32: round to nearest even, saturate, NaN -> 0
+ * (kernel/csrc/turing/sage/numeric_conversion.cuh:144-149). */
+static inline int8_t cvt_rni_sat_s8(float x) {
+    if (isnan(x)) return 0;
+    float r = nearbyintf(x);
+    if (r > 127.0f) r = 127.0f;
+    if (r < -128.0f) r = -128.0f;
+    return (int8_t)r;
+}
+
+/* Per-tile INT8 quantizer QuantInt8Kernel (kernel/csrc/turing/sage/fused.cu:66-200).
+ * x is [tiles_outer, L, D] with arbitrary strides given in elements:
+ *   element (o, t, d) at x[o*s_outer + t*s_tok + d]; out uses the same
+ *   strides (the reference requires contiguous outputs with the input shape).
+ * tile tokens T (16 = Q per-warp, 64 = K per-block).  scale [outer, tiles].
+ * mean (optional, bf16/f16 bits, [outer, D] with stride s_mean_outer): the
+ * sub_mean branch (fused.cu:97-128), subtracted in fp32.
+ * Division semantics: the reference extension is built with --use_fast_math;
+ * this oracle fixes IEEE 127/amax and amax/127 (see the module docstring). */
+void orc_sage_quant(const uint16_t *x, int in_fp16, int64_t outer, int64_t L, int64_t D,
+                    int64_t s_outer, int64_t s_tok, int64_t T, int64_t tiles,
+                    const uint16_t *mean, int64_t s_mean_outer, int8_t *out, float *scale) {
+    /* tiles >= ceil(L/T): the per-warp Q layout pads to whole 64-token blocks
+     * and stores a scale for every warp tile (empty ones: 1e-7 / 127). */
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t t = 0; t < tiles; ++t) {
+            float amax = 0.0000001f;
+            for (int64_t i = 0; i < T; ++i) {
+                int64_t tok = t * T + i;
+                if (tok >= L) break;
+                for (int64_t d = 0; d < D; ++d) {
+                    uint16_t h = x[o * s_outer + tok * s_tok + d];
+                    float v = in_fp16 ? f16_to_f32(h) : bf16_to_f32(h);
+                    if (mean) {
+                        uint16_t mh = mean[o * s_mean_outer + d];
+                        v -= in_fp16 ? f16_to_f32(mh) : bf16_to_f32(mh);
+                    }
+                    amax = fmaxf(amax, fabsf(v));
+                }
+            }
+            scale[o * tiles + t] = amax / 127.0f;
+            float tmp = 127.0f / amax;
+            for (int64_t i = 0; i < T; ++i) {
+                int64_t tok = t * T + i;
+                if (tok >= L) break;
+                for (int64_t d = 0; d < D; ++d) {
+                    uint16_t h = x[o * s_outer + tok * s_tok + d];
+                    float v = in_fp16 ? f16_to_f32(h) : bf16_to_f32(h);
+                    if (mean) {
+                        uint16_t mh = mean[o * s_mean_outer + d];
+                        v -= in_fp16 ? f16_to_f32(mh) : bf16_to_f32(mh);
+                    }
+                    out[o * s_outer + tok * s_tok + d] = cvt_rni_sat_s8(v * tmp);
+                }
+            }
+        }
+    }
+}
+
+/* K smoothing mean over tokens, per (outer, channel): accumulated in double,
+ * divided by L, rounded to float and then to the input dtype.  The sum is in
+ * double so that the value does not depend on the summation order the CUDA
+ * kernel uses (it also accumulates in double). */
+void orc_token_mean(const uint16_t *x, int in_fp16, int64_t outer, int64_t L, int64_t D,
+                    int64_t s_outer, int64_t s_tok, uint16_t *mean) {
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t d = 0; d < D; ++d) {
+            double s = 0.0;
+            for (int64_t t = 0; t < L; ++t) {
+                uint16_t h = x[o * s_outer + t * s_tok + d];
+                s += (double)(in_fp16 ? f16_to_f32(h) : bf16_to_f32(h));
+            }
+            float m = (float)(s / (double)L);
+            mean[o * D + d] = in_fp16 ? f32_to_f16_rn(m) : f32_to_bf16_rn(m);
+        }
+    }
+}
+
+/* ------------------------------------------------------------ helpers ---- */
+
+void orc_f32_to_bf16(const float *x, int64_t n, uint16_t *out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f32_to_bf16_rn(x[i]);
+}
+
+void orc_bf16_to_f32(const uint16_t *x, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = bf16_to_f32(x[i]);
+}
+
+void orc_f32_to_f16(const float *x, int64_t n, uint16_t *out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f32_to_f16_rn(x[i]);
+}
+
+void orc_f16_to_f32(const uint16_t *x, int64_t n, float *out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f16_to_f32(x[i]);
+}

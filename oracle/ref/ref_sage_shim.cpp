@@ -1,0 +1,16 @@
+// TEST INFRASTRUCTURE ONLY: pybind shim exposing the reference's own Sage
+// quantizers and attention (kernel/csrc/turing/sage/fused.h, attn_cuda_sm75.h),
+// compiled from the reference checkout by oracle/ref/build_ref.py into
+// oracle/_ref/.  Used to generate golden fixtures on a B200.
+#include <torch/extension.h>
+
+#include "attn_cuda_sm75.h"
+#include "fused.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("quant_per_block_int8_cuda",
+        py::overload_cast<at::Tensor, at::Tensor, at::Tensor, int, int>(&quant_per_block_int8_cuda));
+  m.def("quant_per_warp_int8_cuda",
+        py::overload_cast<at::Tensor, at::Tensor, at::Tensor, int, int, int>(&quant_per_warp_int8_cuda));
+  m.def("qk_int8_sv_f16_accum_f32_attn", &qk_int8_sv_f16_accum_f32_attn);
+}

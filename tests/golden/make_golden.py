@@ -1,0 +1,168 @@
+"""Generate the golden fixtures under tests/golden/ by running the REFERENCE's
+own CUDA kernels (built from its sources by oracle/ref/build_ref.py into
+oracle/_ref) on seeded CPU-generated inputs, on a B200.
+
+    python tests/golden/make_golden.py [out_dir]
+
+Each fixture is a compressed .npz holding the inputs (as raw bits) and the
+reference's outputs.  tests/test_oracle_golden.py checks the CPU oracle
+against them; nothing at run time reads the reference checkout.
+"""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+from oracle import refkernels as R  # noqa: E402
+
+
+def bits(t):
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16) \
+        if t.dtype in (torch.bfloat16, torch.float16) else t.detach().cpu().numpy()
+
+
+def act(rows, cols, seed, outliers=True):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((rows, cols), generator=g)
+    if outliers:
+        idx = torch.randperm(cols, generator=g)[: max(1, int(round(cols * 0.005)))]
+        x[:, idx] *= 20.0
+    return x.to(torch.bfloat16)
+
+
+def main(out_dir: Path) -> None:
+    out_dir.mkdir(parents=True, exist_ok=True)
+    dev = torch.device("cuda:0")
+    L = R.linear()
+    S = R.sage()
+    fx = {}
+
+    # --- ConvRot row-buffer (plain / SwiGLU / GELU, INT8 / INT4) ---------------
+    cases = {"plain_5120": (act(8, 5120, 1), 0, 0), "plain_256": (act(3, 256, 2), 0, 0),
+             "swiglu_5376": (act(3, 2 * 5376, 3, False), 1, 0),
+             "gelu_13824": (act(4, 13824, 4), 0, 1)}
+    edge = np.zeros((3, 512), np.uint16)
+    edge[0, 5], edge[1, :], edge[2, 300] = 0x7FC0, 0x7F7F, 0xFF80
+    cases["edge_512"] = (torch.from_numpy(edge.view(np.int16)).view(torch.bfloat16), 0, 0)
+    for name, (x, swiglu, gelu) in cases.items():
+        hidden = x.shape[1] // (2 if swiglu else 1)
+        rec = {"x": bits(x)}
+        for int4 in (0, 1):
+            q = torch.empty((x.shape[0], hidden // 2 if int4 else hidden), dtype=torch.int8, device=dev)
+            s = torch.empty((x.shape[0], 1), dtype=torch.float32, device=dev)
+            xd = x.to(dev)
+            R.check(L.ref_bf16_convrot(R.ptr(xd), x.shape[0], hidden, swiglu, gelu, int4, R.ptr(q),
+                                       R.ptr(s), R.stream()), "convrot")
+            torch.cuda.synchronize()
+            rec[f"q{4 if int4 else 8}"], rec[f"s{4 if int4 else 8}"] = bits(q), bits(s)
+            if swiglu or gelu:
+                for fp16 in (0, 1):
+                    xs = x.to(torch.float16) if fp16 else x
+                    xs = xs.to(dev)
+                    r = torch.empty((x.shape[0], hidden), dtype=xs.dtype, device=dev)
+                    pa = torch.empty((x.shape[0], hidden // 256), dtype=torch.float32, device=dev)
+                    q2 = torch.empty_like(q)
+                    s2 = torch.empty_like(s)
+                    R.check(L.ref_staged_convrot(R.ptr(xs), fp16, x.shape[0], hidden, gelu, int4,
+                                                 R.ptr(r), R.ptr(pa), R.ptr(q2), R.ptr(s2),
+                                                 R.stream()), "staged convrot")
+                    torch.cuda.synchronize()
+                    tag = f"staged{'16' if fp16 else ''}_{4 if int4 else 8}"
+                    rec[f"q_{tag}"], rec[f"s_{tag}"] = bits(q2), bits(s2)
+        fx[f"convrot_{name}"] = rec
+
+    # --- W8A8 linear / W4A8 / codebook / dequant ------------------------------
+    for i, (m, n, k) in enumerate([(33, 128, 128), (129, 264, 256)]):
+        g = torch.Generator().manual_seed(4300 + i)
+        a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+        w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+        a_s = torch.rand((m,), generator=g) * 0.02 + 0.001
+        w_s = torch.rand((n,), generator=g) * 4e-3 + 1e-3
+        b = (torch.randn((n,), generator=g) * 0.02).to(torch.bfloat16).float()
+        o = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        ad, wd, asd, wsd, bd = (t.to(dev) for t in (a, w, a_s, w_s, b))
+        R.check(L.ref_int8_linear(R.ptr(ad), R.ptr(wd), R.ptr(asd), R.ptr(wsd), R.ptr(bd), R.ptr(o),
+                                  m, n, k, R.stream()), "int8 linear")
+        torch.cuda.synchronize()
+        fx[f"int8_linear_{m}x{n}x{k}"] = {"a": a.numpy(), "w": w.numpy(), "a_s": a_s.numpy(),
+                                          "w_s": w_s.numpy(), "bias": b.numpy(), "out": bits(o)}
+    g = torch.Generator().manual_seed(4301)
+    m, n, k = 17, 72, 80
+    a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+    w = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    packed = ((w[:, 0::2].int() & 0xF) | ((w[:, 1::2].int() & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.02 + 0.001
+    w_s = torch.rand((n,), generator=g) * 0.03 + 0.001
+    o = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    ad, pd, asd, wsd = (t.to(dev) for t in (a, packed, a_s, w_s))
+    R.check(L.ref_w4a8_linear(R.ptr(ad), R.ptr(pd), R.ptr(asd), R.ptr(wsd), None, R.ptr(o), m, n, k,
+                              R.stream()), "w4a8")
+    torch.cuda.synchronize()
+    fx["w4a8_17x72x80"] = {"a": a.numpy(), "w_packed": packed.numpy(), "a_s": a_s.numpy(),
+                           "w_s": w_s.numpy(), "out": bits(o)}
+    for gsz in (16, 128):
+        g = torch.Generator().manual_seed(4388 + gsz)
+        m, n, k = 7, 24, 256
+        a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+        codes = torch.randint(0, 16, (n, k), generator=g, dtype=torch.int32)
+        packed = ((codes[:, 0::2] & 0xF) | ((codes[:, 1::2] & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+        cb = torch.linspace(-1.0, 1.0, 16)
+        gs = (torch.rand((n, k // gsz), generator=g) * 64.0 + 4.0).to(torch.float8_e4m3fn).view(torch.uint8)
+        a_s = torch.rand((m,), generator=g) * 0.01
+        c_s = torch.rand((n,), generator=g) * 0.02
+        b = torch.randn((n,), generator=g).to(torch.bfloat16).float()
+        ws = torch.empty((n, k), dtype=torch.int8, device=dev)
+        o = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        t = [x.to(dev) for x in (a, packed, a_s, gs, c_s, cb, b)]
+        R.check(L.ref_codebook_linear(*[R.ptr(x) for x in t], R.ptr(ws), n, R.ptr(o), m, n, k, gsz,
+                                      R.stream()), "codebook")
+        torch.cuda.synchronize()
+        fx[f"codebook_g{gsz}"] = {"a": a.numpy(), "w_packed": packed.numpy(), "a_s": a_s.numpy(),
+                                  "gs": gs.numpy(), "c_s": c_s.numpy(), "codebook": cb.numpy(),
+                                  "bias": b.numpy(), "w8": ws.cpu().numpy(), "out": bits(o)}
+    g = torch.Generator().manual_seed(2)
+    acc = torch.randint(-2 ** 24, 2 ** 24, (37, 64), generator=g, dtype=torch.int32)
+    a_s = torch.rand((37,), generator=g) * 0.01
+    w_s = torch.rand((64,), generator=g) * 0.02
+    o = torch.empty((37, 64), dtype=torch.bfloat16, device=dev)
+    t = [x.to(dev) for x in (acc, a_s, w_s)]
+    R.check(L.ref_dequant(R.ptr(t[0]), R.ptr(t[1]), R.ptr(t[2]), 64, R.ptr(o), 37, 64, R.stream()),
+            "dequant")
+    torch.cuda.synchronize()
+    fx["dequant_37x64"] = {"acc": acc.numpy(), "a_s": a_s.numpy(), "w_s": w_s.numpy(), "out": bits(o)}
+
+    # --- Sage quantizers + attention (reference built with --use_fast_math) ---
+    for layout, lid in (("HND", 1), ("NHD", 0)):
+        g = torch.Generator().manual_seed(77 + lid)
+        q = torch.randn((1, 2, 129, 128), generator=g).to(torch.bfloat16)
+        k = (torch.randn((1, 2, 151, 128), generator=g) + 1.5).to(torch.bfloat16)
+        v = torch.randn((1, 2, 151, 128), generator=g).to(torch.bfloat16)
+        if layout == "NHD":
+            q, k, v = (x.transpose(1, 2).contiguous() for x in (q, k, v))
+        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        q8 = torch.empty(q.shape, dtype=torch.int8, device=dev)
+        k8 = torch.empty(k.shape, dtype=torch.int8, device=dev)
+        qs = torch.empty((1, 2, 12), dtype=torch.float32, device=dev)
+        ks = torch.empty((1, 2, 3), dtype=torch.float32, device=dev)
+        S.quant_per_warp_int8_cuda(qd, q8, qs, 64, 16, lid)
+        S.quant_per_block_int8_cuda(kd, k8, ks, 64, lid)
+        o = torch.empty(q.shape, dtype=torch.bfloat16, device=dev)
+        S.qk_int8_sv_f16_accum_f32_attn(q8, k8, vd, o, qs, ks, lid, 0, 2, 128 ** -0.5, 0)
+        torch.cuda.synchronize()
+        fx[f"sage_{layout}"] = {"q": bits(q), "k": bits(k), "v": bits(v), "q8": bits(q8),
+                                "qs": bits(qs), "k8": bits(k8), "ks": bits(ks), "out": bits(o)}
+
+    for name, rec in fx.items():
+        np.savez_compressed(out_dir / f"{name}.npz", **rec)
+    print(f"wrote {len(fx)} fixtures to {out_dir}")
+
+
+if __name__ == "__main__":
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent)
