@@ -52,6 +52,9 @@ SIGNATURES: dict[str, list] = {
     "tb_quant_per_warp_int8": [_p, _int, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int,
                                _int, _int, _p],
     "tb_token_mean": [_p, _int, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int, _p],
+    "tb_qk_int8_sv_f16_accum_f32_attn": [_p, _p, _p, _int, _p, _int, _p, _p, _p, _i64, _i64,
+                                         _i64, _i64, _i64, _i64, _p, _int, _int, _int,
+                                         ctypes.c_float, _p],
 }
 
 _lock = threading.Lock()

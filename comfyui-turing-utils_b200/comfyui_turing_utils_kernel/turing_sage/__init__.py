@@ -1,6 +1,6 @@
 """Sage INT8 attention facade (kernel/comfyui_turing_utils_kernel/turing_sage/
-__init__.py): quantizers and, once the attention kernel is loaded, the
-sageattn family."""
+__init__.py:16-430): availability probes, the sageattn family, split
+prequantize/execute, and the torch.compile-friendly custom-op wrapper."""
 from __future__ import annotations
 
 import importlib
@@ -12,6 +12,7 @@ from .quant import per_warp_int8, quantize_key_per_block, quantize_query_per_war
 
 def available() -> bool:
     try:
+        importlib.import_module("comfyui_turing_utils_kernel._sage_qattn_sm75")
         importlib.import_module("comfyui_turing_utils_kernel._sage_fused_sm75")
         from .._lib import load
 
@@ -21,4 +22,37 @@ def available() -> bool:
     return True
 
 
-__all__ = ["available", "per_warp_int8", "quantize_key_per_block", "quantize_query_per_warp"]
+def sageattn(*args, **kwargs):
+    """Run the Sage INT8 attention (HND or NHD)."""
+    from .core import sageattn as _impl
+
+    return _impl(*args, **kwargs)
+
+
+def sageattn_compiled(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor, *,
+                      tensor_layout: str = "HND", is_causal: bool = False,
+                      sm_scale: float | None = None) -> torch.Tensor:
+    """torch.compile leaf (turing_sage/__init__.py:166-184)."""
+    from .custom_ops import sage_attention
+
+    return sage_attention(query, key, value, tensor_layout, is_causal,
+                          -1.0 if sm_scale is None else float(sm_scale))
+
+
+def prequantize_sageattn(*args, **kwargs):
+    from .core import prequantize_sageattn as _impl
+
+    return _impl(*args, **kwargs)
+
+
+def sageattn_from_prequantized(*args, **kwargs):
+    from .core import sageattn_from_prequantized as _impl
+
+    return _impl(*args, **kwargs)
+
+
+from . import custom_ops  # noqa: E402,F401  (registers turing_utils::sage_attention)
+
+__all__ = ["available", "per_warp_int8", "prequantize_sageattn", "quantize_key_per_block",
+           "quantize_query_per_warp", "sageattn", "sageattn_compiled",
+           "sageattn_from_prequantized"]

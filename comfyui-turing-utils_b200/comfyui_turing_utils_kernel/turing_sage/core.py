@@ -1,0 +1,149 @@
+"""Sage INT8 attention facades (kernel/comfyui_turing_utils_kernel/turing_sage/
+core.py:367-653): split prequantize / execute, head-dim padding, output
+slicing, the same dataclass and validation messages.
+
+Differences from the reference, by design:
+  * no short-sequence SDPA fallback: the sm_100a kernel masks any length;
+  * smooth_k=True is accepted (K mean smoothing, softmax-invariant); the
+    reference rejects it in production (core.py:421-422);
+  * head_dim <= 128 is padded to 128 (the kernel's one tile width).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from functools import wraps
+from typing import Any, Optional
+
+import torch
+
+from .. import _sage_qattn_sm75 as _qattn
+from .quant import per_warp_int8
+
+
+@dataclass(frozen=True, slots=True)
+class PrequantizedSageAttention:
+    query_int8: torch.Tensor
+    query_scale: torch.Tensor
+    key_int8: torch.Tensor
+    key_scale: torch.Tensor
+    value: torch.Tensor
+    tensor_layout: str
+    original_head_dim: int
+    is_causal: bool
+    sm_scale: float
+
+
+def _on_input_device(function):
+    @wraps(function)
+    def wrapped(q: torch.Tensor, *args, **kwargs):
+        with torch.cuda.device(q.device):
+            return function(q, *args, **kwargs)
+
+    return wrapped
+
+
+def _validate_fixed_qkv(q, k, v, tensor_layout: str) -> None:
+    """core.py:323-340."""
+    if tensor_layout not in {"HND", "NHD"}:
+        raise ValueError(f"Unsupported tensor_layout: {tensor_layout}")
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("fixed-length Q/K/V must be four-dimensional")
+    head_dim = q.size(-1)
+    if k.size(-1) != head_dim or v.size(-1) != head_dim:
+        raise ValueError("Q/K/V head dimensions must match")
+    head_axis = 1 if tensor_layout == "HND" else 2
+    seq_axis = 2 if tensor_layout == "HND" else 1
+    if q.size(0) != k.size(0) or q.size(0) != v.size(0):
+        raise ValueError("Q/K/V batch sizes must match")
+    if k.size(head_axis) != v.size(head_axis) or k.size(seq_axis) != v.size(seq_axis):
+        raise ValueError("K/V head counts and sequence lengths must match")
+    if k.size(head_axis) == 0 or q.size(head_axis) % k.size(head_axis) != 0:
+        raise ValueError("the Q head count must be divisible by the KV head count")
+    if q.size(seq_axis) == 0 or k.size(seq_axis) == 0:
+        raise ValueError("empty Q/K sequences are not supported")
+
+
+@_on_input_device
+def prequantize_sageattn(q, k, v, tensor_layout: str = "HND", is_causal: bool = False,
+                         sm_scale: Optional[float] = None, smooth_k: bool = False,
+                         **kwargs: Any) -> PrequantizedSageAttention:
+    """Quantize Q (per 16-row warp tile) and K (per 64-key block) to INT8."""
+    if not q.is_cuda:
+        raise ValueError("Input tensors must be on CUDA")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("Turing Sage Q/K/V must be float16 or bfloat16")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("Q/K/V must be on the same device")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise TypeError("Q/K/V must have matching dtypes")
+    _validate_fixed_qkv(q, k, v, tensor_layout)
+    head_dim = q.size(-1)
+    if head_dim > 128:
+        raise ValueError(f"Unsupported head_dim: {head_dim}")
+    padding = 128 - head_dim
+    if padding:
+        q = torch.nn.functional.pad(q, (0, padding))
+        k = torch.nn.functional.pad(k, (0, padding))
+        v = torch.nn.functional.pad(v, (0, padding))
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError("the last Q/K/V dimension must be contiguous")
+    scale = float(sm_scale) if sm_scale is not None else head_dim ** -0.5
+    q_int8, q_scale, k_int8, k_scale = per_warp_int8(q, k, tensor_layout=tensor_layout,
+                                                     smooth_k=smooth_k)
+    return PrequantizedSageAttention(q_int8, q_scale, k_int8, k_scale, v.contiguous(),
+                                     tensor_layout, head_dim, bool(is_causal), scale)
+
+
+@_on_input_device
+def sageattn_prequantized(q_int8, q_scale, k_int8, k_scale, v, *, tensor_layout: str = "NHD",
+                          is_causal: bool = False, sm_scale: Optional[float] = None,
+                          return_lse: bool = False, output: Optional[torch.Tensor] = None):
+    """core.py:573-653 checks, then the tcgen05 kernel."""
+    if tensor_layout not in {"HND", "NHD"}:
+        raise ValueError(f"Unsupported tensor_layout: {tensor_layout}")
+    if q_int8.dtype != torch.int8 or k_int8.dtype != torch.int8:
+        raise TypeError("prequantized Sage Q/K must be int8")
+    if v.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("prequantized Sage V must be float16 or bfloat16")
+    if q_int8.ndim != 4 or k_int8.ndim != 4 or v.ndim != 4:
+        raise ValueError("prequantized Sage Q/K/V must be four-dimensional")
+    head_axis = 1 if tensor_layout == "HND" else 2
+    seq_axis = 2 if tensor_layout == "HND" else 1
+    if (q_int8.size(0) != k_int8.size(0) or k_int8.size(head_axis) != v.size(head_axis)
+            or k_int8.size(seq_axis) != v.size(seq_axis) or q_int8.size(-1) != k_int8.size(-1)
+            or q_int8.size(-1) != v.size(-1)):
+        raise ValueError("prequantized Sage Q/K/V shapes are incompatible")
+    if q_int8.size(-1) != 128:
+        raise ValueError("prequantized Sage on sm_100a requires head_dim 128 (pad smaller heads)")
+    scale = float(sm_scale) if sm_scale is not None else q_int8.size(-1) ** -0.5
+    if output is None:
+        output = torch.empty(q_int8.shape, dtype=v.dtype, device=v.device)
+    layout_id = 0 if tensor_layout == "NHD" else 1
+    lse = _qattn.qk_int8_sv_f16_accum_f32_attn(
+        q_int8.contiguous(), k_int8.contiguous(), v, output, q_scale.contiguous(),
+        k_scale.contiguous(), layout_id, int(is_causal), 2, scale, int(return_lse))
+    return (output, lse / 1.44269504) if return_lse else output
+
+
+def sageattn_from_prequantized(quantized: PrequantizedSageAttention, *, return_lse: bool = False):
+    with torch.cuda.device(quantized.query_int8.device):
+        result = sageattn_prequantized(
+            quantized.query_int8, quantized.query_scale, quantized.key_int8,
+            quantized.key_scale, quantized.value, tensor_layout=quantized.tensor_layout,
+            is_causal=quantized.is_causal, sm_scale=quantized.sm_scale, return_lse=return_lse)
+    if return_lse:
+        output, lse = result
+        return output[..., :quantized.original_head_dim], lse
+    return result[..., :quantized.original_head_dim]
+
+
+@_on_input_device
+def sageattn(q, k, v, tensor_layout: str = "HND", is_causal: bool = False,
+             sm_scale: Optional[float] = None, return_lse: bool = False, smooth_k: bool = False,
+             **kwargs: Any):
+    """Sage INT8 attention: per-warp INT8 Q, per-block INT8 K (optionally mean
+    smoothed), 16-bit PV with fp32 accumulation (core.py:543-570)."""
+    quantized = prequantize_sageattn.__wrapped__(q, k, v, tensor_layout=tensor_layout,
+                                                 is_causal=is_causal, sm_scale=sm_scale,
+                                                 smooth_k=smooth_k)
+    return sageattn_from_prequantized(quantized, return_lse=return_lse)

@@ -164,3 +164,67 @@ int tb_token_mean(const void* input, int dtype, void* mean, int64_t B, int64_t H
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ attention ----
+namespace tb {
+struct AttnArgs {
+  const int8_t* q;
+  const int8_t* k;
+  const void* v;
+  int v_dtype;
+  void* out;
+  int out_dtype;
+  const float* q_scale;
+  const float* k_scale;
+  float* lse;
+  int64_t B, Hq, Hk, Lq, Lk, D;
+  int64_t q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl, o_sb, o_sh, o_sl;
+  int64_t q_tiles_scale, k_tiles_scale;
+  int causal;
+  float sm_scale;
+};
+void sage_attn_launch(const AttnArgs& a, cudaStream_t stream);
+}  // namespace tb
+
+extern "C" int tb_qk_int8_sv_f16_accum_f32_attn(
+    const int8_t* q, const int8_t* k, const void* v, int v_dtype, void* out, int out_dtype,
+    const float* q_scale, const float* k_scale, float* lse, int64_t B, int64_t Hq, int64_t Hk,
+    int64_t Lq, int64_t Lk, int64_t D, const int64_t* strides, int layout, int is_causal,
+    int qk_quant_gran, float sm_scale, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(q && k && v && out && q_scale && k_scale && strides,
+               "query, key, value, output and scales must be CUDA tensors");
+    TB_REQUIRE(layout == TB_LAYOUT_NHD || layout == TB_LAYOUT_HND, "tensor_layout must be 0 or 1");
+    TB_REQUIRE(qk_quant_gran == 2, "production Turing Sage requires per-warp Q/K quantization");
+    TB_REQUIRE(B > 0 && Hq > 0 && Hk > 0 && Lq > 0 && Lk > 0, "empty Q/K sequences are not supported");
+    TB_REQUIRE(Hq % Hk == 0, "num_qo_heads must be divisible by num_kv_heads");
+    TB_REQUIRE(Lq <= INT32_MAX && Lk <= INT32_MAX, "sequence length exceeds the kernel range");
+    tb::require_sm100();
+    tb::AttnArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.v_dtype = v_dtype;
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.q_scale = q_scale;
+    a.k_scale = k_scale;
+    a.lse = lse;
+    a.B = B;
+    a.Hq = Hq;
+    a.Hk = Hk;
+    a.Lq = Lq;
+    a.Lk = Lk;
+    a.D = D;
+    // strides: q (b, h, l), k (b, h, l), v (b, h, l), o (b, h, l), in elements.
+    a.q_sb = strides[0]; a.q_sh = strides[1]; a.q_sl = strides[2];
+    a.k_sb = strides[3]; a.k_sh = strides[4]; a.k_sl = strides[5];
+    a.v_sb = strides[6]; a.v_sh = strides[7]; a.v_sl = strides[8];
+    a.o_sb = strides[9]; a.o_sh = strides[10]; a.o_sl = strides[11];
+    a.q_tiles_scale = (Lq + 63) / 64 * 4;
+    a.k_tiles_scale = (Lk + 63) / 64;
+    a.causal = is_causal;
+    a.sm_scale = sm_scale;
+    tb::sage_attn_launch(a, static_cast<cudaStream_t>(stream));
+  });
+}

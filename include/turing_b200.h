@@ -173,6 +173,25 @@ TB_API int tb_token_mean(const void *input, int dtype, void *mean, int64_t B, in
                   int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_l, int layout,
                   tb_stream_t stream);
 
+/* ------------------------------------------------------- Sage attention -- */
+
+/* INT8 QK^T / 16-bit PV attention with fp32 accumulation: q, k int8 with
+ * per-warp (16-row) Q scales [B, Hq, ceil(Lq/64)*4] and per-block (64-key) K
+ * scales [B, Hk, ceil(Lk/64)]; v and out of dtype v_dtype (== out_dtype);
+ * strides: 12 element strides (batch, head, token) of q, k, v, out in that
+ * order, last dim contiguous; layout TB_LAYOUT_HND or TB_LAYOUT_NHD; D = 128
+ * (the binding pads 64 < D < 128); lse: optional [B, Hq, Lq] base-2 log-sum-exp.
+ * Replaces attn_cuda_sm75.h:21-31 qk_int8_sv_f16_accum_f32_attn
+ * (qk_int_sv_f16_cuda_sm75.cu:984-1123). */
+TB_API int tb_qk_int8_sv_f16_accum_f32_attn(const int8_t *q, const int8_t *k, const void *v,
+                                            int v_dtype, void *out, int out_dtype,
+                                            const float *q_scale, const float *k_scale,
+                                            float *lse, int64_t B, int64_t Hq, int64_t Hk,
+                                            int64_t Lq, int64_t Lk, int64_t D,
+                                            const int64_t *strides, int layout, int is_causal,
+                                            int qk_quant_gran, float sm_scale,
+                                            tb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,116 @@
+"""GPU parity: tcgen05 Sage INT8 attention vs references.
+
+Two bars:
+  * the reference's own validation tolerance against fp32 SDPA of the
+    unquantized inputs (kernel/scripts/validate_compatible.py:458-575:
+    rtol 0.08 / atol 0.06, MQA 0.15 / 0.12, LSE 0.02);
+  * the north-star bound against the oracle's fp32 dequantize-then-attention
+    of the kernel's own INT8 Q/K (cosine >= 0.9995, relative L2 <= 1e-2);
+    the quantizer codes themselves are bit-exact (test_gpu_sage_quant.py).
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from comfyui_turing_utils_kernel import turing_sage  # noqa: E402
+from comfyui_turing_utils_kernel.turing_sage import quant  # noqa: E402
+
+
+def _sdpa(q, k, v, causal=False, layout="HND"):
+    if layout == "NHD":
+        q, k, v = (t.transpose(1, 2) for t in (q, k, v))
+    out = torch.nn.functional.scaled_dot_product_attention(
+        q.float(), k.float(), v.float(), is_causal=causal, enable_gqa=q.size(1) != k.size(1))
+    return out.transpose(1, 2) if layout == "NHD" else out
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("head_dim,causal", [(32, False), (64, True), (96, False), (128, False),
+                                             (128, True)])
+def test_validate_sage_port(dtype, head_dim, causal):
+    g = torch.Generator().manual_seed(head_dim + 7 * causal)
+    q = (torch.randn((1, 4, 129, head_dim), generator=g) * 0.4).to(dtype).cuda()
+    k = (torch.randn((1, 2, 151, head_dim), generator=g) * 0.4).to(dtype).cuda()
+    v = torch.randn((1, 2, 151, head_dim), generator=g).to(dtype).cuda()
+    out = turing_sage.sageattn(q, k, v, tensor_layout="HND", is_causal=causal)
+    ref = _sdpa(q, k, v, causal)
+    torch.testing.assert_close(out.float(), ref, rtol=0.08, atol=0.06)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_nhd_and_prequantized_bridge(dtype):
+    g = torch.Generator().manual_seed(3)
+    q = (torch.randn((1, 4, 129, 128), generator=g) * 0.4).to(dtype).cuda()
+    k = (torch.randn((1, 2, 151, 128), generator=g) * 0.4).to(dtype).cuda()
+    v = torch.randn((1, 2, 151, 128), generator=g).to(dtype).cuda()
+    qn, kn, vn = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+    out_nhd = turing_sage.sageattn(qn, kn, vn, tensor_layout="NHD")
+    torch.testing.assert_close(out_nhd.float(), _sdpa(q, k, v).transpose(1, 2), rtol=0.08, atol=0.06)
+    from comfyui_turing_utils_kernel.turing_sage.core import sageattn_prequantized
+
+    q8, qs, k8, ks = quant.per_warp_int8(qn, kn, tensor_layout="NHD")
+    pre = sageattn_prequantized(q8, qs, k8, ks, vn, tensor_layout="NHD")
+    assert torch.equal(pre, out_nhd)
+
+
+def test_mqa_and_lse():
+    g = torch.Generator().manual_seed(4)
+    q = torch.randn((1, 4, 65, 64), generator=g).to(torch.bfloat16).cuda()
+    k = torch.randn((1, 1, 73, 64), generator=g).to(torch.bfloat16).cuda()
+    v = torch.randn((1, 1, 73, 64), generator=g).to(torch.bfloat16).cuda()
+    out, lse = turing_sage.sageattn(q, k, v, return_lse=True)
+    torch.testing.assert_close(out.float(), _sdpa(q, k, v), rtol=0.15, atol=0.12)
+    key = torch.repeat_interleave(k.float(), 4, dim=1)
+    ref_lse = torch.logsumexp(torch.matmul(q.float(), key.transpose(-2, -1)) * 64 ** -0.5, dim=-1)
+    torch.testing.assert_close(lse, ref_lse, rtol=0.02, atol=0.02)
+
+
+@pytest.mark.parametrize("L", [1, 63, 64, 127, 128, 129, 255, 256, 257, 1000])
+@pytest.mark.parametrize("smooth", [False, True])
+def test_north_star_bound_vs_dequant_attention(oracle, L, smooth):
+    g = torch.Generator().manual_seed(L)
+    q = torch.randn((2, 3, L, 128), generator=g).to(torch.bfloat16).cuda()
+    k = (torch.randn((2, 3, L, 128), generator=g)
+         + torch.randn((2, 3, 1, 128), generator=g) * 2.0).to(torch.bfloat16).cuda()
+    v = torch.randn((2, 3, L, 128), generator=g).to(torch.bfloat16).cuda()
+    pre = turing_sage.prequantize_sageattn(q, k, v, smooth_k=smooth)
+    out = turing_sage.sageattn_from_prequantized(pre)
+    ref = oracle.dequant_attention_reference(pre.query_int8.cpu(), pre.query_scale.cpu(),
+                                             pre.key_int8.cpu(), pre.key_scale.cpu(), v.cpu(),
+                                             sm_scale=128 ** -0.5)
+    m = oracle.metrics(out.cpu().float(), ref)
+    assert m["cosine"] >= oracle.NORTH_STAR_COSINE and m["rel_l2"] <= oracle.NORTH_STAR_REL_L2, m
+
+
+def test_config2_shape_sampled_rows(oracle):
+    """BASELINE config 2 (B=1, H=40, L=32760, D=128, K + per-channel offset,
+    K smoothing): all heads on the GPU; 64 sampled rows of 3 heads checked
+    against the dequantize-then-attention oracle over all 32760 keys."""
+    B, H, L, D = 1, 40, 32760, 128
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn((B, H, L, D), generator=g).to(torch.bfloat16)
+    k = (torch.randn((B, H, L, D), generator=g) + torch.randn((B, H, 1, D), generator=g) * 2.0
+         ).to(torch.bfloat16)
+    v = torch.randn((B, H, L, D), generator=g).to(torch.bfloat16)
+    pre = turing_sage.prequantize_sageattn(q.cuda(), k.cuda(), v.cuda(), smooth_k=True)
+    out = turing_sage.sageattn_from_prequantized(pre).cpu()
+    rows = torch.randperm(L, generator=torch.Generator().manual_seed(1))[:64]
+    for h in (0, 17, 39):
+        sl = slice(h, h + 1)
+        ref = oracle.dequant_attention_reference(
+            pre.query_int8[:, sl].cpu(), pre.query_scale[:, sl].cpu(), pre.key_int8[:, sl].cpu(),
+            pre.key_scale[:, sl].cpu(), v[:, sl], sm_scale=D ** -0.5, q_rows=rows)
+        m = oracle.metrics(out[:, sl][:, :, rows].float(), ref)
+        assert m["cosine"] >= oracle.NORTH_STAR_COSINE and m["rel_l2"] <= oracle.NORTH_STAR_REL_L2, m
+
+
+def test_custom_op_and_no_watchdog_errors():
+    q = torch.randn((1, 2, 200, 128), device="cuda").to(torch.bfloat16)
+    out = torch.ops.turing_utils.sage_attention(q, q, q, "HND", False, -1.0)
+    assert out.shape == q.shape and torch.isfinite(out.float()).all()
+    from comfyui_turing_utils_kernel import _lib
+
+    assert _lib.device_error() == 0
