@@ -181,6 +181,17 @@ class LinearWorkload:
         self.out_host.copy_(out, non_blocking=True)
         return out
 
+    cpu_sample_desc = "rows of X, full N and K (ConvRot oracle + torch fp32 dequantize-then-matmul)"
+
+    def roofline(self, dom_ms, peaks):
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.ops / (dom_ms * 1e-3) / 1e12
+        return {"kernel": self.dominant, "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s (MEASURED_PEAKS.json "
+                               "bf16_tflops); dense INT8 = 2 x BF16 on B200",
+                "kernel_ms": round(dom_ms, 4)}
+
     def cpu_reference_step(self, rows: int):
         """Reference CPU path on a row sample: ConvRot restatement + fp32
         dequantize-then-matmul (validate_compatible.py:110-114)."""
@@ -201,7 +212,82 @@ class LinearWorkload:
         self.bias_cpu = self.bias.cpu().float()
 
 
-WORKLOADS = {"linear": LinearWorkload}
+class AttentionWorkload:
+    name = "attention"
+    config = {"workload": "sage_int8_attention (BASELINE configs[1])", "batch": 1, "heads": 40,
+              "seq_len": 32760, "head_dim": 128, "layout": "HND", "causal": False,
+              "q_quant": "int8 per 16-token warp tile", "k_quant": "int8 per 64-token block",
+              "k_smoothing": True, "pv": "bf16 P x bf16 V, fp32 accumulation"}
+
+    def __init__(self, device, seed):
+        from comfyui_turing_utils_kernel import turing_sage
+        from comfyui_turing_utils_kernel.turing_sage import core
+
+        self.ts, self.core = turing_sage, core
+        B, H, L, D = (self.config[k] for k in ("batch", "heads", "seq_len", "head_dim"))
+        self.ops = 4.0 * B * H * L * L * D
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.q = torch.randn((B, H, L, D), generator=g, device=device).to(torch.bfloat16)
+        k = torch.randn((B, H, L, D), generator=g, device=device)
+        k += torch.randn((B, H, 1, D), generator=g, device=device) * 2.0
+        self.k = k.to(torch.bfloat16)
+        del k
+        self.v = torch.randn((B, H, L, D), generator=g, device=device).to(torch.bfloat16)
+        self.host = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
+        self.out_host = torch.empty_like(self.host[0]).pin_memory()
+        self.launches_per_step = 4  # Q quant, K token mean, K quant, attention
+        self.dominant = "sage_attn"
+        self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
+        self.d2h_bytes = self.out_host.numel() * 2
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        pre = self.core.prequantize_sageattn(self.q, self.k, self.v, smooth_k=True)
+        if ev:
+            ev[1].record()
+        out = self.core.sageattn_from_prequantized(pre)
+        if ev:
+            ev[2].record()
+        return out
+
+    def step_e2e(self):
+        dev = self.q.device
+        q, k, v = (t.to(dev, non_blocking=True) for t in self.host)
+        out = self.ts.sageattn(q, k, v, tensor_layout="HND", smooth_k=True)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    def roofline(self, dom_ms, peaks):
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.ops / (dom_ms * 1e-3) / 1e12
+        # QK^T runs at the INT8 rate, PV at the 16-bit rate: mixed floor.
+        half = self.ops / 2
+        floor_ms = (half / (int8_peak * 1e12) + half / (peaks["bf16_tflops"] * 1e12)) * 1e3
+        return {"kernel": self.dominant, "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s (MEASURED_PEAKS.json "
+                               "bf16_tflops); dense INT8 = 2 x BF16 on B200",
+                "mixed_floor_ms": round(floor_ms, 3),
+                "frac_of_mixed_floor": round(floor_ms / dom_ms, 4),
+                "kernel_ms": round(dom_ms, 4)}
+
+    def prepare_cpu(self):
+        self.q_cpu, self.k_cpu, self.v_cpu = (t[0].float() for t in self.host)
+
+    def cpu_reference_step(self, rows: int):
+        """Reference CPU path (validate_compatible.py:540-546): fp32 SDPA of
+        `rows` query rows of one head against all keys."""
+        h = self._cpu_head = (getattr(self, "_cpu_head", -1) + 1) % self.config["heads"]
+        q = self.q_cpu[h:h + 1, :rows]
+        out = torch.nn.functional.scaled_dot_product_attention(
+            q[None], self.k_cpu[h:h + 1][None], self.v_cpu[h:h + 1][None])
+        return out, 4.0 * rows * self.config["seq_len"] * self.config["head_dim"]
+
+    cpu_sample_desc = "query rows of one head (cycling heads) vs all 32760 keys, fp32 SDPA"
+
+
+WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload}
 
 
 def default_workload() -> str:
@@ -303,9 +389,8 @@ def run_ours(args, world, rank, local):
     dev_err = _lib.device_error()
 
     peaks = load_peaks()
-    int8_peak = 2.0 * peaks["bf16_tflops"]
-    achieved = wl.ops / (dom_avg * 1e-3) / 1e12
-    traffic = ncu_traffic(wl.dominant, wl.name)
+    roof = wl.roofline(dom_avg, peaks)
+    roof["traffic"] = ncu_traffic(wl.dominant, wl.name)
     result = {
         "metric": METRIC,
         "value": round(world * wl.ops / (ms * 1e-3) / 1e12, 2),
@@ -322,12 +407,7 @@ def run_ours(args, world, rank, local):
         "config": dict(wl.config, parallelism=f"independent shards x{world} (no collective)",
                        l2="256 MB buffer written between steps; per-step CUDA events exclude it"),
         "impl": "ours",
-        "roofline": {"kernel": wl.dominant, "bound": "tensor", "achieved": round(achieved, 1),
-                     "peak": round(int8_peak, 1), "unit": "TOPS",
-                     "frac": round(achieved / int8_peak, 4),
-                     "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s "
-                                    "(MEASURED_PEAKS.json bf16_tflops); dense INT8 = 2 x BF16 on B200",
-                     "traffic": traffic, "kernel_ms": round(dom_avg, 4)},
+        "roofline": roof,
         "e2e": {"value": round(world * wl.ops / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
                 "ms_per_step": round(e2e_ms, 4)},
@@ -354,8 +434,7 @@ def cpu_baseline(wl, args) -> dict:
         reps += 1
     dt = time.perf_counter() - t0
     return {"value": round(ops / dt / 1e12, 5), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{reps} x {rows} of {wl.config['m']} rows, full N and K "
-                      "(ConvRot oracle + torch fp32 dequantize-then-matmul)",
+            "sample": f"{reps} x {rows} {wl.cpu_sample_desc}",
             "seconds": round(dt, 2)}
 
 
@@ -377,8 +456,7 @@ def run_reference(args, world, rank, local):
         total_ops += ops
     value = total_ops / sum(times) / 1e12
     ms = sum(times) / len(times) * 1e3
-    sample = (f"{rows} of {wl.config['m']} rows per step, full N and K "
-              "(ConvRot oracle + torch fp32 dequantize-then-matmul)")
+    sample = f"{rows} {wl.cpu_sample_desc} per step"
     return {
         "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),

@@ -205,7 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = static_cast<uint32_t>(local >> 1) & 1u;
-      if (!mbar_wait(&sh->acc_full[acc], acc_phase, abort_flag, kDevWaitTimeoutEpilogue)) break;
+      // Warp vote: the tcgen05.ld below is warp-collective.
+      if (!__all_sync(0xffffffffu, mbar_wait(&sh->acc_full[acc], acc_phase, abort_flag,
+                                             kDevWaitTimeoutEpilogue)))
+        break;
       tc_fence_after();
       int m0, n0;
       tile_coords(p, tile, m0, n0);

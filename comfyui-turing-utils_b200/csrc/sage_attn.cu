@@ -279,12 +279,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;  // exponent reference point
     float d = 0.0f;
     bool ok = n_kv > 0;
+    // Control flow in this loop stays warp-uniform: tcgen05.ld / st are
+    // .sync.aligned warp-collective instructions, so every decision that
+    // guards one (waits, the rescale) is taken by a warp vote.
     for (int j = 0; j < n_kv && ok; ++j) {
-      if (!mbar_wait(&bar->s_full[t], static_cast<uint32_t>(j) & 1u, abort_flag,
-                     kDevWaitTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[t], static_cast<uint32_t>(j) & 1u,
+                                             abort_flag, kDevWaitTimeoutSoftmax));
+      if (!ok) break;
       tc_fence_after();
       const int key0 = j * kBlockN;
       // Keys visible to this row in this tile: [key0, key_end).
@@ -311,30 +312,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_tile = -INFINITY;
       if (mx0 != INT32_MIN) m_tile = i2f_exact(mx0) * c0;
       if (mx1 != INT32_MIN) m_tile = fmaxf(m_tile, i2f_exact(mx1) * c1);
-      if (m_tile > m_ref + 8.0f) {
-        // New reference point; rescale O and d (O is complete up to tile j-1).
-        if (j > 0 && m_ref != -INFINITY) {
-          if (!mbar_wait(&bar->o_done[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag,
-                         kDevWaitTimeoutSoftmax)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float f = ex2(m_ref - m_tile);
-          d *= f;
+      // New reference point when the row max grew by more than 2^8.  Rows
+      // that already had one rescale O and d (O is complete up to tile j-1).
+      const bool move = m_tile > m_ref + 8.0f;
+      const bool rescale = move && j > 0 && m_ref != -INFINITY;
+      if (__any_sync(0xffffffffu, rescale)) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&bar->o_done[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag,
+                                  kDevWaitTimeoutSoftmax));
+        if (!ok) break;
+        tc_fence_after();
+        const float f = rescale ? ex2(m_ref - m_tile) : 1.0f;
+        d *= f;
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(o_tmem + c * 16, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t o[16];
+          tmem_ld16(o_tmem + c * 16, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st16(o_tmem + c * 16, o);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st16(o_tmem + c * 16, o);
         }
-        m_ref = m_tile;
+        tmem_wait_st();
       }
+      if (move) m_ref = m_tile;
       // Pass 2: p = exp2(s * c - m_ref), rowsum, pack to 16-bit into TMEM.
       const float nm = (m_ref == -INFINITY) ? 0.0f : -m_ref;
       float dsum = 0.0f;
@@ -365,8 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&bar->p_full[t]);
     }
     // Epilogue: O / d -> out (16-bit), optional base-2 LSE.
-    if (ok && mbar_wait(&bar->o_done[t], static_cast<uint32_t>(n_kv - 1) & 1u, abort_flag,
-                        kDevWaitTimeoutSoftmax)) {
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_done[t],
+                                                   static_cast<uint32_t>(n_kv - 1) & 1u,
+                                                   abort_flag, kDevWaitTimeoutSoftmax));
+    if (ok) {
       tc_fence_after();
       const float inv = d > 0.0f ? 1.0f / d : 0.0f;
       TV* orow = static_cast<TV*>(p.out) + b * p.o_sb + h * p.o_sh +

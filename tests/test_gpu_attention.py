@@ -114,3 +114,27 @@ def test_custom_op_and_no_watchdog_errors():
     from comfyui_turing_utils_kernel import _lib
 
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("late", [True, False])
+def test_lazy_rescale_path(oracle, late):
+    """Rows whose max grows by far more than 2^8 after the first tile (a key
+    aligned with every query placed in the last tile), and rows that
+    attend mostly to themselves (q = k): O and d are rescaled in TMEM."""
+    g = torch.Generator().manual_seed(9)
+    L = 700
+    q = torch.randn((1, 2, L, 128), generator=g)
+    if late:
+        k = torch.randn((1, 2, L, 128), generator=g) * 0.1
+        k[:, :, L - 5] = q.mean(dim=2) * 40.0
+    else:
+        k = q.clone()
+    v = torch.randn((1, 2, L, 128), generator=g)
+    q, k, v = (t.to(torch.bfloat16).cuda() for t in (q, k, v))
+    pre = turing_sage.prequantize_sageattn(q, k, v)
+    out = turing_sage.sageattn_from_prequantized(pre)
+    ref = oracle.dequant_attention_reference(pre.query_int8.cpu(), pre.query_scale.cpu(),
+                                             pre.key_int8.cpu(), pre.key_scale.cpu(), v.cpu(),
+                                             sm_scale=128 ** -0.5)
+    m = oracle.metrics(out.cpu().float(), ref)
+    assert m["cosine"] >= oracle.NORTH_STAR_COSINE and m["rel_l2"] <= oracle.NORTH_STAR_REL_L2, m
