@@ -13,15 +13,26 @@
 // grows by more than 2^8 over the reference point (p stays <= 256), which
 // changes no result beyond rounding.
 //
-// CTA = 2 query tiles of 128 rows (256 rows of one head), 12 warps:
-//   warp 0      TMA producer: Q (once), then K (int8) and V (16-bit) tiles of
+// CTA = 2 query tiles of 128 rows (256 rows of one head), 20 warps:
+//   warps 0-15  softmax: warp w serves query tile w / 8, key half (w / 4) % 2
+//               (keys 0-63 or 64-127 of each 128-key tile, and the matching
+//               64 O columns) and TMEM lane quadrant w % 4 (one query row per
+//               thread).  Four softmax warps per SM sub-partition keep the
+//               exp (MUFU) and integer/float pipes fed; the two query tiles
+//               run independently, so one tile's exponentials overlap the
+//               tensor work of the other.
+//   warp 16     TMA producer: Q (once), then K (int8) and V (16-bit) tiles of
 //               128 keys into a 3-stage ring (128B swizzle);
-//   warp 1      TMEM owner + MMA issuer, ping-ponging the two query tiles:
+//   warp 17     TMEM owner + MMA issuer, alternating the two query tiles:
 //               S_t = Q_t K_j^T (kind::i8, M=N=128) into TMEM, then
 //               O_t += P_t V_j (kind::f16, A = P read from TMEM, B = V
 //               MN-major from shared memory);
-//   warps 4-7   softmax of query tile 0 (thread = row = TMEM lane);
-//   warps 8-11  softmax of query tile 1.
+//   warps 18-19 idle (they complete the control warpgroup).
+// A softmax thread reads its 64 scores with one TMEM wait, takes their max
+// with 3-input integer max, combines it with the other half's through shared
+// memory and an mbarrier, and forms p with packed f32x2 arithmetic (exact
+// int->float by the 2^23 magic constant, then scale and exponent offset) and
+// one ex2 per element.  Row sums are kept per half and added in the epilogue.
 // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_t is
 // written as packed 16-bit pairs over the first 64 columns of S_t.
 // Every wait is bounded (tb_common.cuh).
@@ -35,7 +46,10 @@ constexpr int kBlockM = 128;   // rows per query tile
 constexpr int kQTiles = 2;     // query tiles per CTA
 constexpr int kBlockN = 128;   // keys per KV tile
 constexpr int kStages = 3;
-constexpr int kThreads = 384;
+constexpr int kThreads = 640;
+constexpr int kSoftmaxWarps = 16;
+constexpr int kProducerWarp = 16;
+constexpr int kMmaWarp = 17;
 
 struct AttnParams {
   int B, Hq, Hk, Lq, Lk, groups;  // groups = Hq / Hk
@@ -67,6 +81,10 @@ struct __align__(8) AttnBarriers {
   uint64_t p_full[kQTiles];
   uint64_t o_done[kQTiles];
   uint64_t drain;
+  uint64_t max_ready[kQTiles];  // both halves posted their partial row max
+  uint64_t sum_ready[kQTiles];  // both halves posted their row sums
+  float row_max[kQTiles][2][kBlockM];  // per-half partial max of each row
+  float row_sum[kQTiles][2][kBlockM];  // epilogue: per-half row sums
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -93,6 +111,29 @@ __device__ __forceinline__ float i2f_exact(int32_t v) {
   return __int_as_float(v + 0x4B400000) - 12582912.0f;
 }
 
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float f2_hi(uint64_t v) {
+  return __uint_as_float(static_cast<uint32_t>(v >> 32));
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
 template <typename TV>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (std::is_same<TV, __nv_bfloat16>::value) return pack_bf16x2(lo, hi);
@@ -100,6 +141,11 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 
 template <int D, typename TV, bool CAUSAL>
+// Launched at <= 96 registers per thread (640 threads, 61,440 registers);
+// after set-up the control warpgroup (warps 16-19) gives registers back
+// (setmaxnreg.dec to 40) and the four softmax warpgroups take them
+// (setmaxnreg.inc to 104): 128 x 40 + 512 x 104 = 58,368 <= 61,440, and per
+// SM sub-partition 4 x 32 x 104 + 32 x 40 = 14,592 <= 16,384.
 __global__ void __launch_bounds__(kThreads, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -133,14 +179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&bar->s_full[t], 1);
-      mbar_init(&bar->p_full[t], 4);
+      mbar_init(&bar->p_full[t], 8);
       mbar_init(&bar->o_done[t], 1);
+      mbar_init(&bar->max_ready[t], 8);
+      mbar_init(&bar->sum_ready[t], 8);
     }
     mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&bar->tmem_base, 512);
     tmem_relinquish();
   }
@@ -149,8 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort_flag = &bar->abort_flag;
-
-  if (warp == 0) {
+  if (warp >= kSoftmaxWarps) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
+  }
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_kv > 0) {
       tma_prefetch_desc(&tm_q);
@@ -192,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(&bar->kv_full[s], ph);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t idesc_qk = idesc_i8(kBlockM, kBlockN);
@@ -262,58 +312,75 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bar->drain);
       drain_wait(&bar->drain, 0);
     }
-  } else if (warp >= 4) {
+  } else if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------ softmax
-    const int t = (warp - 4) >> 2;        // query tile of this warpgroup
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
+    const int t = warp >> 3;              // query tile
+    const int half = (warp >> 2) & 1;     // key half of each tile / O column half
     const int quad = warp & 3;            // TMEM lane quadrant
-    const int r = quad * 32 + lane;       // row within the tile
+    const int r = quad * 32 + lane;       // row within the query tile
     const int row = q0 + t * kBlockM + r; // query row
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t s_tmem = tmem + lane_off + static_cast<uint32_t>(t * 128);
-    const uint32_t o_tmem = tmem + lane_off + 256u + static_cast<uint32_t>(t * 128);
+    const uint32_t s_tmem = tmem + lane_off + static_cast<uint32_t>(t * 128 + half * 64);
+    const uint32_t p_tmem = tmem + lane_off + static_cast<uint32_t>(t * 128 + half * 32);
+    const uint32_t o_tmem = tmem + lane_off + 256u + static_cast<uint32_t>(t * 128 + half * 64);
     const int bh = b * p.Hq + h;
-    const float qs = row < p.Lq ? __ldg(p.q_scale + static_cast<int64_t>(bh) * p.q_tiles_scale + row / 16)
-                                : 0.0f;
     const float* ks_row = p.k_scale + static_cast<int64_t>(b * p.Hk + hk) * p.k_tiles_scale;
+    const float qs = row < p.Lq
+        ? __ldg(p.q_scale + static_cast<int64_t>(bh) * p.q_tiles_scale + row / 16) : 0.0f;
     const float cq = p.sm_scale_log2 * qs;
     float m_ref = -INFINITY;  // exponent reference point
-    float d = 0.0f;
+    float dsum = 0.0f;        // this half's row sum
     bool ok = n_kv > 0;
-    // Control flow in this loop stays warp-uniform: tcgen05.ld / st are
-    // .sync.aligned warp-collective instructions, so every decision that
-    // guards one (waits, the rescale) is taken by a warp vote.
+    // Control flow stays warp-uniform: tcgen05.ld / st are .sync.aligned
+    // warp-collective instructions, so every decision that guards one is
+    // taken by a warp vote.
     for (int j = 0; j < n_kv && ok; ++j) {
+      const int key0 = j * kBlockN + half * 64;
+      const float c = key0 < p.Lk ? cq * __ldg(ks_row + 2 * j + half) : 0.0f;
       ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[t], static_cast<uint32_t>(j) & 1u,
                                              abort_flag, kDevWaitTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      const int key0 = j * kBlockN;
-      // Keys visible to this row in this tile: [key0, key_end).
-      int key_end = min(p.Lk, key0 + kBlockN);
+      // Keys of this half visible to this row: [key0, key_end).
+      int key_end = min(p.Lk, key0 + 64);
       if (CAUSAL) key_end = min(key_end, row + 1);
       const int valid = key_end - key0;  // may be <= 0 (fully masked)
-      const float c0 = cq * __ldg(ks_row + 2 * j);
-      const float c1 = (key0 + 64 < p.Lk) ? cq * __ldg(ks_row + 2 * j + 1) : 0.0f;
-      // Pass 1: integer row max per 64-key half.
-      int mx0 = INT32_MIN, mx1 = INT32_MIN;
+      uint32_t v[64];
+      tmem_ld32(s_tmem + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+      tmem_wait_ld();
+      const bool full = valid >= 64;
+      if (!full) {
+        // Ragged last tile or causal diagonal: masked keys never win the max
+        // and get p = 0 below.
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_tmem + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c * 32 + i;
-          const int s = col < valid ? static_cast<int>(v[i]) : INT32_MIN;
-          if (c < 2) mx0 = max(mx0, s);
-          else mx1 = max(mx1, s);
-        }
+        for (int i = 0; i < 64; ++i)
+          if (i >= valid) v[i] = static_cast<uint32_t>(INT32_MIN);
       }
-      float m_tile = -INFINITY;
-      if (mx0 != INT32_MIN) m_tile = i2f_exact(mx0) * c0;
-      if (mx1 != INT32_MIN) m_tile = fmaxf(m_tile, i2f_exact(mx1) * c1);
-      // New reference point when the row max grew by more than 2^8.  Rows
-      // that already had one rescale O and d (O is complete up to tile j-1).
+      int mx;
+      {
+        int a[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          int m = static_cast<int>(v[16 * q]);
+#pragma unroll
+          for (int i = 1; i < 15; i += 2)
+            m = __vimax3_s32(m, static_cast<int>(v[16 * q + i]), static_cast<int>(v[16 * q + i + 1]));
+          a[q] = max(m, static_cast<int>(v[16 * q + 15]));
+        }
+        mx = max(__vimax3_s32(a[0], a[1], a[2]), a[3]);
+      }
+      // Row max over both halves: partial maxima meet in shared memory.
+      bar->row_max[t][half][r] = mx != INT32_MIN ? i2f_exact(mx) * c : -INFINITY;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar->max_ready[t]);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar->max_ready[t], static_cast<uint32_t>(j) & 1u,
+                                             abort_flag, kDevWaitTimeoutSoftmax));
+      if (!ok) break;
+      const float m_tile = fmaxf(bar->row_max[t][0][r], bar->row_max[t][1][r]);
+      // New reference point when the row max grew by more than 2^8; rows that
+      // already had one rescale O and d (O is complete up to tile j-1).
       const bool move = m_tile > m_ref + 8.0f;
       const bool rescale = move && j > 0 && m_ref != -INFINITY;
       if (__any_sync(0xffffffffu, rescale)) {
@@ -323,61 +390,67 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const float f = rescale ? ex2(m_ref - m_tile) : 1.0f;
-        d *= f;
+        dsum *= f;
 #pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
+        for (int cc = 0; cc < D / 32; ++cc) {
           uint32_t o[16];
-          tmem_ld16(o_tmem + c * 16, o);
+          tmem_ld16(o_tmem + cc * 16, o);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st16(o_tmem + c * 16, o);
+          tmem_st16(o_tmem + cc * 16, o);
         }
         tmem_wait_st();
       }
       if (move) m_ref = m_tile;
-      // Pass 2: p = exp2(s * c - m_ref), rowsum, pack to 16-bit into TMEM.
+      // p = exp2(s * c - m_ref) on packed pairs; partial row sum; 16-bit P
+      // packed in place over the consumed scores, then into TMEM (this
+      // half's 32 packed columns of the first 64 of S_t).
       const float nm = (m_ref == -INFINITY) ? 0.0f : -m_ref;
-      float dsum = 0.0f;
+      const uint64_t magic2 = f2_pack(12582912.0f, 12582912.0f);
+      const uint64_t cx2 = f2_pack(c, c), nmx2 = f2_pack(nm, nm);
+      uint64_t sum2[2] = {0ull, 0ull};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_tmem + c * 32, v);
-        tmem_wait_ld();
-        const float cc = c < 2 ? c0 : c1;
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int col = c * 32 + i;
-          float p0 = ex2(fmaf(i2f_exact(static_cast<int>(v[i])), cc, nm));
-          float p1 = ex2(fmaf(i2f_exact(static_cast<int>(v[i + 1])), cc, nm));
-          p0 = col < valid ? p0 : 0.0f;
-          p1 = col + 1 < valid ? p1 : 0.0f;
-          dsum += p0 + p1;
-          pk[i >> 1] = pack2<TV>(p0, p1);
+      for (int i = 0; i < 64; i += 2) {
+        const uint64_t t2 = f2_pack(__int_as_float(static_cast<int>(v[i]) + 0x4B400000),
+                                    __int_as_float(static_cast<int>(v[i + 1]) + 0x4B400000));
+        const uint64_t x2 = f2_fma(f2_sub(t2, magic2), cx2, nmx2);
+        float p0 = ex2(f2_lo(x2)), p1 = ex2(f2_hi(x2));
+        if (!full) {
+          p0 = i < valid ? p0 : 0.0f;
+          p1 = i + 1 < valid ? p1 : 0.0f;
         }
-        // P columns [c*16, c*16+16) of this row (packed pairs).
-        tmem_st16(s_tmem + c * 16, pk);
+        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));
+        v[i >> 1] = pack2<TV>(p0, p1);
       }
+      tmem_st32(p_tmem, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      const uint64_t s01 = f2_add(sum2[0], sum2[1]);
+      dsum += f2_lo(s01) + f2_hi(s01);
       tmem_wait_st();
-      d += dsum;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar->p_full[t]);
     }
-    // Epilogue: O / d -> out (16-bit), optional base-2 LSE.
+    // Epilogue: O / d -> out (16-bit), optional base-2 LSE.  Each half owns
+    // 64 O columns; the row sum is the sum of the two halves' partial sums.
+    bar->row_sum[t][half][r] = dsum;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar->sum_ready[t]);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->sum_ready[t], 0, abort_flag,
+                                                   kDevWaitTimeoutSoftmax));
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_done[t],
                                                    static_cast<uint32_t>(n_kv - 1) & 1u,
                                                    abort_flag, kDevWaitTimeoutSoftmax));
     if (ok) {
       tc_fence_after();
+      const float d = bar->row_sum[t][0][r] + bar->row_sum[t][1][r];
       const float inv = d > 0.0f ? 1.0f / d : 0.0f;
       TV* orow = static_cast<TV*>(p.out) + b * p.o_sb + h * p.o_sh +
-                 static_cast<int64_t>(row) * p.o_sl;
+                 static_cast<int64_t>(row) * p.o_sl + half * 64;
 #pragma unroll 1
-      for (int c = 0; c < D / 16; ++c) {
+      for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t o[16];
-        tmem_ld16(o_tmem + c * 16, o);
+        tmem_ld16(o_tmem + cc * 16, o);
         tmem_wait_ld();
         if (row < p.Lq) {
           uint4 w0 = make_uint4(pack2<TV>(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv),
@@ -388,11 +461,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 pack2<TV>(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv),
                                 pack2<TV>(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv),
                                 pack2<TV>(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv));
-          *reinterpret_cast<uint4*>(orow + c * 16) = w0;
-          *reinterpret_cast<uint4*>(orow + c * 16 + 8) = w1;
+          *reinterpret_cast<uint4*>(orow + cc * 16) = w0;
+          *reinterpret_cast<uint4*>(orow + cc * 16 + 8) = w1;
         }
       }
-      if (p.lse != nullptr && row < p.Lq) {
+      if (p.lse != nullptr && row < p.Lq && half == 0) {
         float l2;
         asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l2) : "f"(d));
         p.lse[static_cast<int64_t>(bh) * p.Lq + row] = m_ref + l2;
@@ -402,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
