@@ -22,6 +22,24 @@ def available() -> bool:
     return True
 
 
+def _not_built() -> bool:
+    return False
+
+
+# The plugin probes these before choosing a backend (turing_sage/__init__.py:25-145 of the
+# reference).  The sparse (Sol/SLA), W8A8-PV, varlen, fused Q/K preprocessing and VAE overlap
+# kernels are not part of this package, so each probe answers False and the plugin keeps the
+# plain Sage INT8 backend.
+sparse_available = _not_built
+sla_available = _not_built
+w8a8_available = _not_built
+w8a8_varlen_available = _not_built
+split_prequantization_available = _not_built
+fused_qk_preprocessing_available = _not_built
+overlap_blend_available = _not_built
+overlap_accumulate_available = _not_built
+
+
 def sageattn(*args, **kwargs):
     """Run the Sage INT8 attention (HND or NHD)."""
     from .core import sageattn as _impl
@@ -53,6 +71,8 @@ def sageattn_from_prequantized(*args, **kwargs):
 
 from . import custom_ops  # noqa: E402,F401  (registers turing_utils::sage_attention)
 
-__all__ = ["available", "per_warp_int8", "prequantize_sageattn", "quantize_key_per_block",
+__all__ = ["available", "fused_qk_preprocessing_available", "overlap_accumulate_available",
+           "overlap_blend_available", "per_warp_int8", "prequantize_sageattn", "quantize_key_per_block",
            "quantize_query_per_warp", "sageattn", "sageattn_compiled",
-           "sageattn_from_prequantized"]
+           "sageattn_from_prequantized", "sla_available", "sparse_available",
+           "split_prequantization_available", "w8a8_available", "w8a8_varlen_available"]
