@@ -23,6 +23,8 @@
 // holds elements l + 16 j; stages S=16 and S=64 then also run in registers.
 // The rotated row is kept as bf16 in shared memory (never in HBM) until the
 // row scale is known; the quantized codes leave as 16-byte coalesced stores.
+#include <mutex>
+
 #include "tb_capi_internal.h"
 #include "tb_tu.cuh"
 
@@ -484,3 +486,76 @@ void convrot_quantize_impl(const void* input, int dtype, int64_t rows64, int64_t
 }
 
 }  // namespace tb
+
+// ------------------------------------------------------------------------
+// Allocation-free staged quantizer.
+//
+// Some callers cannot allocate device memory at the point where they quantize:
+// a host application whose memory manager owns every VRAM byte and forbids
+// untracked allocations, code that must not stall on cudaMalloc's implicit
+// device synchronisation, or a runtime that has already handed its memory to
+// a pool.  For them the staged SwiGLU INT8 quantizer below keeps its scratch
+// (the rotated rows and the per-group absmax) in a fixed array that is part of
+// this library's device image: it is reserved on every GPU that loads the
+// library and held until the process exits.  The caller passes only inputs
+// and outputs.
+namespace tb {
+namespace {
+
+// 16 MiB of scratch: rotated values first, then the fp32 partial absmax.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[64] = {};  // device address of the array, per device
+
+// Looks up the device address of the scratch array for the current device
+// (once per device).  The array's name is only a host-side stand-in; kernels
+// must be given this address.
+void* noalloc_scratch_for_current_device() {
+  int dev = 0;
+  TB_CUDA_CHECK(cudaGetDevice(&dev));
+  TB_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range for the scratch table");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    TB_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    g_noalloc_addr[dev] = ptr;
+  }
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace
+}  // namespace tb
+
+extern "C" int tb_swiglu_int8_convrot_quantize_noalloc(const void* input, int dtype, int64_t rows,
+                                                       int64_t hidden, int8_t* output,
+                                                       float* scales, tb_stream_t stream) {
+  return tb::guarded([&] {
+    TB_REQUIRE(input != nullptr && output != nullptr && scales != nullptr,
+               "input, output and scales must be CUDA tensors");
+    TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16,
+               "input must be float16 or bfloat16");
+    TB_REQUIRE(rows > 0, "staged ConvRot requires at least one row");
+    TB_REQUIRE(hidden > 0 && hidden % 256 == 0,
+               "activated SwiGLU width must be positive and divisible by 256");
+    TB_REQUIRE(rows <= INT32_MAX && hidden <= INT32_MAX,
+               "staged ConvRot dimensions exceed the CUDA kernel range");
+    // Scratch: rotated [rows, hidden] (2 bytes each, 256-byte aligned), then
+    // partial absmax [rows, hidden / 256] fp32.
+    const uint64_t rotated_bytes =
+        (static_cast<uint64_t>(rows) * static_cast<uint64_t>(hidden) * 2 + 255) & ~uint64_t{255};
+    const uint64_t partial_bytes = static_cast<uint64_t>(rows) * static_cast<uint64_t>(hidden / 256) * 4;
+    TB_REQUIRE(rotated_bytes + partial_bytes <= tb::kNoAllocScratchBytes,
+               "problem too large for the allocation-free quantizer: rows * hidden * 2 + "
+               "rows * hidden / 64 bytes must fit in its 16 MiB scratch; split the rows or use "
+               "tb_swiglu_int8_convrot_quantize with caller-owned scratch");
+    tb::require_sm100();
+    unsigned char* scratch = static_cast<unsigned char*>(tb::noalloc_scratch_for_current_device());
+    // Nothing in the scratch has to start at zero: the first pass writes every
+    // rotated value and every partial absmax before the second pass reads them.
+    tb::convrot_quantize_impl(input, dtype, rows, hidden, /*act=*/1, /*int4=*/0, /*staged=*/1,
+                              scratch, reinterpret_cast<float*>(scratch + rotated_bytes), output,
+                              scales, static_cast<cudaStream_t>(stream));
+  });
+}

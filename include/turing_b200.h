@@ -102,6 +102,23 @@ TB_API int tb_gelu_int4_convrot_quantize(const void *input, int dtype, int64_t r
                                   void *rotated, float *partial_absmax, int8_t *output,
                                   float *scales, tb_stream_t stream);
 
+/* Allocation-free SwiGLU INT8 ConvRot quantizer (staged two-pass form) for
+ * callers that cannot allocate device memory when they quantize -- e.g. a host
+ * whose memory manager owns all VRAM and forbids untracked allocations, or a
+ * path that must not take cudaMalloc's implicit device synchronisation.
+ * Same arguments and results as tb_swiglu_int8_convrot_quantize minus the two
+ * scratch buffers: the scratch is a fixed 16 MiB array inside the library's
+ * device image, reserved on every GPU that loads the library until the process
+ * exits.  Limit: rows * hidden * 2 (rounded up to 256) + rows * hidden / 64
+ * bytes <= 16 MiB; larger problems are rejected with TB_ERR_INVALID.  The first
+ * call on each device looks up the array's device address; make that first
+ * call before any stream capture.  All calls share the one array, so calls
+ * that overlap on the GPU (different streams without ordering) race on it.
+ * No counterpart in the reference. */
+TB_API int tb_swiglu_int8_convrot_quantize_noalloc(const void *input, int dtype, int64_t rows,
+                                                   int64_t hidden, int8_t *output, float *scales,
+                                                   tb_stream_t stream);
+
 /* --------------------------------------------------- GEMM + epilogue ---- */
 
 /* W8A8 linear: out[m, n] = bf16(((float)sum_k act[m,k] w[n,k] * a_s[m]) * w_s[n]
