@@ -13,28 +13,30 @@
 // grows by more than 2^8 over the reference point (p stays <= 256), which
 // changes no result beyond rounding.
 //
-// CTA = 2 query tiles of 128 rows (256 rows of one head), 20 warps:
-//   warps 0-15  softmax: warp w serves query tile w / 8, key half (w / 4) % 2
-//               (keys 0-63 or 64-127 of each 128-key tile, and the matching
-//               64 O columns) and TMEM lane quadrant w % 4 (one query row per
-//               thread).  Four softmax warps per SM sub-partition keep the
-//               exp (MUFU) and integer/float pipes fed; the two query tiles
-//               run independently, so one tile's exponentials overlap the
-//               tensor work of the other.
-//   warp 16     TMA producer: Q (once), then K (int8) and V (16-bit) tiles of
-//               128 keys into a 3-stage ring (128B swizzle);
-//   warp 17     TMEM owner + MMA issuer, alternating the two query tiles:
-//               S_t = Q_t K_j^T (kind::i8, M=N=128) into TMEM, then
+// CTA = 2 query tiles of 128 rows (256 rows of one head), keys in blocks of
+// 64 (one k_scale block), 12 warps:
+//   warps 0-7   softmax: warp w serves query tile w / 4 and TMEM lane
+//               quadrant w % 4, one query row per thread;
+//   warp 8      TMA producer: Q (once), then K (int8) and V (16-bit) blocks
+//               of 64 keys into a 6-stage ring (128B swizzle);
+//   warps 9-10  MMA issuers, one per query tile (warp 9 also owns TMEM):
+//               S_t = Q_t K_j^T (kind::i8, M=128, N=64) and
 //               O_t += P_t V_j (kind::f16, A = P read from TMEM, B = V
 //               MN-major from shared memory);
-//   warps 18-19 idle (they complete the control warpgroup).
-// A softmax thread reads its 64 scores with one TMEM wait, takes their max
-// with 3-input integer max, combines it with the other half's through shared
-// memory and an mbarrier, and forms p with packed f32x2 arithmetic (exact
-// int->float by the 2^23 magic constant, then scale and exponent offset) and
-// one ex2 per element.  Row sums are kept per half and added in the epilogue.
-// TMEM columns: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512); P_t is
-// written as packed 16-bit pairs over the first 64 columns of S_t.
+//   warp 11     idle (it completes the control warpgroup).
+// Each query tile has two S buffers: while the softmax turns S_t(j) into P,
+// the tensor core already computes S_t(j+1), so the softmax warps of both
+// tiles run back to back and never wait on the tensor core.  An issuing
+// thread's barrier wait drains the tensor pipe (it is ordered after the
+// shared-memory operand reads of the MMAs before it), so each tile has its
+// own issuer and one issuer's waits overlap the other's MMAs.
+// For a full block with an established reference point the softmax takes
+// the exponentials first and the row max in the same pass (the reference
+// rarely moves); a block whose max does move is read again from TMEM and
+// redone after the rescale.
+// TMEM columns: O0 [0,128) O1 [128,256) and S(t, b) at 256 + 128 t + 64 b;
+// P_t(j) is written as packed 16-bit pairs over the first 32 columns of its
+// S buffer.
 // Every wait is bounded (tb_common.cuh).
 #include "tb_capi_internal.h"
 #include "tb_tu.cuh"
@@ -44,12 +46,19 @@ namespace {
 
 constexpr int kBlockM = 128;   // rows per query tile
 constexpr int kQTiles = 2;     // query tiles per CTA
-constexpr int kBlockN = 128;   // keys per KV tile
-constexpr int kStages = 3;
-constexpr int kThreads = 640;
-constexpr int kSoftmaxWarps = 16;
-constexpr int kProducerWarp = 16;
-constexpr int kMmaWarp = 17;
+constexpr int kBlockN = 64;    // keys per KV block (= one k_scale block)
+constexpr int kStages = 6;
+constexpr int kThreads = 384;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;    // warps 9 and 10: MMA issuers of tiles 0 and 1
+constexpr uint32_t kOCols = 128;
+constexpr uint32_t kSBase = 256;
+// Pairs (bit i: pair i mod 16 of a block) whose exp2 runs on the FMA pipe.
+#ifndef TB_ATTN_POLY_MASK
+#define TB_ATTN_POLY_MASK 0x0000u
+#endif
+constexpr uint32_t kPolyPairMask = TB_ATTN_POLY_MASK;
 
 struct AttnParams {
   int B, Hq, Hk, Lq, Lk, groups;  // groups = Hq / Hk
@@ -76,15 +85,12 @@ struct AttnSmem {
 struct __align__(8) AttnBarriers {
   uint64_t q_full;
   uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full[kQTiles];
-  uint64_t p_full[kQTiles];
-  uint64_t o_done[kQTiles];
-  uint64_t drain;
-  uint64_t max_ready[kQTiles];  // both halves posted their partial row max
-  uint64_t sum_ready[kQTiles];  // both halves posted their row sums
-  float row_max[kQTiles][2][kBlockM];  // per-half partial max of each row
-  float row_sum[kQTiles][2][kBlockM];  // epilogue: per-half row sums
+  uint64_t kv_empty[kStages];          // one commit per issuer
+  uint64_t s_full[kQTiles][2];         // S buffer b of tile t computed
+  uint64_t p_full[kQTiles][2];         // the tile's 4 softmax warps stored P in buffer b
+  uint64_t o_done[kQTiles];            // after each of the tile's last two PVs
+  uint64_t o_final[kQTiles];           // after the tile's last PV
+  uint64_t drain[kQTiles];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -134,18 +140,134 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
   return r;
 }
 
+// The helpers below keep each key pair in one 64-bit register pair built
+// inside a single asm block (mov.b64 {lo, hi}), so the packed f32x2
+// arithmetic needs no moves to assemble its operands.
+
+// Float bits of 1.5 * 2^23 + s for a pair of int32 scores (exact for
+// |s| < 2^22).
+__device__ __forceinline__ uint64_t magic_pair(uint32_t s0, uint32_t s1) {
+  uint64_t r;
+  asm("{\n\t.reg .b32 a, b;\n\t"
+      "add.s32 a, %1, 0x4B400000;\n\t"
+      "add.s32 b, %2, 0x4B400000;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(r)
+      : "r"(s0), "r"(s1));
+  return r;
+}
+
+// 2^x of both halves on the MUFU unit.
+__device__ __forceinline__ uint64_t ex2_pair(uint64_t x2) {
+  uint64_t r;
+  asm("{\n\t.reg .f32 a, b;\n\t"
+      "mov.b64 {a, b}, %1;\n\t"
+      "ex2.approx.ftz.f32 a, a;\n\t"
+      "ex2.approx.ftz.f32 b, b;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(r)
+      : "l"(x2));
+  return r;
+}
+
+// 2^x of both halves on the FMA pipe.  x = n + f with n = rint(x) (the
+// 1.5 * 2^23 rounding constant leaves n in the low mantissa bits of r) and f
+// in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients are a
+// minimax fit of the relative error on [-0.5, 0.5] (Remez exchange; max
+// relative error 7.5e-5, far below the 2^-9 rounding of the 16-bit P); 2^n is
+// added to the exponent field: bits(r) << 23 == n << 23 (mod 2^32).  x is
+// clamped at -120 first (2^-120 is 0 for every later use) so the exponent
+// stays in range; x < 128 holds because scores never exceed the reference by
+// 2^8.
+__device__ __forceinline__ uint64_t exp2_poly_pair(uint64_t x2) {
+  asm("{\n\t.reg .f32 a, b;\n\t"
+      "mov.b64 {a, b}, %0;\n\t"
+      "max.f32 a, a, 0fC2F00000;\n\t"
+      "max.f32 b, b, 0fC2F00000;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "+l"(x2));
+  const uint64_t rnd = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t r2 = f2_add(x2, rnd);
+  const uint64_t fr = f2_sub(x2, f2_sub(r2, rnd));
+  uint64_t q = f2_fma(fr, f2_pack(0.0551716685295105f, 0.0551716685295105f),
+                      f2_pack(0.2426111251115799f, 0.2426111251115799f));
+  q = f2_fma(q, fr, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  q = f2_fma(q, fr, f2_pack(0.9999280571937561f, 0.9999280571937561f));
+  uint64_t out;
+  asm("{\n\t.reg .b32 q0, q1, r0, r1;\n\t"
+      "mov.b64 {q0, q1}, %1;\n\t"
+      "mov.b64 {r0, r1}, %2;\n\t"
+      "shl.b32 r0, r0, 23;\n\t"
+      "shl.b32 r1, r1, 23;\n\t"
+      "add.s32 q0, q0, r0;\n\t"
+      "add.s32 q1, q1, r1;\n\t"
+      "mov.b64 %0, {q0, q1};\n\t}"
+      : "=l"(out)
+      : "l"(q), "l"(r2));
+  return out;
+}
+
 template <typename TV>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (std::is_same<TV, __nv_bfloat16>::value) return pack_bf16x2(lo, hi);
   else return pack_f16x2(lo, hi);
 }
 
+// Both halves of a pair rounded to TV and packed (low half = even key).
+template <typename TV>
+__device__ __forceinline__ uint32_t pack_pair(uint64_t p2) {
+  uint32_t r;
+  if constexpr (std::is_same<TV, __nv_bfloat16>::value) {
+    asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.bf16x2.f32 %0, b, a;\n\t}"
+        : "=r"(r)
+        : "l"(p2));
+  } else {
+    asm("{\n\t.reg .f32 a, b;\n\tmov.b64 {a, b}, %1;\n\tcvt.rn.f16x2.f32 %0, b, a;\n\t}"
+        : "=r"(r)
+        : "l"(p2));
+  }
+  return r;
+}
+
+// The fast path of a full block: p = exp2(s * c - m_ref) against the current
+// reference, in place as exp_block, with the integer row max of the raw
+// scores accumulated in the same loop (the ALU work of the max hides under
+// the exponentials).  Returns that max.
+template <typename TV>
+__device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
+                                             uint64_t (&sum2)[2]) {
+  int m[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
+#pragma unroll
+  for (int i = 0; i < kBlockN / 2; ++i) {
+    m[i & 3] = __vimax3_s32(m[i & 3], static_cast<int>(v[2 * i]), static_cast<int>(v[2 * i + 1]));
+    const uint64_t x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
+    const uint64_t p2 = ((kPolyPairMask >> (i & 15)) & 1u) ? exp2_poly_pair(x2) : ex2_pair(x2);
+    sum2[i & 1] = f2_add(sum2[i & 1], p2);
+    v[i] = pack_pair<TV>(p2);
+  }
+  return max(max(m[0], m[1]), max(m[2], m[3]));
+}
+
+// p = exp2(s * c - m_ref) for the 64 scores of a block, in place: packed pair
+// i (16-bit P) overwrites v[i], whose score was consumed by pair i / 2.  The
+// row sum of p accumulates in sum2.  MASKED zeroes keys >= valid; it is
+// instantiated separately so full blocks carry no per-key selects.
+template <typename TV, bool MASKED>
+__device__ __forceinline__ void exp_block(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
+                                          int valid, uint64_t (&sum2)[2]) {
+#pragma unroll
+  for (int i = 0; i < kBlockN / 2; ++i) {
+    const uint64_t x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
+    uint64_t p2 = ((kPolyPairMask >> (i & 15)) & 1u) ? exp2_poly_pair(x2) : ex2_pair(x2);
+    if constexpr (MASKED) {
+      p2 = f2_pack(2 * i < valid ? f2_lo(p2) : 0.0f, 2 * i + 1 < valid ? f2_hi(p2) : 0.0f);
+    }
+    sum2[i & 1] = f2_add(sum2[i & 1], p2);
+    v[i] = pack_pair<TV>(p2);
+  }
+}
+
 template <int D, typename TV, bool CAUSAL>
-// Launched at <= 96 registers per thread (640 threads, 61,440 registers);
-// after set-up the control warpgroup (warps 16-19) gives registers back
-// (setmaxnreg.dec to 40) and the four softmax warpgroups take them
-// (setmaxnreg.inc to 104): 128 x 40 + 512 x 104 = 58,368 <= 61,440, and per
-// SM sub-partition 4 x 32 x 104 + 32 x 40 = 14,592 <= 16,384.
 __global__ void __launch_bounds__(kThreads, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -166,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hk = h / p.groups;
   const int q0 = qblk * kBlockM * kQTiles;
 
-  // KV tiles this CTA visits (causal: up to the last row of the block).
+  // KV blocks this CTA visits (causal: up to the last row of the block).
   int kv_len = p.Lk;
   if (CAUSAL) kv_len = min(p.Lk, q0 + kBlockM * kQTiles);
   const int n_kv = (kv_len + kBlockN - 1) / kBlockN;
@@ -175,16 +297,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bar->q_full, 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bar->kv_full[s], 1);
-      mbar_init(&bar->kv_empty[s], 1);
+      mbar_init(&bar->kv_empty[s], kQTiles);
     }
     for (int t = 0; t < kQTiles; ++t) {
-      mbar_init(&bar->s_full[t], 1);
-      mbar_init(&bar->p_full[t], 8);
+      for (int bb = 0; bb < 2; ++bb) {
+        mbar_init(&bar->s_full[t][bb], 1);
+        mbar_init(&bar->p_full[t][bb], 4);
+      }
       mbar_init(&bar->o_done[t], 1);
-      mbar_init(&bar->max_ready[t], 8);
-      mbar_init(&bar->sum_ready[t], 8);
+      mbar_init(&bar->o_final[t], 1);
+      mbar_init(&bar->drain[t], 1);
     }
-    mbar_init(&bar->drain, 1);
     bar->abort_flag = 0;
     fence_barrier_init();
   }
@@ -197,9 +320,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_base;
   volatile int* abort_flag = &bar->abort_flag;
-  if (warp >= kSoftmaxWarps) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 40;\n" ::: "memory");
-  }
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_kv > 0) {
@@ -242,213 +362,216 @@ __global__ void __launch_bounds__(kThreads, 1)
         drain_wait(&bar->kv_full[s], ph);
       }
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+    // ------------------------------------------------------------ MMA issuers
+    const int t = warp - kMmaWarp;  // query tile this thread serves
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t idesc_qk = idesc_i8(kBlockM, kBlockN);
       constexpr uint32_t idesc_pv =
           idesc_f16(kBlockM, D, std::is_same<TV, __nv_bfloat16>::value, /*b_mn_major=*/true);
-      const uint32_t q_addr = smem_u32(q_smem);
       const uint32_t kv_addr = smem_u32(kv_smem);
-      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, kDevWaitTimeoutMma);
-      // S_t(j) = Q_t K_j^T
-      auto issue_s = [&](int t, int stage) {
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>(t * 128);
-        const uint64_t a = umma_desc_sw128(q_addr + t * SM::kQBytes);
+      const uint32_t o_tmem = tmem + static_cast<uint32_t>(t) * kOCols;
+      const uint32_t s_tmem0 = tmem + kSBase + static_cast<uint32_t>(t) * 2u * kBlockN;
+      const uint64_t q_desc = umma_desc_sw128(smem_u32(q_smem) + t * SM::kQBytes);
+      // S_t(j) = Q_t K_j^T into S buffer j % 2.
+      auto issue_s = [&](int j) {
+        const int stage = j % kStages;
+        const uint32_t d_tmem = s_tmem0 + static_cast<uint32_t>(j & 1) * kBlockN;
         const uint64_t bk = umma_desc_sw128(kv_addr + stage * SM::kStageBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 32; ++kk)
-          mma_i8_ss(d_tmem, a + 2u * kk, bk + 2u * kk, idesc_qk, kk > 0 ? 1u : 0u);
-        mma_commit(&bar->s_full[t]);
+          mma_i8_ss(d_tmem, q_desc + 2u * kk, bk + 2u * kk, idesc_qk, kk > 0 ? 1u : 0u);
       };
-      // O_t += P_t V_j
-      auto issue_pv = [&](int t, int stage, int j) {
-        const uint32_t d_tmem = tmem + 256u + static_cast<uint32_t>(t * 128);
-        const uint32_t p_tmem = tmem + static_cast<uint32_t>(t * 128);
+      auto wait_kv = [&](int j) {
+        return mbar_wait(&bar->kv_full[j % kStages], static_cast<uint32_t>(j / kStages) & 1u,
+                         abort_flag, kDevWaitTimeoutMma);
+      };
+      bool ok = mbar_wait(&bar->q_full, 0, abort_flag, kDevWaitTimeoutMma);
+      for (int j = 0; j < 2 && j < n_kv && ok; ++j) {
+        ok = wait_kv(j);
+        if (ok) {
+          tc_fence_after();
+          issue_s(j);
+          mma_commit(&bar->s_full[t][j & 1]);
+        }
+      }
+      // Per block: both waits first (a barrier wait issued after an MMA would
+      // wait for that MMA's shared-memory reads), then PV(j) and QK^T(j + 2)
+      // back to back, then the commits.  The s_full commit of S_t(j + 2) also
+      // tells the softmax that PV(j) is done; o_done marks the last two PVs,
+      // which no S commit follows.
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const bool next_s = j + 2 < n_kv;
+        if (!mbar_wait(&bar->p_full[t][j & 1], static_cast<uint32_t>(j >> 1) & 1u, abort_flag,
+                       kDevWaitTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        if (next_s && !wait_kv(j + 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // O_t += P_t(j) V_j: 16 keys per MMA = two 8-row swizzle atoms of V
+        // (2 x 1024 B); the D halves are separate TMA boxes kBlockN * 128 B
+        // apart (LBO).
+        const int stage = j % kStages;
         const uint32_t v_addr = kv_addr + stage * SM::kStageBytes + SM::kKBytes;
+        const uint32_t p_tmem = s_tmem0 + static_cast<uint32_t>(j & 1) * kBlockN;
 #pragma unroll
         for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          // 16 keys per MMA = two 8-row swizzle atoms (2 x 1024 B); the D
-          // halves are separate TMA boxes kBlockN * 128 B apart (LBO).
           const uint64_t bv = umma_desc_sw128_mn(v_addr + kk * 2048, kBlockN * 128, 1024);
-          mma_f16_ts(d_tmem, p_tmem + static_cast<uint32_t>(kk * 8), bv, idesc_pv,
+          mma_f16_ts(o_tmem, p_tmem + static_cast<uint32_t>(kk * 8), bv, idesc_pv,
                      (j > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&bar->o_done[t]);
-      };
-      if (ok) ok = mbar_wait(&bar->kv_full[0], 0, abort_flag, kDevWaitTimeoutMma);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-      }
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int next_stage = stage + 1 == kStages ? 0 : stage + 1;
-        const uint32_t next_phase = next_stage == 0 ? phase ^ 1u : phase;
-        for (int t = 0; t < kQTiles; ++t) {
-          if (!mbar_wait(&bar->p_full[t], static_cast<uint32_t>(j) & 1u, abort_flag,
-                         kDevWaitTimeoutMma)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(t, stage, j);
-          if (t == kQTiles - 1) mma_commit(&bar->kv_empty[stage]);
-          if (j + 1 < n_kv) {
-            if (t == 0 && !mbar_wait(&bar->kv_full[next_stage], next_phase, abort_flag,
-                                     kDevWaitTimeoutMma)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            issue_s(t, next_stage);
-          }
+        // S buffer j % 2 is free once PV(j) has read P_t(j): S_t(j + 2).
+        if (next_s) {
+          issue_s(j + 2);
+          mma_commit(&bar->s_full[t][j & 1]);
+        } else {
+          mma_commit(&bar->o_done[t]);
         }
-        stage = next_stage;
-        phase = next_phase;
+        mma_commit(&bar->kv_empty[stage]);
+        if (j + 1 == n_kv) mma_commit(&bar->o_final[t]);
       }
-      mma_commit(&bar->drain);
-      drain_wait(&bar->drain, 0);
+      mma_commit(&bar->drain[t]);
+      drain_wait(&bar->drain[t], 0);
     }
   } else if (warp < kSoftmaxWarps) {
     // ------------------------------------------------------------ softmax
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
-    const int t = warp >> 3;              // query tile
-    const int half = (warp >> 2) & 1;     // key half of each tile / O column half
+    const int t = warp >> 2;              // query tile
     const int quad = warp & 3;            // TMEM lane quadrant
     const int r = quad * 32 + lane;       // row within the query tile
     const int row = q0 + t * kBlockM + r; // query row
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t s_tmem = tmem + lane_off + static_cast<uint32_t>(t * 128 + half * 64);
-    const uint32_t p_tmem = tmem + lane_off + static_cast<uint32_t>(t * 128 + half * 32);
-    const uint32_t o_tmem = tmem + lane_off + 256u + static_cast<uint32_t>(t * 128 + half * 64);
+    const uint32_t s_tmem0 = tmem + lane_off + kSBase + static_cast<uint32_t>(t) * 2u * kBlockN;
+    const uint32_t o_tmem = tmem + lane_off + static_cast<uint32_t>(t) * kOCols;
     const int bh = b * p.Hq + h;
     const float* ks_row = p.k_scale + static_cast<int64_t>(b * p.Hk + hk) * p.k_tiles_scale;
     const float qs = row < p.Lq
         ? __ldg(p.q_scale + static_cast<int64_t>(bh) * p.q_tiles_scale + row / 16) : 0.0f;
     const float cq = p.sm_scale_log2 * qs;
+    float ks = n_kv > 0 ? __ldg(ks_row) : 0.0f;  // k_scale of block j, loaded one ahead
     float m_ref = -INFINITY;  // exponent reference point
-    float dsum = 0.0f;        // this half's row sum
+    float dsum = 0.0f;        // row sum of p
     bool ok = n_kv > 0;
     // Control flow stays warp-uniform: tcgen05.ld / st are .sync.aligned
     // warp-collective instructions, so every decision that guards one is
     // taken by a warp vote.
     for (int j = 0; j < n_kv && ok; ++j) {
-      const int key0 = j * kBlockN + half * 64;
-      const float c = key0 < p.Lk ? cq * __ldg(ks_row + 2 * j + half) : 0.0f;
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[t], static_cast<uint32_t>(j) & 1u,
-                                             abort_flag, kDevWaitTimeoutSoftmax));
+      const float c = cq * ks;
+      if (j + 1 < n_kv) ks = __ldg(ks_row + j + 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&bar->s_full[t][j & 1],
+                                             static_cast<uint32_t>(j >> 1) & 1u, abort_flag,
+                                             kDevWaitTimeoutSoftmax));
       if (!ok) break;
       tc_fence_after();
-      // Keys of this half visible to this row: [key0, key_end).
-      int key_end = min(p.Lk, key0 + 64);
+      const uint32_t s_tmem = s_tmem0 + static_cast<uint32_t>(j & 1) * kBlockN;
+      // Keys of this block visible to this row: [key0, key_end).
+      const int key0 = j * kBlockN;
+      int key_end = min(p.Lk, key0 + kBlockN);
       if (CAUSAL) key_end = min(key_end, row + 1);
       const int valid = key_end - key0;  // may be <= 0 (fully masked)
-      uint32_t v[64];
-      tmem_ld32(s_tmem + 0, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      uint32_t v[kBlockN];
+      tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
       tmem_wait_ld();
-      const bool full = valid >= 64;
-      if (!full) {
-        // Ragged last tile or causal diagonal: masked keys never win the max
-        // and get p = 0 below.
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i >= valid) v[i] = static_cast<uint32_t>(INT32_MIN);
+      // Warp-uniform: full blocks take the paths without per-key selects.
+      const bool all_full = __all_sync(0xffffffffu, valid >= kBlockN);
+      const uint64_t cx2 = f2_pack(c, c);
+      uint64_t sum2[2] = {0ull, 0ull};
+      // x = s * c - m_ref = fma(t, c, b) with t = 1.5 * 2^23 + s (exact, by
+      // integer addition to the float bits) and b = -(1.5 * 2^23 * c) - m_ref:
+      // one packed FMA per key pair.
+      bool done = false;
+      if (all_full && __all_sync(0xffffffffu, m_ref != -INFINITY)) {
+        // Usual case: the reference point stands, so the exponentials need
+        // not wait for the row max.  If any row's max moved past it, the
+        // scores are read again and the block takes the general path.
+        const float bb = fmaf(-12582912.0f, c, -m_ref);
+        const int mx = exp_block_max<TV>(v, cx2, f2_pack(bb, bb), sum2);
+        done = !__any_sync(0xffffffffu, i2f_exact(mx) * c > m_ref + 8.0f);
+        if (!done) {
+          sum2[0] = sum2[1] = 0ull;
+          tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(v));
+          tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          tmem_wait_ld();
+        }
       }
-      int mx;
-      {
+      if (!done) {
+        if (!all_full) {
+          // Ragged last block or causal diagonal: masked keys never win the
+          // max and get p = 0 below.
+#pragma unroll
+          for (int i = 0; i < kBlockN; ++i)
+            if (i >= valid) v[i] = static_cast<uint32_t>(INT32_MIN);
+        }
+        // Row max (integer max, then one multiply).
         int a[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          int m = static_cast<int>(v[16 * q]);
+          const uint32_t* w = v + 16 * q;
+          int m = static_cast<int>(w[0]);
 #pragma unroll
           for (int i = 1; i < 15; i += 2)
-            m = __vimax3_s32(m, static_cast<int>(v[16 * q + i]), static_cast<int>(v[16 * q + i + 1]));
-          a[q] = max(m, static_cast<int>(v[16 * q + 15]));
+            m = __vimax3_s32(m, static_cast<int>(w[i]), static_cast<int>(w[i + 1]));
+          a[q] = max(m, static_cast<int>(w[15]));
         }
-        mx = max(__vimax3_s32(a[0], a[1], a[2]), a[3]);
-      }
-      // Row max over both halves: partial maxima meet in shared memory.
-      bar->row_max[t][half][r] = mx != INT32_MIN ? i2f_exact(mx) * c : -INFINITY;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->max_ready[t]);
-      ok = __all_sync(0xffffffffu, mbar_wait(&bar->max_ready[t], static_cast<uint32_t>(j) & 1u,
-                                             abort_flag, kDevWaitTimeoutSoftmax));
-      if (!ok) break;
-      const float m_tile = fmaxf(bar->row_max[t][0][r], bar->row_max[t][1][r]);
-      // New reference point when the row max grew by more than 2^8; rows that
-      // already had one rescale O and d (O is complete up to tile j-1).
-      const bool move = m_tile > m_ref + 8.0f;
-      const bool rescale = move && j > 0 && m_ref != -INFINITY;
-      if (__any_sync(0xffffffffu, rescale)) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&bar->o_done[t], static_cast<uint32_t>(j - 1) & 1u, abort_flag,
-                                  kDevWaitTimeoutSoftmax));
-        if (!ok) break;
-        tc_fence_after();
-        const float f = rescale ? ex2(m_ref - m_tile) : 1.0f;
-        dsum *= f;
+        const int mx = max(__vimax3_s32(a[0], a[1], a[2]), a[3]);
+        const float m_blk = mx != INT32_MIN ? i2f_exact(mx) * c : -INFINITY;
+        // New reference point when the row max grew by more than 2^8; rows
+        // that already had one rescale O and d once PV(j - 1) is done: the
+        // commit of S_t(j + 1), issued right after PV(j - 1), marks it, and
+        // o_done (phase 0) marks PV(n_kv - 2) when no S_t(j + 1) exists.
+        const bool move = m_blk > m_ref + 8.0f;
+        const bool rescale = move && j > 0 && m_ref != -INFINITY;
+        if (__any_sync(0xffffffffu, rescale)) {
+          const bool waited =
+              j + 1 < n_kv
+                  ? mbar_wait(&bar->s_full[t][(j + 1) & 1], static_cast<uint32_t>((j + 1) >> 1) & 1u,
+                              abort_flag, kDevWaitTimeoutSoftmax)
+                  : mbar_wait(&bar->o_done[t], 0u, abort_flag, kDevWaitTimeoutSoftmax);
+          ok = __all_sync(0xffffffffu, waited);
+          if (!ok) break;
+          tc_fence_after();
+          const float f = rescale ? ex2(m_ref - m_blk) : 1.0f;
+          dsum *= f;
 #pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t o[16];
-          tmem_ld16(o_tmem + cc * 16, o);
-          tmem_wait_ld();
+          for (int cc = 0; cc < D / 16; ++cc) {
+            uint32_t o[16];
+            tmem_ld16(o_tmem + cc * 16, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st16(o_tmem + cc * 16, o);
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st16(o_tmem + cc * 16, o);
+          }
+          tmem_wait_st();
         }
-        tmem_wait_st();
+        if (move) m_ref = m_blk;
+        const float nm = (m_ref == -INFINITY) ? 0.0f : -m_ref;
+        const float bb = fmaf(-12582912.0f, c, nm);
+        const uint64_t bx2 = f2_pack(bb, bb);
+        if (all_full) exp_block<TV, false>(v, cx2, bx2, valid, sum2);
+        else exp_block<TV, true>(v, cx2, bx2, valid, sum2);
       }
-      if (move) m_ref = m_tile;
-      // p = exp2(s * c - m_ref) on packed pairs; partial row sum; 16-bit P
-      // packed in place over the consumed scores, then into TMEM (this
-      // half's 32 packed columns of the first 64 of S_t).
-      const float nm = (m_ref == -INFINITY) ? 0.0f : -m_ref;
-      const uint64_t magic2 = f2_pack(12582912.0f, 12582912.0f);
-      const uint64_t cx2 = f2_pack(c, c), nmx2 = f2_pack(nm, nm);
-      uint64_t sum2[2] = {0ull, 0ull};
-#pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        const uint64_t t2 = f2_pack(__int_as_float(static_cast<int>(v[i]) + 0x4B400000),
-                                    __int_as_float(static_cast<int>(v[i + 1]) + 0x4B400000));
-        const uint64_t x2 = f2_fma(f2_sub(t2, magic2), cx2, nmx2);
-        float p0 = ex2(f2_lo(x2)), p1 = ex2(f2_hi(x2));
-        if (!full) {
-          p0 = i < valid ? p0 : 0.0f;
-          p1 = i + 1 < valid ? p1 : 0.0f;
-        }
-        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));
-        v[i >> 1] = pack2<TV>(p0, p1);
-      }
-      tmem_st32(p_tmem, *reinterpret_cast<uint32_t(*)[32]>(v + 0));
+      tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(v));
       const uint64_t s01 = f2_add(sum2[0], sum2[1]);
       dsum += f2_lo(s01) + f2_hi(s01);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar->p_full[t]);
+      if (lane == 0) mbar_arrive(&bar->p_full[t][j & 1]);
     }
-    // Epilogue: O / d -> out (16-bit), optional base-2 LSE.  Each half owns
-    // 64 O columns; the row sum is the sum of the two halves' partial sums.
-    bar->row_sum[t][half][r] = dsum;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&bar->sum_ready[t]);
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->sum_ready[t], 0, abort_flag,
+    // Epilogue: O / d -> out (16-bit), optional base-2 LSE.
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_final[t], 0u, abort_flag,
                                                    kDevWaitTimeoutSoftmax));
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&bar->o_done[t],
-                                                   static_cast<uint32_t>(n_kv - 1) & 1u,
-                                                   abort_flag, kDevWaitTimeoutSoftmax));
     if (ok) {
       tc_fence_after();
-      const float d = bar->row_sum[t][0][r] + bar->row_sum[t][1][r];
-      const float inv = d > 0.0f ? 1.0f / d : 0.0f;
+      const float inv = dsum > 0.0f ? 1.0f / dsum : 0.0f;
       TV* orow = static_cast<TV*>(p.out) + b * p.o_sb + h * p.o_sh +
-                 static_cast<int64_t>(row) * p.o_sl + half * 64;
+                 static_cast<int64_t>(row) * p.o_sl;
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < D / 16; ++cc) {
         uint32_t o[16];
         tmem_ld16(o_tmem + cc * 16, o);
         tmem_wait_ld();
@@ -465,9 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(orow + cc * 16 + 8) = w1;
         }
       }
-      if (p.lse != nullptr && row < p.Lq && half == 0) {
+      if (p.lse != nullptr && row < p.Lq) {
         float l2;
-        asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l2) : "f"(d));
+        asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(l2) : "f"(dsum));
         p.lse[static_cast<int64_t>(bh) * p.Lq + row] = m_ref + l2;
       }
     }

@@ -128,12 +128,37 @@ constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per probe
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
   uint32_t ok;
+#ifdef TB_TRY_WAIT_NO_HINT
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
       : "r"(bar_addr), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+#endif
+  return ok != 0;
+}
+
+// One probe that never parks the warp (test_wait): for the single-thread
+// issuers whose next instruction feeds the tensor core, where a parked warp's
+// wake-up latency would idle the pipe.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
       : "memory");
   return ok != 0;
 }
@@ -148,6 +173,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   const uint64_t t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > TB_WAIT_TIMEOUT_NS) {
+      record_device_error(code);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// As mbar_wait, but polls with test_wait (the warp is never parked).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                               int code) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_test_wait(addr, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_test_wait(addr, parity)) return true;
     if (*abort) return false;
     if (globaltimer_ns() - t0 > TB_WAIT_TIMEOUT_NS) {
       record_device_error(code);
