@@ -75,6 +75,150 @@ def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=
     return out
 
 
+def _pad_k16(activation, weight_packed):
+    """Zero-pad K to a multiple of 16 (zero codes add nothing to the sums): the
+    sm_100a GEMM reads K in 16-byte TMA rows, the reference accepts K % 4."""
+    k = activation.size(1)
+    pad = (-k) % 16
+    if pad == 0:
+        return activation, weight_packed
+    return (torch.nn.functional.pad(activation, (0, pad)),
+            torch.nn.functional.pad(weight_packed, (0, pad // 2)))
+
+
+def _n_tail_linear(m, n, dev, run):
+    """N-tail handling of bindings.cpp:205-259: the first N - N % 8 channels in
+    one call, the last N % 8 channels padded with zero rows to 8 in a second,
+    into an output of ceil(N / 8) * 8 columns that is sliced back to N."""
+    padded_n = (n + 7) // 8 * 8
+    out = torch.empty((m, padded_n), dtype=torch.bfloat16, device=dev)
+    bulk = n // 8 * 8
+    if bulk > 0:
+        run(0, bulk, bulk, out)
+    if bulk != n:
+        run(bulk, n - bulk, 8, out)
+    return out if padded_n == n else out.narrow(1, 0, n).contiguous()
+
+
+def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=None,
+                       tile_policy=0):
+    """bindings.cpp:167-259: signed-nibble W4A8, weight [N, K/2] packed int8
+    storage (low nibble = even column).  The weight rows are unpacked to int8
+    in a bounded workspace and contracted by the tcgen05 INT8 GEMM."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = _as_f32_vec(activation_scale)
+    weight_scale = _as_f32_vec(weight_scale)
+    if bias is not None:
+        bias = _as_f32_vec(bias)
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check(activation.dtype == torch.int8, "activation must be int8")
+    _check(weight.dtype == torch.int8, "weight must be packed int8 storage")
+    _check(activation.device == weight.device,
+           "activation and weight must be on the same CUDA device")
+    _check(activation_scale.is_cuda and weight_scale.is_cuda, "scales must be CUDA tensors")
+    _check(activation_scale.device == activation.device
+           and weight_scale.device == activation.device,
+           "scales must be on the activation device")
+    _check(activation.size(1) % 4 == 0, "activation K must be divisible by 4")
+    _check(weight.size(1) * 2 == activation.size(1), "packed weight K must match activation K")
+    _check(activation_scale.numel() == activation.size(0),
+           "activation_scale must contain one value per row")
+    _check(weight_scale.numel() == weight.size(0),
+           "weight_scale must contain one value per output channel")
+    if bias is not None:
+        _check(bias.is_cuda and bias.device == activation.device,
+               "bias must be on the activation device")
+        _check(bias.numel() == weight.size(0), "bias must contain one value per output channel")
+    dev = activation.device
+    m = activation.size(0)
+    n = weight.size(0)
+    with torch.cuda.device(dev):
+        _require_blackwell(dev, "turing_w4a8_linear")
+        activation, weight = _pad_k16(activation, weight)
+        k = activation.size(1)
+        if m == 0 or n == 0:
+            return torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+        def run(n0, count, width, out):
+            w = weight.narrow(0, n0, count)
+            ws = weight_scale.narrow(0, n0, count)
+            b = None if bias is None else bias.narrow(0, n0, count)
+            if width != count:
+                w = torch.nn.functional.pad(w, (0, 0, 0, width - count))
+                ws = torch.nn.functional.pad(ws, (0, width - count))
+                b = None if b is None else torch.nn.functional.pad(b, (0, width - count))
+            rows = min(width, 4096)
+            workspace = torch.empty((rows, k), dtype=torch.int8, device=dev)
+            call("tb_w4a8_linear", ptr(activation), ptr(w.contiguous()), ptr(activation_scale),
+                 ptr(ws.contiguous()), ptr(None if b is None else b.contiguous()), ptr(workspace),
+                 rows, ptr(out.narrow(1, n0, width)), m, width, k, out.size(1),
+                 int(tile_policy) if width == count else 1, stream_of(activation))
+
+        return _n_tail_linear(m, n, dev, run)
+
+
+def turing_int4_linear(activation, weight, activation_scale, weight_scale, bias=None):
+    """W4A4 linear for the plugin's INT4 ConvRot path (in place of the
+    comfy-kitchen int4_linear call, comfyui_turing_utils/quantization/
+    dispatch.py:791-804): activation [M, K/2] and weight [N, K/2] packed signed
+    4-bit codes (low nibble = even column), activation_scale [M] (absmax / 7),
+    weight_scale [N]; returns bf16 [M, N] =
+    bf16(((sum a4 * w4) * a_s) * w_s + bias)."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = _as_f32_vec(activation_scale)
+    weight_scale = _as_f32_vec(weight_scale)
+    if bias is not None:
+        bias = _as_f32_vec(bias)
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check(activation.dtype == torch.int8, "activation must be packed int8 storage")
+    _check(weight.dtype == torch.int8, "weight must be packed int8 storage")
+    dev = activation.device
+    _check(weight.device == dev and activation_scale.device == dev and weight_scale.device == dev,
+           "W4A4 tensors must be on the activation device")
+    _check(weight.size(1) == activation.size(1), "packed activation and weight K must match")
+    _check(activation.size(1) % 2 == 0, "activation K must be divisible by 4")
+    _check(activation_scale.numel() == activation.size(0),
+           "activation_scale must contain one value per row")
+    _check(weight_scale.numel() == weight.size(0),
+           "weight_scale must contain one value per output channel")
+    if bias is not None:
+        _check(bias.is_cuda and bias.device == dev, "bias must be on the activation device")
+        _check(bias.numel() == weight.size(0), "bias must contain one value per output channel")
+    m = activation.size(0)
+    n = weight.size(0)
+    with torch.cuda.device(dev):
+        _require_blackwell(dev, "turing_int4_linear")
+        pad = (-activation.size(1)) % 8
+        if pad:
+            activation = torch.nn.functional.pad(activation, (0, pad))
+            weight = torch.nn.functional.pad(weight, (0, pad))
+        k = activation.size(1) * 2
+        if m == 0 or n == 0:
+            return torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        act_workspace = torch.empty((m, k), dtype=torch.int8, device=dev)
+
+        def run(n0, count, width, out):
+            w = weight.narrow(0, n0, count)
+            ws = weight_scale.narrow(0, n0, count)
+            b = None if bias is None else bias.narrow(0, n0, count)
+            if width != count:
+                w = torch.nn.functional.pad(w, (0, 0, 0, width - count))
+                ws = torch.nn.functional.pad(ws, (0, width - count))
+                b = None if b is None else torch.nn.functional.pad(b, (0, width - count))
+            rows = min(width, 4096)
+            workspace = torch.empty((rows, k), dtype=torch.int8, device=dev)
+            call("tb_int4_linear", ptr(activation), ptr(w.contiguous()), ptr(activation_scale),
+                 ptr(ws.contiguous()), ptr(None if b is None else b.contiguous()),
+                 ptr(act_workspace), ptr(workspace), rows, ptr(out.narrow(1, n0, width)), m,
+                 width, k, out.size(1), stream_of(activation))
+
+        return _n_tail_linear(m, n, dev, run)
+
+
 def turing_int8_gemm_s32(activation, weight):
     """Exact INT32 accumulators [M, N] (the INT32 GEMM the plugin pairs with
     turing_dequantize_int8_bf16, dispatch.py:481-535)."""

@@ -14,10 +14,12 @@ from .ops import (
     turing_dequantize_int8_bf16,
     turing_gelu_int4_convrot_quantize,
     turing_gelu_int8_convrot_quantize,
+    turing_int4_linear,
     turing_int8_gemm_s32,
     turing_int8_linear,
     turing_swiglu_int4_convrot_quantize,
     turing_swiglu_int8_convrot_quantize,
+    turing_w4a8_linear,
 )
 from . import turing_sage
 
@@ -32,9 +34,11 @@ __all__ = [
     "turing_dequantize_int8_bf16",
     "turing_gelu_int8_convrot_quantize",
     "turing_gelu_int4_convrot_quantize",
+    "turing_int4_linear",
     "turing_int8_gemm_s32",
     "turing_int8_linear",
     "turing_swiglu_int8_convrot_quantize",
     "turing_swiglu_int4_convrot_quantize",
+    "turing_w4a8_linear",
     "turing_sage",
 ]

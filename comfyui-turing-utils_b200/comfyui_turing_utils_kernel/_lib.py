@@ -44,6 +44,8 @@ SIGNATURES: dict[str, list] = {
     "tb_gelu_int4_convrot_quantize": [_p, _int, _i64, _i64, _p, _p, _p, _p, _p],
     "tb_swiglu_int8_convrot_quantize_noalloc": [_p, _int, _i64, _i64, _p, _p, _p],
     "tb_int8_linear": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p],
+    "tb_w4a8_linear": [_p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _int, _p],
+    "tb_int4_linear": [_p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p],
     "tb_codebook_w4a8_linear": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64,
                                 _int, _int, _p],
     "tb_int8_gemm_s32": [_p, _p, _p, _i64, _i64, _i64, _i64, _p],

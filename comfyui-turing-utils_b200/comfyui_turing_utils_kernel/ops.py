@@ -20,6 +20,50 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what} requires an sm_100 (B200) device for this build")
 
 
+@torch.library.custom_op("turing_utils::w4a8_linear", mutates_args=())
+def turing_w4a8_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Signed-nibble W4A8 linear (ops.py:8-26)."""
+    _require_cuda(activation, "Turing W4A8")
+    return _C.turing_w4a8_linear(
+        activation.contiguous(), weight.contiguous(), activation_scale.contiguous(),
+        weight_scale.contiguous(), None if bias is None else bias.contiguous())
+
+
+@turing_w4a8_linear.register_fake
+def _w4a8_fake(activation, weight, activation_scale, weight_scale, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16,
+                       device=activation.device)
+
+
+@torch.library.custom_op("turing_utils::int4_linear", mutates_args=())
+def turing_int4_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """W4A4 linear on packed INT4 ConvRot activations (no counterpart in the
+    reference package: the plugin calls comfy-kitchen's int4_linear there,
+    comfyui_turing_utils/quantization/dispatch.py:791-804)."""
+    _require_cuda(activation, "Turing W4A4")
+    return _C.turing_int4_linear(
+        activation.contiguous(), weight.contiguous(), activation_scale.contiguous(),
+        weight_scale.contiguous(), None if bias is None else bias.contiguous())
+
+
+@turing_int4_linear.register_fake
+def _int4_fake(activation, weight, activation_scale, weight_scale, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16,
+                       device=activation.device)
+
+
 @torch.library.custom_op("turing_utils::codebook_w4a8_linear", mutates_args=())
 def turing_codebook_w4a8_linear(
     activation: torch.Tensor,

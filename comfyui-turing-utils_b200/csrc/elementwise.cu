@@ -2,8 +2,10 @@
 //   * INT32 -> BF16 dequant epilogue (kernel/csrc/turing/bf16_epilogue.cu:46-143):
 //       out = bf16_rn((acc * a_s[row]) * w_s[col]), w_s scalar or per column;
 //   * grouped-codebook W4 -> INT8 decode (kernel/csrc/turing/w4a8.cu:907-973):
-//       w8 = clamp(rint(codebook[idx] * e4m3(group_scale)), -127, 127).
-// Both move 16-byte vectors per thread with grid-stride loops sized to the SM
+//       w8 = clamp(rint(codebook[idx] * e4m3(group_scale)), -127, 127);
+//   * signed 4-bit -> INT8 unpack for the W4A8 and W4A4 linears
+//     (w4a8.cu:34-72): low nibble = even column, two's-complement nibbles.
+// All move 16-byte vectors per thread with grid-stride loops sized to the SM
 // count.
 #include <cuda_fp8.h>
 
@@ -110,6 +112,33 @@ __global__ void __launch_bounds__(256) codebook_decode_kernel(
   }
 }
 
+// Eight packed nibbles (one 32-bit word, columns 0..7) -> eight int8 values.
+// Per byte, (b ^ 8) - 8 sign-extends a nibble b in [0, 15]; __vsub4 keeps the
+// four byte lanes independent.  Two byte permutes interleave the even-column
+// and odd-column bytes: lo = e0 o0 e1 o1, hi = e2 o2 e3 o3.
+__device__ __forceinline__ void unpack_s4_word(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t even = __vsub4((w & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+  const uint32_t odd = __vsub4(((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+  lo = __byte_perm(even, odd, 0x5140);
+  hi = __byte_perm(even, odd, 0x7362);
+}
+
+// packed holds n_vec 8-byte vectors (16 nibbles each); out receives 16 int8
+// per vector.  Rows need no special handling: a row-major [rows, k/2] packed
+// matrix maps nibble-for-nibble onto the row-major [rows, k] output.
+__global__ void __launch_bounds__(256) unpack_s4_kernel(const uint2* __restrict__ packed,
+                                                        uint4* __restrict__ out, int64_t n_vec) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n_vec;
+       i += stride) {
+    const uint2 w = __ldg(packed + i);
+    uint4 r;
+    unpack_s4_word(w.x, r.x, r.y);
+    unpack_s4_word(w.y, r.z, r.w);
+    out[i] = r;
+  }
+}
+
 int grid_for(int64_t work_items, int threads) {
   int64_t blocks = (work_items + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
@@ -152,6 +181,19 @@ void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
   const int grid = grid_for(static_cast<int64_t>(rows) * (k / 16), 256);
   codebook_decode_kernel<<<grid, 256, 0, stream>>>(packed, group_scale, codebook, out, rows, k,
                                                    group_size);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+void unpack_s4_launch(const int8_t* packed, int8_t* out, int64_t rows, int64_t k,
+                      cudaStream_t stream) {
+  TB_REQUIRE(k % 16 == 0, "signed 4-bit unpack requires K divisible by 16");
+  TB_REQUIRE((reinterpret_cast<uintptr_t>(packed) & 7u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(out) & 15u) == 0,
+             "signed 4-bit unpack requires 8-byte aligned input and 16-byte aligned output");
+  const int64_t n_vec = rows * (k / 16);
+  if (n_vec == 0) return;
+  unpack_s4_kernel<<<grid_for(n_vec, 256), 256, 0, stream>>>(
+      reinterpret_cast<const uint2*>(packed), reinterpret_cast<uint4*>(out), n_vec);
   TB_CUDA_CHECK(cudaGetLastError());
 }
 

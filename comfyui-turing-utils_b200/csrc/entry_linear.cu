@@ -12,6 +12,8 @@ void dequant_launch(const int32_t* acc, int64_t acc_stride, const float* a_s, co
 void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
                             const float* codebook, int8_t* out, int rows, int k, int group_size,
                             cudaStream_t stream);
+void unpack_s4_launch(const int8_t* packed, int8_t* out, int64_t rows, int64_t k,
+                      cudaStream_t stream);
 void sage_quant_launch(const void* input, int dtype, int8_t* out, float* scale, int64_t B,
                        int64_t H, int64_t L, int64_t D, int64_t sb, int64_t sh, int64_t sl,
                        int tile, int64_t num_tiles, int layout, const void* mean,
@@ -109,6 +111,61 @@ int tb_codebook_w4a8_linear(const int8_t* activation, const int8_t* weight_packe
       tb::gemm_i8_launch(activation, workspace, m, rows, k, activation_scale,
                          channel_scale + row, bias ? bias + row : nullptr,
                          static_cast<__nv_bfloat16*>(output) + row, n, 0, s);
+    }
+  });
+}
+
+int tb_w4a8_linear(const int8_t* activation, const int8_t* weight_packed,
+                   const float* activation_scale, const float* weight_scale, const float* bias,
+                   int8_t* workspace, int64_t workspace_rows, void* output, int64_t m, int64_t n,
+                   int64_t k, int64_t ldo, int tile_policy, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(activation && weight_packed && activation_scale && weight_scale && output,
+               "Turing W4A8 tensors must be CUDA tensors");
+    TB_REQUIRE(tile_policy >= 0 && tile_policy <= 5, "invalid Turing W4A8 tile policy");
+    if (m == 0 || n == 0 || k == 0) return;
+    TB_REQUIRE(k % 16 == 0 && n % 8 == 0, "Turing W4A8 linear requires K%16=0 and N%8=0");
+    TB_REQUIRE(workspace != nullptr && workspace_rows > 0 && workspace_rows % 8 == 0,
+               "Turing W4A8 linear needs an 8-row-aligned int8 weight workspace");
+    TB_REQUIRE(ldo >= n, "output row stride must cover N columns");
+    tb::require_sm100();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Unpack a chunk of weight rows to int8 in the workspace, then contract it
+    // into the matching output columns.
+    for (int64_t row = 0; row < n; row += workspace_rows) {
+      const int64_t rows = (n - row) < workspace_rows ? (n - row) : workspace_rows;
+      tb::unpack_s4_launch(weight_packed + row * (k / 2), workspace, rows, k, s);
+      tb::gemm_i8_launch(activation, workspace, m, rows, k, activation_scale, weight_scale + row,
+                         bias ? bias + row : nullptr, static_cast<__nv_bfloat16*>(output) + row,
+                         ldo, 0, s);
+    }
+  });
+}
+
+int tb_int4_linear(const int8_t* activation_packed, const int8_t* weight_packed,
+                   const float* activation_scale, const float* weight_scale, const float* bias,
+                   int8_t* activation_workspace, int8_t* weight_workspace,
+                   int64_t workspace_rows, void* output, int64_t m, int64_t n, int64_t k,
+                   int64_t ldo, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(activation_packed && weight_packed && activation_scale && weight_scale && output,
+               "Turing W4A4 tensors must be CUDA tensors");
+    if (m == 0 || n == 0 || k == 0) return;
+    TB_REQUIRE(k % 16 == 0 && n % 8 == 0, "Turing W4A4 linear requires K%16=0 and N%8=0");
+    TB_REQUIRE(activation_workspace != nullptr,
+               "Turing W4A4 linear needs an int8 [M, K] activation workspace");
+    TB_REQUIRE(weight_workspace != nullptr && workspace_rows > 0 && workspace_rows % 8 == 0,
+               "Turing W4A4 linear needs an 8-row-aligned int8 weight workspace");
+    TB_REQUIRE(ldo >= n, "output row stride must cover N columns");
+    tb::require_sm100();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    tb::unpack_s4_launch(activation_packed, activation_workspace, m, k, s);
+    for (int64_t row = 0; row < n; row += workspace_rows) {
+      const int64_t rows = (n - row) < workspace_rows ? (n - row) : workspace_rows;
+      tb::unpack_s4_launch(weight_packed + row * (k / 2), weight_workspace, rows, k, s);
+      tb::gemm_i8_launch(activation_workspace, weight_workspace, m, rows, k, activation_scale,
+                         weight_scale + row, bias ? bias + row : nullptr,
+                         static_cast<__nv_bfloat16*>(output) + row, ldo, 0, s);
     }
   });
 }

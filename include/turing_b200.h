@@ -145,6 +145,35 @@ TB_API int tb_codebook_w4a8_linear(const int8_t *activation, const int8_t *weigh
                             int64_t n, int64_t k, int64_t group_size, int inline_decode,
                             int tile_policy, tb_stream_t stream);
 
+/* Signed-nibble W4A8 linear: weight_packed [n, k/2] holds two's-complement
+ * 4-bit weights, low nibble = even column; each chunk of workspace_rows
+ * weight rows (workspace: caller-owned int8 [workspace_rows, k], a multiple of
+ * 8) is unpacked to int8 and contracted as tb_int8_linear, writing output
+ * columns [row, row + chunk) with row stride ldo.  Requires k % 16 == 0 and
+ * n % 8 == 0 (the Python binding pads an N tail to 8, as the reference does).
+ * Replaces kernel_api.h:7-13 turing_w4a8_linear (w4a8.cu:34-72, 1000-1086,
+ * bindings.cpp:167-259). */
+TB_API int tb_w4a8_linear(const int8_t *activation, const int8_t *weight_packed,
+                          const float *activation_scale, const float *weight_scale,
+                          const float *bias, int8_t *workspace, int64_t workspace_rows,
+                          void *output, int64_t m, int64_t n, int64_t k, int64_t ldo,
+                          int tile_policy, tb_stream_t stream);
+
+/* W4A4 linear: both operands packed signed 4-bit (low nibble = even column),
+ * activation_packed [m, k/2] as written by the INT4 ConvRot quantizers with
+ * activation_scale [m] (absmax / 7), weight_packed [n, k/2] with weight_scale
+ * [n].  out = bf16(((float)sum_k a4 * w4 * a_s[m]) * w_s[n] + bias[n]).  The
+ * activations are unpacked into activation_workspace (int8 [m, k]) and the
+ * weights chunk by chunk into weight_workspace (int8 [workspace_rows, k]).
+ * Replaces the comfy-kitchen int4_linear call of the plugin's W4A4 path
+ * (comfyui_turing_utils/quantization/dispatch.py:791-804); the INT4 codes
+ * come from convrot_quant.cu:409-433. */
+TB_API int tb_int4_linear(const int8_t *activation_packed, const int8_t *weight_packed,
+                          const float *activation_scale, const float *weight_scale,
+                          const float *bias, int8_t *activation_workspace,
+                          int8_t *weight_workspace, int64_t workspace_rows, void *output,
+                          int64_t m, int64_t n, int64_t k, int64_t ldo, tb_stream_t stream);
+
 /* INT32 accumulator GEMM: acc[m, n] = sum_k act[m,k] * w[n,k] (exact int32),
  * acc row stride acc_stride (elements).  Replaces the INT32 cuBLAS GEMM that
  * the plugin feeds into turing_dequantize_int8_bf16

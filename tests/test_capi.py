@@ -24,6 +24,7 @@ def test_header_declares_the_path():
     names = declared_symbols()
     for required in ("tb_int8_linear", "tb_bf16_int8_convrot_quantize",
                      "tb_codebook_w4a8_linear", "tb_dequantize_int8_bf16",
+                     "tb_w4a8_linear", "tb_int4_linear",
                      "tb_quant_per_warp_int8", "tb_quant_per_block_int8"):
         assert required in names
 
@@ -67,6 +68,14 @@ def test_invalid_arguments_are_rejected_with_messages():
                                      4, 16, 32, 12, 0, 0, None)
     assert st == L.TB_ERR_INVALID
     assert L.last_error() == "unsupported Turing codebook W4A8 group size"
+    st = lib.tb_w4a8_linear(fake, fake, fake, fake, None, fake, 8, fake, 4, 8, 24, 8, 0, None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "Turing W4A8 linear requires K%16=0 and N%8=0"
+    st = lib.tb_w4a8_linear(fake, fake, fake, fake, None, None, 8, fake, 4, 8, 32, 8, 0, None)
+    assert L.last_error() == "Turing W4A8 linear needs an 8-row-aligned int8 weight workspace"
+    st = lib.tb_int4_linear(fake, fake, fake, fake, None, None, fake, 8, fake, 4, 8, 32, 8, None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "Turing W4A4 linear needs an int8 [M, K] activation workspace"
     st = lib.tb_quant_per_warp_int8(fake, 0, fake, fake, 1, 1, 64, 128, 0, 0, 128, 64, 48, 1,
                                     None)
     assert st == L.TB_ERR_INVALID
