@@ -219,11 +219,16 @@ class AttentionWorkload:
               "q_quant": "int8 per 16-token warp tile", "k_quant": "int8 per 64-token block",
               "k_smoothing": True, "pv": "bf16 P x bf16 V, fp32 accumulation"}
 
-    def __init__(self, device, seed):
+    def __init__(self, device, seed, heads=None):
         from comfyui_turing_utils_kernel import turing_sage
         from comfyui_turing_utils_kernel.turing_sage import core
 
         self.ts, self.core = turing_sage, core
+        if heads is not None and heads != self.config["heads"]:
+            # Fewer heads: a smaller case of the same kernel (profiling captures).
+            self.config = dict(self.config, heads=heads,
+                               workload=f"sage_int8_attention, configs[1] shape with {heads} heads")
+            self.name = f"attention_h{heads}"  # no committed traffic figure for this size
         B, H, L, D = (self.config[k] for k in ("batch", "heads", "seq_len", "head_dim"))
         self.ops = 4.0 * B * H * L * L * D
         g = torch.Generator(device=device).manual_seed(seed)
@@ -290,6 +295,12 @@ class AttentionWorkload:
 WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload}
 
 
+def make_workload(args, device, seed):
+    if args.workload == "attention":
+        return AttentionWorkload(device, seed, heads=args.heads)
+    return WORKLOADS[args.workload](device, seed)
+
+
 def default_workload() -> str:
     return "attention" if "attention" in WORKLOADS else "linear"
 
@@ -340,7 +351,7 @@ def run_ours(args, world, rank, local):
     from comfyui_turing_utils_kernel import _lib
 
     device = torch.device("cuda", local)
-    wl = WORKLOADS[args.workload](device, seed=1000 + rank)
+    wl = make_workload(args, device, seed=1000 + rank)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     for _ in range(args.warmup):
         wl.step()
@@ -441,7 +452,7 @@ def cpu_baseline(wl, args) -> dict:
 def run_reference(args, world, rank, local):
     """CPU reference arm (rank 0 only)."""
     device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
-    wl = WORKLOADS[args.workload](device, seed=1000)
+    wl = make_workload(args, device, seed=1000)
     wl.prepare_cpu()
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
@@ -480,6 +491,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="attention heads (default: the config's 40); smaller cases for profiling")
     args = ap.parse_args()
     args.workload = args.workload or default_workload()
     args.warmup = max(args.warmup, 3)
