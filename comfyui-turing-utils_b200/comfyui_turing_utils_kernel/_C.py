@@ -8,10 +8,12 @@ device (the reference's TorchOpContext, bindings.cpp:17-31).
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import _lib
-from ._lib import call, ptr, stream_of
+from ._lib import call, float_dtype_code, ptr, stream_of
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -428,3 +430,79 @@ def turing_gelu_int8_convrot_quantize(input, group_size=256):
 
 def turing_gelu_int4_convrot_quantize(input, group_size=256):
     return _staged(input, group_size, 2, True)
+
+
+def _check_float_like(t: torch.Tensor, name: str) -> None:
+    _check(t.dtype in (torch.float16, torch.bfloat16, torch.float32),
+           f"{name} must be float16, bfloat16, or float32")
+
+
+def turing_segmented_rms_adaln(input, weight, scale, shift, segments, epsilon):
+    """bindings.cpp:734-801: affine RMSNorm + segmented AdaLN modulation."""
+    input = input.contiguous()
+    weight = weight.contiguous()
+    segments = segments.contiguous()
+    _check_cuda_2d(input, "input")
+    _check_float_like(input, "input")
+    _check(weight.is_cuda and weight.dim() == 1 and weight.is_contiguous(),
+           "weight must be a contiguous 1D CUDA tensor")
+    _check(scale.is_cuda and scale.dim() == 2 and scale.stride(1) == 1,
+           "scale must be a CUDA matrix with contiguous rows")
+    _check(shift.is_cuda and shift.dim() == 2 and shift.stride(1) == 1,
+           "shift must be a CUDA matrix with contiguous rows")
+    _check(segments.is_cuda and segments.dim() == 2 and segments.is_contiguous(),
+           "segments must be a contiguous 2D CUDA tensor")
+    _check(segments.dtype == torch.int32 and segments.size(1) == 3,
+           "segments must be int32 [start, stop, modulation_row] triples")
+    dev = input.device
+    _check(weight.device == dev and scale.device == dev and shift.device == dev
+           and segments.device == dev,
+           "all segmented RMSNorm+AdaLN tensors must use the same CUDA device")
+    _check(weight.dtype == input.dtype and scale.dtype == input.dtype
+           and shift.dtype == input.dtype, "weight, scale, and shift dtypes must match input")
+    rows, hidden = input.shape
+    _check(rows > 0 and hidden > 0, "segmented RMSNorm+AdaLN input dimensions must be positive")
+    _check(weight.numel() == hidden, "RMSNorm weight length must match the input hidden dimension")
+    _check(scale.size(0) > 0 and scale.size(1) == hidden, "scale must be [modulation_rows, hidden]")
+    _check(shift.shape == scale.shape, "shift shape must match scale shape")
+    _check(segments.size(0) > 0, "segments must contain at least one row")
+    _check(math.isfinite(epsilon) and epsilon > 0.0, "RMSNorm epsilon must be finite and positive")
+    with torch.cuda.device(dev):
+        _require_blackwell(dev, "segmented RMSNorm+AdaLN")
+        out = torch.empty_like(input)
+        call("tb_segmented_rms_adaln", ptr(input), ptr(weight), ptr(scale), ptr(shift),
+             ptr(segments), ptr(out), rows, hidden, scale.size(0), scale.stride(0),
+             shift.stride(0), segments.size(0), float_dtype_code(input), float(epsilon),
+             stream_of(input))
+    return out
+
+
+def turing_layer_norm_adaln(input, scale, shift, epsilon):
+    """bindings.cpp:803-849: FP32-statistics LayerNorm + Wan AdaLN modulation."""
+    input = input.contiguous()
+    scale = scale.contiguous()
+    shift = shift.contiguous()
+    _check(input.is_cuda and input.dim() == 3 and input.is_contiguous(),
+           "input must be contiguous CUDA [batch, sequence, hidden]")
+    _check_float_like(input, "input")
+    _check(scale.is_cuda and scale.dim() == 3 and scale.is_contiguous(),
+           "scale must be contiguous CUDA [batch, modulation_steps, hidden]")
+    _check(shift.is_cuda and shift.dim() == 3 and shift.is_contiguous(),
+           "shift must be contiguous CUDA [batch, modulation_steps, hidden]")
+    _check(input.device == scale.device and input.device == shift.device,
+           "LayerNorm+AdaLN tensors must use the same CUDA device")
+    _check(input.dtype == scale.dtype and input.dtype == shift.dtype,
+           "LayerNorm+AdaLN tensor dtypes must match")
+    _check(scale.shape == shift.shape, "shift shape must match scale shape")
+    _check(scale.size(0) == input.size(0) and scale.size(2) == input.size(2),
+           "scale must match input batch and hidden dimensions")
+    _check(input.size(0) > 0 and input.size(1) > 0 and input.size(2) > 0 and scale.size(1) > 0,
+           "LayerNorm+AdaLN dimensions must be positive")
+    _check(math.isfinite(epsilon) and epsilon > 0.0, "LayerNorm epsilon must be finite and positive")
+    with torch.cuda.device(input.device):
+        _require_blackwell(input.device, "LayerNorm+AdaLN")
+        out = torch.empty_like(input)
+        call("tb_layer_norm_adaln", ptr(input), ptr(scale), ptr(shift), ptr(out), input.size(0),
+             input.size(1), input.size(2), scale.size(1), float_dtype_code(input), float(epsilon),
+             stream_of(input))
+    return out

@@ -15,9 +15,11 @@ from .ops import (
     turing_gelu_int4_convrot_quantize,
     turing_gelu_int8_convrot_quantize,
     turing_int4_linear,
+    turing_layer_norm_adaln,
     turing_int8_gemm_s32,
     turing_int8_linear,
     turing_swiglu_int4_convrot_quantize,
+    turing_segmented_rms_adaln,
     turing_swiglu_int8_convrot_quantize,
     turing_w4a8_linear,
 )
@@ -40,5 +42,7 @@ __all__ = [
     "turing_swiglu_int8_convrot_quantize",
     "turing_swiglu_int4_convrot_quantize",
     "turing_w4a8_linear",
+    "turing_segmented_rms_adaln",
+    "turing_layer_norm_adaln",
     "turing_sage",
 ]

@@ -23,6 +23,7 @@ TB_ERR_INTERNAL = 4
 
 TB_DTYPE_BF16 = 0
 TB_DTYPE_F16 = 1
+TB_DTYPE_F32 = 2
 TB_LAYOUT_NHD = 0
 TB_LAYOUT_HND = 1
 
@@ -44,6 +45,9 @@ SIGNATURES: dict[str, list] = {
     "tb_gelu_int4_convrot_quantize": [_p, _int, _i64, _i64, _p, _p, _p, _p, _p],
     "tb_swiglu_int8_convrot_quantize_noalloc": [_p, _int, _i64, _i64, _p, _p, _p],
     "tb_int8_linear": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p],
+    "tb_segmented_rms_adaln": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int,
+                               ctypes.c_float, _p],
+    "tb_layer_norm_adaln": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _p],
     "tb_w4a8_linear": [_p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _int, _p],
     "tb_int4_linear": [_p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _p],
     "tb_codebook_w4a8_linear": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64,
@@ -116,6 +120,13 @@ def ptr(t: torch.Tensor | None):
 
 def stream_of(t: torch.Tensor):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def float_dtype_code(t: torch.Tensor) -> int:
+    """dtype code of a float16 / bfloat16 / float32 tensor (norm + AdaLN ops)."""
+    if t.dtype == torch.float32:
+        return TB_DTYPE_F32
+    return dtype_code(t)
 
 
 def dtype_code(t: torch.Tensor) -> int:

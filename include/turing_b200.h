@@ -36,6 +36,7 @@ extern "C" {
 /* 16-bit floating-point input types. */
 #define TB_DTYPE_BF16 0
 #define TB_DTYPE_F16 1
+#define TB_DTYPE_F32 2  /* norm + AdaLN ops only */
 
 /* Tensor layouts of the Sage entry points (reference: tensor_layout 0/1,
  * kernel/csrc/turing/sage/qk_int_sv_f16_cuda_sm75.cu:1059-1101). */
@@ -173,6 +174,34 @@ TB_API int tb_int4_linear(const int8_t *activation_packed, const int8_t *weight_
                           const float *bias, int8_t *activation_workspace,
                           int8_t *weight_workspace, int64_t workspace_rows, void *output,
                           int64_t m, int64_t n, int64_t k, int64_t ldo, tb_stream_t stream);
+
+/* ---------------------------------------------------- norm + AdaLN ---- */
+
+/* Segmented RMSNorm + AdaLN: out[r, k] = T(x[r,k] * rsqrt(mean_k x^2 + eps) *
+ * w[k] * (1 + scale[m,k]) + shift[m,k]), m = the modulation row of the
+ * int32 [start, stop, row] segment holding token r (sorted by stop; 0 when no
+ * segment holds r or the row is out of range).  input/output [rows, hidden]
+ * contiguous; scale/shift [modulation_rows, hidden] with row strides in
+ * elements; dtype TB_DTYPE_BF16 / F16 / F32 for every tensor.  Replaces
+ * kernel_api.h:86-92 turing_segmented_rms_adaln (segmented_rms_adaln.cu:135-235,
+ * bindings.cpp:734-801). */
+TB_API int tb_segmented_rms_adaln(const void *input, const void *weight, const void *scale,
+                                  const void *shift, const int32_t *segments, void *output,
+                                  int64_t rows, int64_t hidden, int64_t modulation_rows,
+                                  int64_t scale_stride, int64_t shift_stride,
+                                  int64_t segment_count, int dtype, float epsilon,
+                                  tb_stream_t stream);
+
+/* LayerNorm + AdaLN over contiguous [batch, sequence, hidden] with scale/shift
+ * [batch, modulation_steps, hidden]: token t of a batch uses modulation step
+ * min(t / ceil(sequence / steps), steps - 1); n = T((x - mean) * rsqrt(var +
+ * eps)), out = T(float(n) * float(T(1 + scale)) + shift).  Replaces
+ * kernel_api.h:94-98 turing_layer_norm_adaln (segmented_rms_adaln.cu:237-306,
+ * bindings.cpp:803-849). */
+TB_API int tb_layer_norm_adaln(const void *input, const void *scale, const void *shift,
+                               void *output, int64_t batch, int64_t sequence, int64_t hidden,
+                               int64_t modulation_steps, int dtype, float epsilon,
+                               tb_stream_t stream);
 
 /* INT32 accumulator GEMM: acc[m, n] = sum_k act[m,k] * w[n,k] (exact int32),
  * acc row stride acc_stride (elements).  Replaces the INT32 cuBLAS GEMM that

@@ -329,3 +329,58 @@ NORTH_STAR_REL_L2 = 1.0e-2
 
 
 __all__ = [name for name in dir() if not name.startswith("_")]
+
+
+# ------------------------------------------------------------ norm + AdaLN --
+# CPU restatement of kernel/csrc/turing/segmented_rms_adaln.cu with float64
+# statistics (the kernels reduce in fp32 in their own orders, so results agree
+# to the last-bit rounding of the output dtype, not bit for bit).
+
+def _round_to(a64: np.ndarray, dtype) -> np.ndarray:
+    """float64 -> dtype (torch float16 / bfloat16 / float32) -> float64."""
+    import torch
+
+    return torch.from_numpy(np.asarray(a64, np.float64)).to(dtype).double().numpy()
+
+
+def segment_rows(segments: np.ndarray, rows: int, modulation_rows: int) -> np.ndarray:
+    """Modulation row of every token row (segmented_rms_adaln.cu:115-132):
+    the [start, stop, row] segment holding it (segments sorted by stop), 0 when
+    none does or the named row is out of range."""
+    seg = np.asarray(segments, np.int64).reshape(-1, 3)
+    out = np.zeros(rows, np.int64)
+    for r in range(rows):
+        i = int(np.searchsorted(seg[:, 1], r, side="right"))
+        m = -1
+        if i < len(seg) and r >= seg[i, 0]:
+            m = int(seg[i, 2])
+        out[r] = m if 0 <= m < modulation_rows else 0
+    return out
+
+
+def rms_adaln(x, w, scale, shift, segments, eps, dtype):
+    """out = T(x * rsqrt(mean(x^2) + eps) * w * (1 + scale[m]) + shift[m])
+    (segmented_rms_adaln.cu:135-235); inputs as float arrays of T values."""
+    x = np.asarray(x, np.float64)
+    inv = 1.0 / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + eps)
+    m = segment_rows(segments, x.shape[0], np.asarray(scale).shape[0])
+    sc, sh = np.asarray(scale, np.float64)[m], np.asarray(shift, np.float64)[m]
+    return _round_to(x * inv * np.asarray(w, np.float64)[None] * (1.0 + sc) + sh, dtype)
+
+
+def layer_norm_adaln(x, scale, shift, eps, dtype):
+    """n = T((x - mean) * rsqrt(var + eps)), out = T(n * T(1 + scale) + shift) with
+    token t of a batch on modulation step min(t / ceil(seq / steps), steps - 1)
+    (segmented_rms_adaln.cu:237-306)."""
+    x = np.asarray(x, np.float64)
+    batch, seq, hid = x.shape
+    steps = np.asarray(scale).shape[1]
+    per = -(-seq // steps)
+    tok = np.minimum(np.arange(seq) // max(per, 1), steps - 1) if steps > 1 else np.zeros(seq, int)
+    mean = x.mean(axis=2, keepdims=True)
+    var = ((x - mean) ** 2).mean(axis=2, keepdims=True)
+    n = _round_to((x - mean) / np.sqrt(var + eps), dtype)
+    sc = np.asarray(scale, np.float64)[:, tok]
+    sh = np.asarray(shift, np.float64)[:, tok]
+    mult = _round_to(1.0 + sc, dtype)
+    return _round_to(n * mult + sh, dtype)

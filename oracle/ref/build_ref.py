@@ -2,7 +2,8 @@
 
 Compiles, from the reference checkout where the sources lie (read-only), into
 oracle/_ref/ (git-ignored; it travels to the GPU box with the snapshot):
-  * libref_linear.so — kernel/csrc/turing/{convrot_quant,bf16_epilogue,w4a8}.cu
+  * libref_linear.so — kernel/csrc/turing/{convrot_quant,bf16_epilogue,w4a8,
+    segmented_rms_adaln}.cu
     with the reference's nvcc flags (kernel/setup.py:398-412, no fast-math) and
     the CUTLASS 2.x headers vendored in site-packages, plus
     oracle/ref/ref_linear_shim.cu (C entry points);
@@ -49,7 +50,8 @@ def build_linear() -> Path:
     objdir.mkdir(parents=True, exist_ok=True)
     cut = cutlass_include()
     srcs = [CSRC / "turing" / "convrot_quant.cu", CSRC / "turing" / "bf16_epilogue.cu",
-            CSRC / "turing" / "w4a8.cu", HERE / "ref_linear_shim.cu"]
+            CSRC / "turing" / "w4a8.cu", CSRC / "turing" / "segmented_rms_adaln.cu",
+            HERE / "ref_linear_shim.cu"]
     procs, objs = [], []
     for s in srcs:
         o = objdir / (s.stem + ".o")

@@ -115,4 +115,32 @@ int ref_dequant(const int32_t* acc, const float* a_s, const float* w_s, int w_nu
   });
 }
 
+// dtype: 0 bf16, 1 f16, 2 f32.
+static Tensor::ScalarType float_type(int dtype) {
+  return dtype == 0 ? Tensor::BF16 : dtype == 1 ? Tensor::FP16 : Tensor::FP32;
+}
+
+int ref_segmented_rms_adaln(const void* x, const void* w, const void* scale, const void* shift,
+                            const int* segments, void* out, int rows, int hidden, int mod_rows,
+                            int n_seg, int dtype, float eps, void* stream) {
+  return run(stream, [&] {
+    const auto t = float_type(dtype);
+    K::turing_segmented_rms_adaln(mk(x, {rows, hidden}, t), mk(w, {hidden}, t),
+                                  mk(scale, {mod_rows, hidden}, t), mk(shift, {mod_rows, hidden}, t),
+                                  mk(segments, {n_seg, 3}, Tensor::INT32),
+                                  mk(out, {rows, hidden}, t), eps);
+  });
+}
+
+int ref_layer_norm_adaln(const void* x, const void* scale, const void* shift, void* out,
+                         int batch, int seq, int hidden, int steps, int dtype, float eps,
+                         void* stream) {
+  return run(stream, [&] {
+    const auto t = float_type(dtype);
+    K::turing_layer_norm_adaln(mk(x, {batch, seq, hidden}, t), mk(scale, {batch, steps, hidden}, t),
+                               mk(shift, {batch, steps, hidden}, t),
+                               mk(out, {batch, seq, hidden}, t), eps);
+  });
+}
+
 }  // extern "C"

@@ -28,6 +28,9 @@ def linear():
     lib.ref_w4a8_linear.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p]
     lib.ref_codebook_linear.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _i, _i, _i, _p]
     lib.ref_dequant.argtypes = [_p, _p, _p, _i, _p, _i, _i, _p]
+    lib.ref_segmented_rms_adaln.argtypes = [_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i,
+                                            ctypes.c_float, _p]
+    lib.ref_layer_norm_adaln.argtypes = [_p, _p, _p, _p, _i, _i, _i, _i, _i, ctypes.c_float, _p]
     return lib
 
 

@@ -2,7 +2,7 @@
 own CUDA kernels (built from its sources by oracle/ref/build_ref.py into
 oracle/_ref) on seeded CPU-generated inputs, on a B200.
 
-    python tests/golden/make_golden.py [out_dir]
+    python tests/golden/make_golden.py [out_dir] [--only norm]
 
 Each fixture is a compressed .npz holding the inputs (as raw bits) and the
 reference's outputs.  tests/test_oracle_golden.py checks the CPU oracle
@@ -37,8 +37,51 @@ def act(rows, cols, seed, outliers=True):
     return x.to(torch.bfloat16)
 
 
-def main(out_dir: Path) -> None:
+def norm_fixtures(dev, L) -> dict:
+    """Segmented RMSNorm+AdaLN and LayerNorm+AdaLN (segmented_rms_adaln.cu)."""
+    fx = {}
+    codes = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+    for dtype, tag in ((torch.bfloat16, "bf16"), (torch.float16, "f16"), (torch.float32, "f32")):
+        g = torch.Generator().manual_seed(91 + codes[dtype])
+        rows, hidden, mod_rows = 13, (5120 if dtype != torch.float32 else 2048), 3
+        x = (torch.randn((rows, hidden), generator=g) * 3 + 0.5).to(dtype)
+        w = (torch.rand((hidden,), generator=g) + 0.5).to(dtype)
+        sc = (torch.randn((mod_rows, hidden), generator=g) * 0.1).to(dtype)
+        sh = (torch.randn((mod_rows, hidden), generator=g) * 0.1).to(dtype)
+        # Row 11 lies in no segment and row 12 names an out-of-range modulation
+        # row: both fall back to modulation row 0.
+        seg = torch.tensor([[0, 4, 2], [4, 9, 0], [9, 11, 1], [12, 13, 7]], dtype=torch.int32)
+        out = torch.empty((rows, hidden), dtype=dtype, device=dev)
+        xd, wd, scd, shd, segd = (t.to(dev) for t in (x, w, sc, sh, seg))
+        R.check(L.ref_segmented_rms_adaln(R.ptr(xd), R.ptr(wd), R.ptr(scd), R.ptr(shd), R.ptr(segd),
+                                          R.ptr(out), rows, hidden, mod_rows, 4, codes[dtype],
+                                          1e-6, R.stream()), "segmented_rms_adaln")
+        torch.cuda.synchronize()
+        fx[f"rms_adaln_{tag}"] = {"x": bits(x), "w": bits(w), "scale": bits(sc), "shift": bits(sh),
+                                  "segments": seg.numpy(), "out": bits(out)}
+        batch, seq, hid, steps = 2, 9, 1536, 4
+        x = (torch.randn((batch, seq, hid), generator=g) * 2 + 3.0).to(dtype)
+        sc = (torch.randn((batch, steps, hid), generator=g) * 0.1).to(dtype)
+        sh = (torch.randn((batch, steps, hid), generator=g) * 0.1).to(dtype)
+        out = torch.empty((batch, seq, hid), dtype=dtype, device=dev)
+        xd, scd, shd = (t.to(dev) for t in (x, sc, sh))
+        R.check(L.ref_layer_norm_adaln(R.ptr(xd), R.ptr(scd), R.ptr(shd), R.ptr(out), batch, seq,
+                                       hid, steps, codes[dtype], 1e-6, R.stream()),
+                "layer_norm_adaln")
+        torch.cuda.synchronize()
+        fx[f"ln_adaln_{tag}"] = {"x": bits(x), "scale": bits(sc), "shift": bits(sh),
+                                 "out": bits(out)}
+    return fx
+
+
+def main(out_dir: Path, only: str = "") -> None:
     out_dir.mkdir(parents=True, exist_ok=True)
+    if only == "norm":
+        fx = norm_fixtures(torch.device("cuda:0"), R.linear())
+        for name, rec in fx.items():
+            np.savez_compressed(out_dir / f"{name}.npz", **rec)
+        print(f"wrote {len(fx)} fixtures to {out_dir}")
+        return
     dev = torch.device("cuda:0")
     L = R.linear()
     S = R.sage()
@@ -165,4 +208,8 @@ def main(out_dir: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent)
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else ""
+    if only:
+        args = [a for a in args if a != only]
+    main(Path(args[0]) if args else Path(__file__).resolve().parent, only)
