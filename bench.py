@@ -142,7 +142,7 @@ class LinearWorkload:
 
         self.kernel, self._C = kernel, _C
         m, k, n = self.config["m"], self.config["k"], self.config["n"]
-        self.ops = 2.0 * m * n * k
+        self.ops = self.dom_ops = 2.0 * m * n * k
         g = torch.Generator().manual_seed(seed)
         x = torch.randn((m, k), generator=g)
         idx = torch.randperm(k, generator=g)[: int(round(k * 0.005))]
@@ -185,7 +185,7 @@ class LinearWorkload:
 
     def roofline(self, dom_ms, peaks):
         int8_peak = 2.0 * peaks["bf16_tflops"]
-        achieved = self.ops / (dom_ms * 1e-3) / 1e12
+        achieved = self.dom_ops / (dom_ms * 1e-3) / 1e12
         return {"kernel": self.dominant, "bound": "tensor", "achieved": round(achieved, 1),
                 "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
                 "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s (MEASURED_PEAKS.json "
@@ -210,6 +210,207 @@ class LinearWorkload:
         self.w_cpu = self.w.cpu().float()
         self.w_s_cpu = self.w_s.cpu()
         self.bias_cpu = self.bias.cpu().float()
+
+
+class CodebookWorkload:
+    """grouped-codebook W4A8 linear.  The reference's fast
+    path stores symmetric codebook weights (packed 4-bit indices, 16-entry fp32
+    codebook, E4M3 group scales relative to an fp32 channel scale); the config's
+    per-group zero points have no codebook form and run with the zero point
+    fixed at 8 (codebook[i] = i - 8), which leaves the arithmetic unchanged."""
+
+    name = "codebook"
+    config = {"workload": "codebook_w4a8_linear (BASELINE configs[2])", "m": 8192, "k": 5120,
+              "n": 5120, "group_size": 128, "rotation": 256,
+              "activation": "per-token int8 (ConvRot)",
+              "weight": "4-bit codebook indices, e4m3 group scales, fp32 channel scales"}
+
+    def __init__(self, device, seed):
+        import comfyui_turing_utils_kernel as kernel
+        from comfyui_turing_utils_kernel import _C
+
+        self.kernel, self._C = kernel, _C
+        m, k, n, gsz = (self.config[key] for key in ("m", "k", "n", "group_size"))
+        self.ops = self.dom_ops = 2.0 * m * n * k
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn((m, k), generator=g).to(torch.bfloat16)
+        self.x_host = x.pin_memory() if device.type == "cuda" else x
+        self.x = self.x_host.to(device)
+        idx = torch.randint(0, 16, (n, k), generator=g, dtype=torch.int32)
+        packed = (idx[:, 0::2] | (idx[:, 1::2] << 4)).to(torch.uint8).view(torch.int8)
+        self.w_packed = packed.to(device)
+        group_abs = torch.rand((n, k // gsz), generator=g) * 9e-3 + 1e-3
+        # Channel scale so that |codebook| * relative group scale spans +-127.
+        self.c_s = (group_abs.amax(dim=1) * 8.0 / 127.0).to(device)
+        rel = group_abs / self.c_s.cpu()[:, None]
+        self.g_s = rel.to(torch.float8_e4m3fn).view(torch.uint8).to(device)
+        self.codebook = (torch.arange(16, dtype=torch.float32) - 8.0).to(device)
+        self.out_host = torch.empty((m, n), dtype=torch.bfloat16,
+                                    pin_memory=device.type == "cuda")
+        self.launches_per_step = 1 + 2 * ((n + 4095) // 4096)
+        self.dominant = "gemm_i8"
+        self.h2d_bytes = self.x_host.numel() * 2
+        self.d2h_bytes = self.out_host.numel() * 2
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        xq, xs = self._C.turing_bf16_int8_convrot_quantize(self.x)
+        if ev:
+            ev[1].record()
+        out = self._C.turing_codebook_w4a8_linear(xq, self.w_packed, xs, self.g_s, self.c_s,
+                                                  self.codebook, None, self.config["group_size"])
+        if ev:
+            ev[2].record()
+        return out
+
+    def step_e2e(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        xq, xs = self.kernel.turing_bf16_int8_convrot_quantize(x)
+        out = self.kernel.turing_codebook_w4a8_linear(xq, self.w_packed, xs, self.g_s, self.c_s,
+                                                      self.codebook, None,
+                                                      self.config["group_size"])
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    cpu_sample_desc = ("rows of X, full N and K (ConvRot oracle + oracle codebook decode + "
+                       "torch fp32 dequantize-then-matmul)")
+
+    def roofline(self, dom_ms, peaks):
+        return LinearWorkload.roofline(self, dom_ms, peaks)
+
+    def cpu_reference_step(self, rows: int):
+        import numpy as np
+
+        import oracle
+
+        xs = self.x_host[:rows]
+        q, s = oracle.convrot_quantize(xs.view(torch.int16).numpy().view(np.uint16))
+        out = (torch.from_numpy(q).float() @ self.w_cpu.t()) * torch.from_numpy(s) \
+            * self.c_s_cpu[None, :]
+        return out.to(torch.bfloat16), 2.0 * rows * self.config["n"] * self.config["k"]
+
+    def prepare_cpu(self):
+        import oracle
+
+        w8 = oracle.codebook_decode(self.w_packed.cpu().numpy(), self.g_s.cpu().numpy(),
+                                    self.codebook.cpu().numpy(), self.config["group_size"])
+        self.w_cpu = torch.from_numpy(w8).float()
+        self.c_s_cpu = self.c_s.cpu()
+
+
+class W4A4FFNWorkload:
+    """the W4A4 ConvRot FFN pair.  INT4 activations use
+    the reference's per-token scales (absmax / 7, convrot_quant.cu:409-433) and
+    the weights per-channel scales (dispatch.py:907-909): the config's group-64
+    fp16 scales are only validated by the reference, not used."""
+
+    name = "w4a4_ffn"
+    n_events = 4  # the step continues after the timed up projection
+    config = {"workload": "w4a4_convrot_ffn (BASELINE configs[3])", "m": 32760, "dim": 5120,
+              "ffn": 13824, "rotation": 256, "activation": "per-token int4 (ConvRot)",
+              "weight": "int4 per-channel", "between": "GELU-tanh fused into the down "
+              "projection's INT4 quantizer"}
+
+    def __init__(self, device, seed):
+        import comfyui_turing_utils_kernel as kernel
+        from comfyui_turing_utils_kernel import _C
+
+        self.kernel, self._C = kernel, _C
+        m, d, f = self.config["m"], self.config["dim"], self.config["ffn"]
+        self.ops = 2.0 * 2.0 * m * d * f
+        self.dom_ops = 2.0 * m * d * f  # the up projection, timed on its own
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn((m, d), generator=g)
+        idx = torch.randperm(d, generator=g)[: int(round(d * 0.005))]
+        x[:, idx] *= 20.0
+        x = x.to(torch.bfloat16)
+        self.x_host = x.pin_memory() if device.type == "cuda" else x
+        self.x = self.x_host.to(device)
+
+        def pack(rows, cols):
+            v = torch.randint(-8, 8, (rows, cols), generator=g, dtype=torch.int32)
+            return ((v[:, 0::2] & 0xF) | ((v[:, 1::2] & 0xF) << 4)).to(torch.uint8).view(torch.int8)
+
+        self.w_up = pack(f, d).to(device)
+        self.w_down = pack(d, f).to(device)
+        self.s_up = (torch.rand((f,), generator=g) * 4e-3 + 1e-3).to(device)
+        self.s_down = (torch.rand((d,), generator=g) * 4e-3 + 1e-3).to(device)
+        self.b_up = (torch.randn((f,), generator=g) * 0.02).to(device)
+        self.b_down = (torch.randn((d,), generator=g) * 0.02).to(device)
+        self.out_host = torch.empty((m, d), dtype=torch.bfloat16,
+                                    pin_memory=device.type == "cuda")
+        # quantize, W4A4 up (activation unpack + 4 chunks x (unpack, GEMM)), GELU
+        # quantize, W4A4 down (activation unpack + 2 chunks x (unpack, GEMM)).
+        self.launches_per_step = 1 + (1 + 2 * ((f + 4095) // 4096)) + 1 + (1 + 2 * ((d + 4095) // 4096))
+        self.dominant = "gemm_i8"
+        self.h2d_bytes = self.x_host.numel() * 2
+        self.d2h_bytes = self.out_host.numel() * 2
+
+    def _ffn(self, x, ev=None, public=False):
+        K = self.kernel if public else self._C
+        if ev:
+            ev[0].record()
+        q, s = K.turing_bf16_int4_convrot_quantize(x)
+        if ev:
+            ev[1].record()
+        h = K.turing_int4_linear(q, self.w_up, s.reshape(-1), self.s_up, self.b_up)
+        if ev:
+            ev[2].record()
+        q2, s2 = K.turing_bf16_gelu_int4_convrot_quantize(h)
+        out = K.turing_int4_linear(q2, self.w_down, s2.reshape(-1), self.s_down, self.b_down)
+        if ev:
+            ev[3].record()
+        return out
+
+    def step(self, ev=None):
+        return self._ffn(self.x, ev)
+
+    def step_e2e(self):
+        x = self.x_host.to(self.x.device, non_blocking=True)
+        out = self._ffn(x, public=True)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    cpu_sample_desc = ("rows of X through both projections (ConvRot INT4 oracle, torch fp32 "
+                       "dequantize-then-matmul, GELU-fused INT4 oracle)")
+
+    def roofline(self, dom_ms, peaks):
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        achieved = self.dom_ops / (dom_ms * 1e-3) / 1e12
+        return {"kernel": self.dominant, "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": round(int8_peak, 1), "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s (MEASURED_PEAKS.json "
+                               "bf16_tflops); dense INT8 = 2 x BF16 on B200",
+                "kernel_ms": round(dom_ms, 4),
+                "timed": "W4A4 up projection (INT4 unpacks + tcgen05 INT8 GEMM)"}
+
+    def cpu_reference_step(self, rows: int):
+        import numpy as np
+
+        import oracle
+
+        def lin(q_packed, s, w, ws, b, k):
+            a = torch.from_numpy(oracle.unpack_int4(q_packed, k)).float()
+            return (a @ w.t()) * torch.from_numpy(np.reshape(s, (-1, 1))) * ws[None, :] + b[None, :]
+
+        d, f = self.config["dim"], self.config["ffn"]
+        xs = self.x_host[:rows]
+        q, s = oracle.convrot_quantize(xs.view(torch.int16).numpy().view(np.uint16), int4=True)
+        h = lin(q, s, self.w_up_cpu, self.s_up_cpu, self.b_up_cpu, d).to(torch.bfloat16)
+        q2, s2 = oracle.convrot_quantize(h.view(torch.int16).numpy().view(np.uint16), int4=True,
+                                         act="gelu")
+        out = lin(q2, s2, self.w_down_cpu, self.s_down_cpu, self.b_down_cpu, f)
+        return out.to(torch.bfloat16), 2.0 * 2.0 * rows * d * f
+
+    def prepare_cpu(self):
+        import oracle
+
+        d, f = self.config["dim"], self.config["ffn"]
+        self.w_up_cpu = torch.from_numpy(oracle.unpack_int4(self.w_up.cpu().numpy(), d)).float()
+        self.w_down_cpu = torch.from_numpy(oracle.unpack_int4(self.w_down.cpu().numpy(), f)).float()
+        self.s_up_cpu, self.s_down_cpu = self.s_up.cpu(), self.s_down.cpu()
+        self.b_up_cpu, self.b_down_cpu = self.b_up.cpu(), self.b_down.cpu()
 
 
 class AttentionWorkload:
@@ -292,7 +493,8 @@ class AttentionWorkload:
     cpu_sample_desc = "query rows of one head (cycling heads) vs all 32760 keys, fp32 SDPA"
 
 
-WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload}
+WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload,
+             "codebook": CodebookWorkload, "w4a4_ffn": W4A4FFNWorkload}
 
 
 def make_workload(args, device, seed):
@@ -358,7 +560,7 @@ def run_ours(args, world, rank, local):
         flush.fill_(1.0)
     torch.cuda.synchronize()
 
-    n_ev = 3
+    n_ev = getattr(wl, "n_events", 3)  # step start, dominant start, dominant end[, step end]
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
     sampler = ClockSampler(local)
     barrier(world)
