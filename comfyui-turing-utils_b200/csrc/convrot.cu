@@ -13,11 +13,11 @@
 //   * scale = max(min(amax, dtype_max) / 127, 1e-30) (row-buffer form) or
 //     max(min(amax, dtype_max) * (1/127), 1e-30) (staged form); INT4 uses 7
 //     and 1e-10;
-//   * INT8 code = clamp(rint(round_dtype(v / round_dtype(scale))), -128, 127)
-//     (taken as a multiply by the reciprocal of round_dtype(scale); see
-//     quantize16_store)
-//     with an IEEE divide; INT4 code = clamp(rint(v * (1/scale)), -7, 7),
-//     two per byte, low nibble = even column.
+//   * INT8 code = clamp(rint(round_dtype(v / round_dtype(scale))), -128, 127),
+//     the reference's IEEE divide taken here as a multiply by the correctly
+//     rounded reciprocal of round_dtype(scale) (same codes; see
+//     quantize16_store); INT4 code = clamp(rint(v * (1/scale)), -7, 7), two
+//     per byte, low nibble = even column.
 //
 // B200 layout: one half-warp owns a 256-group, 16 consecutive elements per
 // lane (two 16-byte loads).  Stages S=1 and S=4 run in registers; the group
