@@ -8,10 +8,19 @@ and distributions — the reference benchmarks on no public dataset):
              Q/K/V bf16 ~N(0,1), K + per-channel offset ~N(0,2), K mean
              smoothing, Q per 16-token warp tiles, K per 64-token blocks.
              Step = Q/K quantize + attention.
+  attention_rope
+             configs[1] shape through the fused Q/K prologue a Wan block uses:
+             RMSNorm over the whole 5120-wide row (norm_scope "row") with an
+             affine weight, interleaved RoPE over all 128 channels with
+             per-token rotations, INT8 Q/K in one pass, then the attention.
+             Step = prologue + attention; the prologue is reported against
+             the HBM roofline beside the attention's.
   linear     configs[0]: ConvRot W8A8 linear, X [4096, 5120] bf16 with 0.5%
              outlier channels x20, W [13824, 5120] int8, per-channel scales,
              bf16 bias.  Step = ConvRot INT8 quantize + tcgen05 GEMM with the
              fused dequant/bias/bf16 epilogue.
+  codebook   configs[2]: W4A8 grouped-codebook linear, X [8192, 5120].
+  w4a4_ffn   configs[3]: W4A4 ConvRot FFN pair over 32760 tokens.
 Metric: INT8 TOPS (whole job, all ranks) = algorithmic ops / device time.
 
 Multi-GPU (torchrun): every rank runs its own independent copy of the
@@ -479,7 +488,7 @@ class AttentionWorkload:
                 "kernel_ms": round(dom_ms, 4)}
 
     def prepare_cpu(self):
-        self.q_cpu, self.k_cpu, self.v_cpu = (t[0].float() for t in self.host)
+        self.q_cpu, self.k_cpu, self.v_cpu = (t[0].float() for t in self.host[:3])
 
     def cpu_reference_step(self, rows: int):
         """Reference CPU path (validate_compatible.py:540-546): fp32 SDPA of
@@ -493,13 +502,107 @@ class AttentionWorkload:
     cpu_sample_desc = "query rows of one head (cycling heads) vs all 32760 keys, fp32 SDPA"
 
 
+class AttentionRopeWorkload(AttentionWorkload):
+    """configs[1] attention fed by the fused RMSNorm + RoPE + INT8 Q/K prologue
+    (sage/qk_preprocess.cu; the Wan self-attention normalizes Q and K over the
+    whole row and rotates every channel pair per token)."""
+    name = "attention_rope"
+    config = dict(AttentionWorkload.config,
+                  workload="sage_int8_attention (BASELINE configs[1]) behind the fused "
+                           "RMSNorm(row)+RoPE+INT8 Q/K prologue",
+                  k_smoothing=False, norm_scope="row", rope="interleaved, rot_dim 128, "
+                  "per-token 2x2 rotations [1, L, 1, 64, 2, 2] bf16")
+
+    def __init__(self, device, seed, heads=None):
+        super().__init__(device, seed, heads=heads)
+        self.name = "attention_rope" if heads in (None, 40) else f"attention_rope_h{heads}"
+        B, H, L, D = (self.config[k] for k in ("batch", "heads", "seq_len", "head_dim"))
+        g = torch.Generator(device=device).manual_seed(seed + 1)
+        self.qn = (torch.rand((H * D,), generator=g, device=device) + 0.5).to(torch.bfloat16)
+        self.kn = (torch.rand((H * D,), generator=g, device=device) + 0.5).to(torch.bfloat16)
+        ang = torch.rand((1, L, 1, D // 2, 1, 1), generator=g, device=device) * 6.283
+        c, s_ = torch.cos(ang), torch.sin(ang)
+        self.freqs = torch.cat([torch.cat([c, -s_], -1), torch.cat([s_, c], -1)], -2).to(
+            torch.bfloat16)
+        self.host += [t.cpu().pin_memory() for t in (self.qn, self.kn, self.freqs)]
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host)
+        self.launches_per_step = 3  # row RRMS, fused Q/K prologue, attention
+        # Algorithmic bytes of the prologue: Q and K read once, INT8 codes and
+        # fp32 scales written, the rotations and norm weights read.
+        n = B * H * L * D
+        self.prologue_bytes = (2 * n * 2 + 2 * n + 4 * B * H * ((L + 63) // 64) * 5
+                               + self.freqs.numel() * 2 + 2 * H * D * 2)
+
+    def _prologue(self, q, k, qn, kn, fr):
+        return self.ts.prequantize_rms_rope_qk(q, k, qn, kn, fr, epsilon=1e-6, rot_dim=128,
+                                               norm_scope="row")
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        qk = self._prologue(self.q, self.k, self.qn, self.kn, self.freqs)
+        pre = self.ts.prequantize_sageattn_from_qk(qk, self.v)
+        if ev:
+            ev[1].record()
+        out = self.core.sageattn_from_prequantized(pre)
+        if ev:
+            ev[2].record()
+        return out
+
+    def step_e2e(self):
+        dev = self.q.device
+        q, k, v, qn, kn, fr = (t.to(dev, non_blocking=True) for t in self.host)
+        pre = self.ts.prequantize_sageattn_from_qk(self._prologue(q, k, qn, kn, fr), v)
+        out = self.ts.sageattn_from_prequantized(pre)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    def aux_roofline(self, pro_ms, peaks):
+        achieved = self.prologue_bytes / (pro_ms * 1e-3) / 1e9
+        return {"prologue": {"kernel": "qk_rms_rope (+ row_rrms)", "bound": "hbm",
+                             "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                             "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                             "algorithmic_bytes": self.prologue_bytes,
+                             "ms": round(pro_ms, 4)}}
+
+    def prepare_cpu(self):
+        super().prepare_cpu()
+        B, H, L, D = (self.config[k] for k in ("batch", "heads", "seq_len", "head_dim"))
+        self.qn_cpu, self.kn_cpu = self.host[3].float().view(H, D), self.host[4].float().view(H, D)
+        self.fr_cpu = self.host[5].float().view(L, D // 2, 2, 2)
+        # Row RRMS over all heads (the reference's norm_scope "row").
+        self.q_rrms_cpu = torch.rsqrt(self.q_cpu.pow(2).mean(dim=(0, 2)) + 1e-6)
+        self.k_rrms_cpu = torch.rsqrt(self.k_cpu.pow(2).mean(dim=(0, 2)) + 1e-6)
+
+    def _norm_rope(self, x, rrms, w, tokens):
+        n = (x * rrms[tokens, None] * w).view(x.shape[0], -1, 2)
+        f = self.fr_cpu[tokens]
+        return torch.einsum("tprc,tpc->tpr", f, n).reshape(x.shape)
+
+    def cpu_reference_step(self, rows: int):
+        """RMSNorm + RoPE (fp32) of `rows` query rows and all keys of one head,
+        then the fp32 SDPA of the attention arm."""
+        H, L = self.config["heads"], self.config["seq_len"]
+        h = self._cpu_head = (getattr(self, "_cpu_head", -1) + 1) % H
+        qt, kt = torch.arange(rows), torch.arange(L)
+        q = self._norm_rope(self.q_cpu[h, :rows], self.q_rrms_cpu, self.qn_cpu[h], qt)
+        k = self._norm_rope(self.k_cpu[h], self.k_rrms_cpu, self.kn_cpu[h], kt)
+        out = torch.nn.functional.scaled_dot_product_attention(q[None, None], k[None, None],
+                                                               self.v_cpu[h][None, None])
+        return out, 4.0 * rows * L * self.config["head_dim"]
+
+    cpu_sample_desc = ("query rows of one head (cycling heads): fp32 row RMSNorm + RoPE of "
+                       "those rows and all 32760 keys, then fp32 SDPA")
+
+
 WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload,
+             "attention_rope": AttentionRopeWorkload,
              "codebook": CodebookWorkload, "w4a4_ffn": W4A4FFNWorkload}
 
 
 def make_workload(args, device, seed):
-    if args.workload == "attention":
-        return AttentionWorkload(device, seed, heads=args.heads)
+    if args.workload in ("attention", "attention_rope"):
+        return WORKLOADS[args.workload](device, seed, heads=args.heads)
     return WORKLOADS[args.workload](device, seed)
 
 
@@ -604,6 +707,9 @@ def run_ours(args, world, rank, local):
     peaks = load_peaks()
     roof = wl.roofline(dom_avg, peaks)
     roof["traffic"] = ncu_traffic(wl.dominant, wl.name)
+    if hasattr(wl, "aux_roofline"):
+        pro = [ev[0].elapsed_time(ev[1]) for ev in events]
+        roof.update(wl.aux_roofline(sum(pro) / len(pro), peaks))
     result = {
         "metric": METRIC,
         "value": round(world * wl.ops / (ms * 1e-3) / 1e12, 2),

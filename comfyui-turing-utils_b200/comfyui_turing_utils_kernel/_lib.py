@@ -45,6 +45,9 @@ SIGNATURES: dict[str, list] = {
     "tb_gelu_int4_convrot_quantize": [_p, _int, _i64, _i64, _p, _p, _p, _p, _p],
     "tb_swiglu_int8_convrot_quantize_noalloc": [_p, _int, _i64, _i64, _p, _p, _p],
     "tb_int8_linear": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p],
+    "tb_quant_qk_rms_rope_int8": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                                  _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _int, _int, _int,
+                                  ctypes.c_float, _p],
     "tb_segmented_rms_adaln": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int,
                                ctypes.c_float, _p],
     "tb_layer_norm_adaln": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _p],

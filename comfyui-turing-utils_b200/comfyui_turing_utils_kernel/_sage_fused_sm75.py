@@ -98,3 +98,86 @@ def token_mean_cuda(input, mean, tensor_layout):
     with torch.cuda.device(input.device):
         call("tb_token_mean", ptr(input), dtype_code(input), ptr(mean), B, H, L, D, sb, sh, sl,
              int(tensor_layout), stream_of(input))
+
+
+def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scale, key_scale,
+                                query_norm, key_norm, freqs, query_rrms, key_rrms, anchor_indices,
+                                anchor_values, epsilon, rot_dim, query_block_size,
+                                query_warp_block_size, key_block_size, tensor_layout, norm_scope,
+                                split_half, rotate):
+    """Fused RMSNorm + RoPE + Q/K INT8 quantization (qk_preprocess.cu:566-753).
+    The Hadamard-rotated form with K anchors (rotate=True) feeds only the W8A8
+    attention, which this package does not provide."""
+    _check(not rotate and anchor_indices.numel() == 0,
+           "the Hadamard-rotated Q/K preprocessing (rotate=True, K anchors) is not built in "
+           "this package")
+    for t, name in ((query, "query"), (key, "key"), (query_output, "query_output"),
+                    (key_output, "key_output"), (query_scale, "query_scale"),
+                    (key_scale, "key_scale"), (query_norm, "query_norm"), (key_norm, "key_norm")):
+        _check(t.is_cuda, f"{name} must be a CUDA tensor")
+    _check(query.dim() == 4 and key.dim() == 4, "Q/K must be 4D tensors")
+    _check(query.stride(-1) == 1 and key.stride(-1) == 1, "Q/K last dim must be contiguous")
+    _check(query_output.is_contiguous() and key_output.is_contiguous()
+           and query_scale.is_contiguous() and key_scale.is_contiguous(),
+           "outputs and scales must be contiguous")
+    _check(query_output.dtype == torch.int8 and key_output.dtype == torch.int8,
+           "Q/K outputs must be int8")
+    _check(query_scale.dtype == torch.float32 and key_scale.dtype == torch.float32,
+           "Q/K scales must be float32")
+    _check(query.dtype == key.dtype, "Q/K dtypes must match")
+    _check(query_norm.dtype == query.dtype and key_norm.dtype == query.dtype,
+           "Q/K norm weights must match the input dtype")
+    _check(query_block_size == 64 and query_warp_block_size == 16 and key_block_size == 64,
+           "fused Q/K preprocessing requires the production 64/16/64 quantization contract")
+    _check(norm_scope in (0, 1), "norm_scope must be 0 (per head) or 1 (whole row)")
+    head_dim = query.size(3)
+    _check(head_dim in (64, 128), "fused Q/K preprocessing requires head_dim 64 or 128")
+    _check(key.size(3) == head_dim and query.size(0) == key.size(0), "Q/K shapes are incompatible")
+    B, qh, ql, _, qsb, qsh, qsl = _geometry(query, int(tensor_layout))
+    _, kh, kl, _, ksb, ksh, ksl = _geometry(key, int(tensor_layout))
+    _check(rot_dim >= 0 and rot_dim <= head_dim and rot_dim % 2 == 0,
+           "rot_dim must be even and within head_dim")
+    _check(query_norm.numel() == (head_dim if norm_scope == 0 else qh * head_dim)
+           and key_norm.numel() == (head_dim if norm_scope == 0 else kh * head_dim),
+           "Q/K norm weight shapes are incompatible")
+    _check(query_output.shape == query.shape and key_output.shape == key.shape,
+           "Q/K output shapes must match inputs")
+    qsl_len, ksl_len = (ql + 63) // 64 * 4, (kl + 63) // 64
+    _check(tuple(query_scale.shape) == (B, qh, qsl_len), "Q scale shape is incompatible")
+    _check(tuple(key_scale.shape) == (B, kh, ksl_len), "K scale shape is incompatible")
+    fstr, fb, fs = None, 1, 1
+    if rot_dim > 0:
+        _check(freqs.is_cuda and freqs.dim() == 6, "freqs must be a 6D CUDA tensor")
+        _check(freqs.dtype == query.dtype, "RoPE frequencies must match Q/K dtype")
+        _check(freqs.size(2) == 1 and freqs.size(3) == rot_dim // 2 and freqs.size(4) == 2
+               and freqs.size(5) == 2, "RoPE frequency shape is incompatible")
+        fb, fs = freqs.size(0), freqs.size(1)
+        _check((fb == 1 or fb == B) and (fs == 1 or (fs == ql and ql == kl)),
+               "RoPE batch/sequence broadcasting is incompatible")
+        fstr = torch.tensor([freqs.stride(0), freqs.stride(1), freqs.stride(3), freqs.stride(4),
+                             freqs.stride(5)], dtype=torch.int64)
+    if norm_scope == 1:
+        _check(query_rrms.is_cuda and key_rrms.is_cuda and query_rrms.dtype == torch.float32
+               and key_rrms.dtype == torch.float32, "row RRMS scratch must be float32 CUDA")
+        _check(query_rrms.numel() == B * ql and key_rrms.numel() == B * kl,
+               "row RRMS scratch shapes are incompatible")
+    # The kernel reads the weights as 16-byte packs: give it an aligned copy of
+    # a weight view that starts mid-allocation.
+    if query_norm.data_ptr() % 16:
+        query_norm = query_norm.clone()
+    if key_norm.data_ptr() % 16:
+        key_norm = key_norm.clone()
+    qo = _geometry(query_output, int(tensor_layout))
+    ko = _geometry(key_output, int(tensor_layout))
+    strides = torch.tensor([qsb, qsh, qsl, ksb, ksh, ksl, qo[4], qo[5], qo[6], ko[4], ko[5], ko[6],
+                            query_scale.stride(0), query_scale.stride(1), key_scale.stride(0),
+                            key_scale.stride(1)], dtype=torch.int64)
+    with torch.cuda.device(query.device):
+        call("tb_quant_qk_rms_rope_int8", ptr(query), ptr(key), ptr(query_output),
+             ptr(key_output), ptr(query_scale), ptr(key_scale), ptr(query_norm), ptr(key_norm),
+             ptr(freqs) if rot_dim > 0 else None,
+             ptr(query_rrms) if norm_scope == 1 else None,
+             ptr(key_rrms) if norm_scope == 1 else None, B, qh, kh, ql, kl, head_dim,
+             strides.data_ptr(), None if fstr is None else fstr.data_ptr(), fb, fs, int(rot_dim),
+             int(norm_scope), int(bool(split_half)), dtype_code(query), float(epsilon),
+             stream_of(query))

@@ -2,6 +2,10 @@
 core.py:367-653): split prequantize / execute, head-dim padding, output
 slicing, the same dataclass and validation messages.
 
+The fused RMSNorm + RoPE Q/K prologue (core.py:222-285, 477-517) feeds the
+same attention: prequantize_rms_rope_qk -> PrequantizedQK ->
+prequantize_sageattn_from_qk -> sageattn_from_prequantized.
+
 Differences from the reference, by design:
   * no short-sequence SDPA fallback: the sm_100a kernel masks any length;
   * smooth_k=True is accepted (K mean smoothing, softmax-invariant); the
@@ -31,6 +35,18 @@ class PrequantizedSageAttention:
     original_head_dim: int
     is_causal: bool
     sm_scale: float
+
+
+@dataclass(frozen=True, slots=True)
+class PrequantizedQK:
+    query_int8: torch.Tensor
+    query_scale: torch.Tensor
+    key_int8: torch.Tensor
+    key_scale: torch.Tensor
+    tensor_layout: str
+    input_dtype: torch.dtype
+    original_head_dim: int
+    route_original_basis: bool = False
 
 
 def _on_input_device(function):
@@ -147,3 +163,77 @@ def sageattn(q, k, v, tensor_layout: str = "HND", is_causal: bool = False,
                                                  is_causal=is_causal, sm_scale=sm_scale,
                                                  smooth_k=smooth_k)
     return sageattn_from_prequantized(quantized, return_lse=return_lse)
+
+
+@_on_input_device
+def prequantize_rms_rope_qk(q, k, q_norm, k_norm, freqs, *, epsilon: float, rot_dim: int,
+                            tensor_layout: str = "HND", norm_scope: str = "head",
+                            split_half: bool = False, rotate_qk: bool = False,
+                            stabilize_k: bool = False) -> PrequantizedQK:
+    """Normalize, rotate (RoPE) and quantize Q/K in one pass without
+    materializing the 16-bit intermediates (core.py:222-285).  The
+    Hadamard-rotated variant (rotate_qk) feeds only the W8A8 attention, which
+    is not part of this package, and is rejected."""
+    if not q.is_cuda or not k.is_cuda:
+        raise ValueError("Q/K inputs must be on CUDA")
+    if q.device != k.device:
+        raise ValueError("Q/K inputs must share one CUDA device")
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype:
+        raise TypeError("fused Q/K preprocessing requires matching FP16 or BF16 inputs")
+    if q.ndim != 4 or k.ndim != 4 or q.shape[0] != k.shape[0] or q.shape[-1] != k.shape[-1]:
+        raise ValueError("fused Q/K preprocessing requires compatible four-dimensional tensors")
+    if q.stride(-1) != 1 or k.stride(-1) != 1:
+        raise ValueError("the last Q/K dimension must be contiguous")
+    head_dim = int(q.shape[-1])
+    if head_dim not in (64, 128):
+        raise ValueError("fused Q/K preprocessing requires head_dim 64 or 128")
+    if rotate_qk:
+        raise ValueError("the Hadamard-rotated Q/K preprocessing (rotate_qk) is not built in "
+                         "this package")
+    q_norm = q_norm.to(device=q.device, dtype=q.dtype).contiguous()
+    k_norm = k_norm.to(device=q.device, dtype=q.dtype).contiguous()
+    if freqs is None:
+        freqs = torch.empty(0, device=q.device, dtype=q.dtype)
+    else:
+        freqs = freqs.to(device=q.device, dtype=q.dtype)
+    from .custom_ops import qk_rms_rope_int8
+
+    q_int8, q_scale, k_int8, k_scale = qk_rms_rope_int8(
+        q, k, q_norm, k_norm, freqs, epsilon=float(epsilon), rot_dim=int(rot_dim),
+        tensor_layout=tensor_layout, norm_scope=norm_scope, split_half=bool(split_half),
+        rotate_qk=False, stabilize_k=bool(stabilize_k))
+    return PrequantizedQK(q_int8, q_scale, k_int8, k_scale, tensor_layout, q.dtype, head_dim,
+                          False)
+
+
+def prequantize_sageattn_from_qk(qk: PrequantizedQK, value: torch.Tensor, *,
+                                 is_causal: bool = False,
+                                 sm_scale: Optional[float] = None) -> PrequantizedSageAttention:
+    """Attach V to a fused Q/K result without rereading Q/K (core.py:477-517).
+    Head dims below 128 are zero-padded: zero INT8 codes add nothing to QK^T."""
+    if qk.tensor_layout not in {"HND", "NHD"}:
+        raise ValueError(f"Unsupported tensor_layout: {qk.tensor_layout}")
+    if value.dtype != qk.input_dtype:
+        raise TypeError("preprocessed Q/K and V must have matching logical dtypes")
+    if value.device != qk.query_int8.device:
+        raise ValueError("preprocessed Q/K and V must share one CUDA device")
+    if value.ndim != 4 or value.stride(-1) != 1:
+        raise ValueError("preprocessed Sage V must be four-dimensional with contiguous channels")
+    head_axis = 1 if qk.tensor_layout == "HND" else 2
+    seq_axis = 2 if qk.tensor_layout == "HND" else 1
+    if (value.size(0) != qk.key_int8.size(0)
+            or value.size(head_axis) != qk.key_int8.size(head_axis)
+            or value.size(seq_axis) != qk.key_int8.size(seq_axis)
+            or value.size(-1) != qk.key_int8.size(-1)):
+        raise ValueError("preprocessed Q/K and V shapes are incompatible")
+    scale = float(sm_scale) if sm_scale is not None else qk.original_head_dim ** -0.5
+    q_int8, k_int8 = qk.query_int8, qk.key_int8
+    padding = 128 - value.size(-1)
+    if padding:
+        q_int8 = torch.nn.functional.pad(q_int8, (0, padding))
+        k_int8 = torch.nn.functional.pad(k_int8, (0, padding))
+        value = torch.nn.functional.pad(value, (0, padding))
+    return PrequantizedSageAttention(q_int8, qk.query_scale, k_int8, qk.key_scale,
+                                     value.contiguous(), qk.tensor_layout,
+                                     qk.original_head_dim, bool(is_causal), scale)
+

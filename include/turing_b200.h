@@ -175,6 +175,32 @@ TB_API int tb_int4_linear(const int8_t *activation_packed, const int8_t *weight_
                           int8_t *weight_workspace, int64_t workspace_rows, void *output,
                           int64_t m, int64_t n, int64_t k, int64_t ldo, tb_stream_t stream);
 
+/* Fused Q/K prologue of the Sage path: RMSNorm (norm_scope 0: over each head's
+ * D channels with weight [D]; 1: over all heads of the token with weight
+ * [heads * D], rrms scratch query_rrms [B, Lq] / key_rrms [B, Lk]), RoPE as
+ * 2x2 rotations from freqs [freq_batches, freq_sequence, 1, rot_dim/2, 2, 2]
+ * (freq_strides: batch, sequence, pair, row, col in elements; split_half
+ * pairs (p, p + rot_dim/2), else (2p, 2p+1)), then INT8 quantization with the
+ * Sage scale layout: Q per 16-token tile into query_scale [B, Hq, ceil(Lq/64)*4],
+ * K per 64-token block into key_scale [B, Hk, ceil(Lk/64)]; codes clamped to
+ * +-127.  strides (elements, 16 values): q (b, h, l), k (b, h, l), q_out
+ * (b, h, l), k_out (b, h, l), q_scale (b, h), k_scale (b, h); the last
+ * dimension is contiguous; Q/K and the norm weights start on 16-byte
+ * boundaries, strides are multiples of 8 elements and the INT8 outputs start
+ * on 8-byte boundaries.  head_dim 64 or 128, dtype BF16 / F16.  Replaces
+ * quant_qk_rms_rope_int8_cuda without the Hadamard/anchor options
+ * (kernel/csrc/turing/sage/qk_preprocess.cu:566-753, fused.h:80). */
+TB_API int tb_quant_qk_rms_rope_int8(const void *query, const void *key, int8_t *query_out,
+                                     int8_t *key_out, float *query_scale, float *key_scale,
+                                     const void *query_norm, const void *key_norm,
+                                     const void *freqs, float *query_rrms, float *key_rrms,
+                                     int64_t batch, int64_t query_heads, int64_t key_heads,
+                                     int64_t query_length, int64_t key_length, int64_t head_dim,
+                                     const int64_t *strides, const int64_t *freq_strides,
+                                     int64_t freq_batches, int64_t freq_sequence, int64_t rot_dim,
+                                     int norm_scope, int split_half, int dtype, float epsilon,
+                                     tb_stream_t stream);
+
 /* ---------------------------------------------------- norm + AdaLN ---- */
 
 /* Segmented RMSNorm + AdaLN: out[r, k] = T(x[r,k] * rsqrt(mean_k x^2 + eps) *

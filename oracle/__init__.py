@@ -64,6 +64,9 @@ def lib() -> ctypes.CDLL:
         L.orc_sage_quant.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ptr,
                                      _i64, _ptr, _ptr]
         L.orc_token_mean.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _ptr]
+        L.orc_qk_rms_rope.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64,
+                                      _i64, _i64, _int, _int, _int, _int, ctypes.c_float, _ptr,
+                                      _ptr]
         L.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         L.orc_e4m3_to_f32.restype = ctypes.c_float
         for name in ("orc_f32_to_bf16", "orc_bf16_to_f32", "orc_f32_to_f16", "orc_f16_to_f32"):
@@ -258,6 +261,38 @@ def token_mean(x_bits: np.ndarray, *, layout: str = "HND", fp16: bool = False) -
     out = np.empty((B, H, D), np.uint16)
     lib().orc_token_mean(_p(x), int(fp16), B * H, L, D, L * D, D, _p(out))
     return out
+
+
+def qk_rms_rope_int8(x_bits: np.ndarray, norm_bits: np.ndarray, freqs_bits, *, tile_tokens: int,
+                     eps: float, rot_dim: int, layout: str = "HND", norm_scope: str = "head",
+                     split_half: bool = False, fp16: bool = False):
+    """Fused RMSNorm + RoPE + INT8 of one of Q (tile_tokens 16, per-warp
+    layout) / K (64) (kernel/csrc/turing/sage/qk_preprocess.cu:151-201,
+    :203-251, :417-563).  x_bits [B, H, L, D] (HND) or [B, L, H, D] (NHD);
+    norm_bits [D] or [H*D]; freqs_bits [fb, fs, 1, rot_dim/2, 2, 2] or None.
+    Returns (codes int8 in the input layout, scale fp32 [B, H, tiles])."""
+    x = _c(x_bits, np.uint16)
+    if layout == "NHD":
+        x = np.ascontiguousarray(x.transpose(0, 2, 1, 3))
+    elif layout != "HND":
+        raise ValueError(f"Unknown tensor layout: {layout}")
+    B, H, L, D = x.shape
+    tiles = (L + 63) // 64 * (64 // tile_tokens)
+    f = None
+    fb = fs = 1
+    if rot_dim > 0:
+        f = _c(freqs_bits, np.uint16)
+        fb, fs = f.shape[0], f.shape[1]
+        f = np.ascontiguousarray(f.reshape(fb, fs, rot_dim // 2, 2, 2))
+    n = _c(norm_bits, np.uint16).reshape(-1)
+    out = np.empty(x.shape, np.int8)
+    scale = np.empty((B, H, tiles), np.float32)
+    lib().orc_qk_rms_rope(_p(x), _p(n), None if f is None else _p(f), B, H, L, D, tile_tokens,
+                          tiles, fb, fs, int(rot_dim), int(bool(split_half)),
+                          int(norm_scope == "row"), int(fp16), float(eps), _p(out), _p(scale))
+    if layout == "NHD":
+        out = np.ascontiguousarray(out.transpose(0, 2, 1, 3))
+    return out, scale
 
 
 def q_scale_shape(B, H, L, block=64, warp=16):

@@ -413,6 +413,140 @@ void orc_token_mean(const uint16_t *x, int in_fp16, int64_t outer, int64_t L, in
     }
 }
 
+/* ------------------------------------------ fused RMSNorm + RoPE + INT8 -- */
+
+/* Correctly rounded 1/sqrt(y) for y > 0 (the value __frsqrt_rn returns):
+ * formed in double, whose 29 extra bits leave a wrong final rounding only
+ * when 1/sqrt(y) lies within 2^-53 (relative) of a float rounding boundary. */
+static inline float rsqrt_rn(float y) { return (float)(1.0 / sqrt((double)y)); }
+
+static inline float round_elem(float v, int fp16) {
+    return fp16 ? f16_to_f32(f32_to_f16_rn(v)) : bf16_to_f32(f32_to_bf16_rn(v));
+}
+
+static inline float elem(const uint16_t *p, int64_t i, int fp16) {
+    return fp16 ? f16_to_f32(p[i]) : bf16_to_f32(p[i]);
+}
+
+/* Row-scope RRMS of token (b, tok) over all H heads, summed in the CUDA
+ * block's order (kernel/csrc/turing/sage/qk_preprocess.cu:203-251 with
+ * reduction_utils.cuh:70-87): 256 per-thread FMA chains over i = h*D + c
+ * strided by 256, an XOR butterfly inside each 32-lane warp, then an XOR
+ * butterfly over the 8 warp partials padded with zeros to 32 lanes. */
+static float row_rrms(const uint16_t *x, int64_t H, int64_t L, int64_t D, int64_t b,
+                      int64_t tok, int fp16, float eps) {
+    float lanes[256], w[32];
+    const int64_t n = H * D;
+    for (int t = 0; t < 256; ++t) {
+        float s = 0.0f;
+        for (int64_t i = t; i < n; i += 256) {
+            const int64_t h = i / D, c = i - h * D;
+            const float v = elem(x, ((b * H + h) * L + tok) * D + c, fp16);
+            s = fmaf(v, v, s);
+        }
+        lanes[t] = s;
+    }
+    for (int wp = 0; wp < 8; ++wp) {
+        float *l = lanes + wp * 32, tmp[32];
+        for (int o = 16; o > 0; o >>= 1) {
+            for (int i = 0; i < 32; ++i) tmp[i] = l[i] + l[i ^ o];
+            memcpy(l, tmp, sizeof(tmp));
+        }
+        w[wp] = l[0];
+    }
+    for (int i = 8; i < 32; ++i) w[i] = 0.0f;
+    for (int o = 16; o > 0; o >>= 1) {
+        float tmp[32];
+        for (int i = 0; i < 32; ++i) tmp[i] = w[i] + w[i ^ o];
+        memcpy(w, tmp, sizeof(tmp));
+    }
+    return rsqrt_rn(w[0] / (float)n + eps);
+}
+
+/* Head-scope RRMS of one token row (qk_preprocess.cu:505-515): an 8-channel
+ * FMA chain per pack, then an XOR butterfly over the D/8 packs. */
+static float head_rrms(const uint16_t *row, int64_t D, int fp16, float eps) {
+    float p[16], tmp[16];
+    const int P = (int)(D / 8);
+    for (int k = 0; k < P; ++k) {
+        float s = 0.0f;
+        for (int c = 0; c < 8; ++c) {
+            const float v = elem(row, k * 8 + c, fp16);
+            s = fmaf(v, v, s);
+        }
+        p[k] = s;
+    }
+    for (int o = P / 2; o > 0; o >>= 1) {
+        for (int i = 0; i < P; ++i) tmp[i] = p[i] + p[i ^ o];
+        memcpy(p, tmp, sizeof(float) * (size_t)P);
+    }
+    return rsqrt_rn(p[0] / (float)D + eps);
+}
+
+/* Fused RMSNorm + RoPE + per-tile INT8 quantization of one of Q/K
+ * (qk_preprocess.cu:151-201 per element, :417-563 per tile).
+ * x: [B, H, L, D] contiguous bits; norm: [D] (head scope) or [H*D] (row);
+ * freqs: [fb, fs, rot_dim/2, 2, 2] contiguous bits or NULL (rot_dim 0).
+ * T tokens per tile, tiles scale entries per (b, h) (empty tiles get the
+ * 1e-7 floor).  Per element: n = T(x * rrms * w); RoPE pairs (2p, 2p+1) or,
+ * split-half, (p, p + rot_dim/2): v = T(fma(f[row][1], n1, f[row][0] * n0));
+ * per tile amax = max(1e-7, max|v|), scale = amax / 127,
+ * q = clamp(rint(v * (127 / amax)), -127, 127), IEEE divides. */
+void orc_qk_rms_rope(const uint16_t *x, const uint16_t *norm, const uint16_t *freqs, int64_t B,
+                     int64_t H, int64_t L, int64_t D, int64_t T, int64_t tiles, int64_t fb,
+                     int64_t fs, int rot_dim, int split_half, int row_scope, int fp16, float eps,
+                     int8_t *out, float *scale) {
+    const int half = rot_dim / 2;
+    float *vals = (float *)malloc(sizeof(float) * (size_t)(T * D));
+    float *nrm = (float *)malloc(sizeof(float) * (size_t)D);
+    for (int64_t b = 0; b < B; ++b) {
+        for (int64_t h = 0; h < H; ++h) {
+            const uint16_t *w = norm + (row_scope ? h * D : 0);
+            for (int64_t t = 0; t < tiles; ++t) {
+                float amax = 0.0000001f;
+                for (int64_t i = 0; i < T; ++i) {
+                    const int64_t tok = t * T + i;
+                    if (tok >= L) break;
+                    const uint16_t *row = x + ((b * H + h) * L + tok) * D;
+                    const float rrms = row_scope ? row_rrms(x, H, L, D, b, tok, fp16, eps)
+                                                 : head_rrms(row, D, fp16, eps);
+                    for (int64_t c = 0; c < D; ++c)
+                        nrm[c] = round_elem(elem(row, c, fp16) * rrms * elem(w, c, fp16), fp16);
+                    for (int64_t c = 0; c < D; ++c) {
+                        float v = nrm[c];
+                        if (c < rot_dim) {
+                            const int64_t pair = split_half ? (c < half ? c : c - half) : c / 2;
+                            const int64_t first = split_half ? pair : 2 * pair;
+                            const int64_t second = split_half ? pair + half : first + 1;
+                            const int64_t comp = split_half ? (c >= half) : (c & 1);
+                            const int64_t fbase = (((fb == 1 ? 0 : b) * fs + (fs == 1 ? 0 : tok)) *
+                                                       half + pair) * 4 + comp * 2;
+                            const float f0 = elem(freqs, fbase, fp16);
+                            const float f1 = elem(freqs, fbase + 1, fp16);
+                            v = round_elem(fmaf(f1, nrm[second], f0 * nrm[first]), fp16);
+                        }
+                        vals[i * D + c] = v;
+                        amax = fmaxf(amax, fabsf(v));
+                    }
+                }
+                scale[(b * H + h) * tiles + t] = amax / 127.0f;
+                const float inv = 127.0f / amax;
+                for (int64_t i = 0; i < T; ++i) {
+                    const int64_t tok = t * T + i;
+                    if (tok >= L) break;
+                    for (int64_t c = 0; c < D; ++c) {
+                        const float r = nearbyintf(vals[i * D + c] * inv);
+                        out[((b * H + h) * L + tok) * D + c] =
+                            (int8_t)fminf(127.0f, fmaxf(-127.0f, r));
+                    }
+                }
+            }
+        }
+    }
+    free(vals);
+    free(nrm);
+}
+
 /* ------------------------------------------------------------ helpers ---- */
 
 void orc_f32_to_bf16(const float *x, int64_t n, uint16_t *out) {

@@ -12,5 +12,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::overload_cast<at::Tensor, at::Tensor, at::Tensor, int, int>(&quant_per_block_int8_cuda));
   m.def("quant_per_warp_int8_cuda",
         py::overload_cast<at::Tensor, at::Tensor, at::Tensor, int, int, int>(&quant_per_warp_int8_cuda));
+  m.def("quant_qk_rms_rope_int8_cuda", &quant_qk_rms_rope_int8_cuda);
   m.def("qk_int8_sv_f16_accum_f32_attn", &qk_int8_sv_f16_accum_f32_attn);
 }

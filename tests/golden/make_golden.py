@@ -2,7 +2,7 @@
 own CUDA kernels (built from its sources by oracle/ref/build_ref.py into
 oracle/_ref) on seeded CPU-generated inputs, on a B200.
 
-    python tests/golden/make_golden.py [out_dir] [--only norm]
+    python tests/golden/make_golden.py [out_dir] [--only norm|qkrope]
 
 Each fixture is a compressed .npz holding the inputs (as raw bits) and the
 reference's outputs.  tests/test_oracle_golden.py checks the CPU oracle
@@ -74,8 +74,66 @@ def norm_fixtures(dev, L) -> dict:
     return fx
 
 
+def rope_freqs(fb, fs, pairs, seed, dtype):
+    """[fb, fs, 1, pairs, 2, 2] rotation matrices [[cos, -sin], [sin, cos]]."""
+    g = torch.Generator().manual_seed(seed)
+    ang = torch.rand((fb, fs, 1, pairs, 1, 1), generator=g) * 6.283
+    c, s = torch.cos(ang), torch.sin(ang)
+    return torch.cat([torch.cat([c, -s], -1), torch.cat([s, c], -1)], -2).to(dtype)
+
+
+# (name, dtype, layout, B, Hq, Hk, Lq, Lk, D, scope, split, rot_dim, fb, fs)
+QKROPE_CASES = [
+    ("bf16_hnd_d128_head", torch.bfloat16, "HND", 1, 3, 3, 150, 150, 128, "head", False, 128, 1, 150),
+    ("f16_nhd_d64_row_split", torch.float16, "NHD", 2, 4, 2, 77, 77, 64, "row", True, 32, 2, 77),
+    ("bf16_hnd_d64_norope", torch.bfloat16, "HND", 2, 2, 2, 70, 200, 64, "head", False, 0, 1, 1),
+    ("bf16_nhd_d128_row", torch.bfloat16, "NHD", 1, 5, 5, 64, 64, 128, "row", False, 96, 1, 1),
+]
+
+
+def qkrope_fixtures(dev, S) -> dict:
+    """Fused RMSNorm + RoPE + INT8 Q/K (sage/qk_preprocess.cu:566-753)."""
+    fx = {}
+    for i, (name, dt, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs) in \
+            enumerate(QKROPE_CASES):
+        g = torch.Generator().manual_seed(300 + i)
+        qshape = (B, hq, lq, D) if layout == "HND" else (B, lq, hq, D)
+        kshape = (B, hk, lk, D) if layout == "HND" else (B, lk, hk, D)
+        q = (torch.randn(qshape, generator=g) * 1.5 + 0.2).to(dt)
+        k = (torch.randn(kshape, generator=g) * 0.8 - 0.3).to(dt)
+        nq, nk = (D if scope == "head" else hq * D), (D if scope == "head" else hk * D)
+        qn = (torch.rand((nq,), generator=g) + 0.5).to(dt)
+        kn = (torch.rand((nk,), generator=g) + 0.5).to(dt)
+        fr = rope_freqs(fb, fs, rot // 2, 400 + i, dt) if rot else torch.empty(0, dtype=dt)
+        qd, kd, qnd, knd, frd = (t.to(dev) for t in (q, k, qn, kn, fr))
+        q8 = torch.empty(qshape, dtype=torch.int8, device=dev)
+        k8 = torch.empty(kshape, dtype=torch.int8, device=dev)
+        qs = torch.empty((B, hq, (lq + 63) // 64 * 4), dtype=torch.float32, device=dev)
+        ks = torch.empty((B, hk, (lk + 63) // 64), dtype=torch.float32, device=dev)
+        qr = torch.empty((B, lq) if scope == "row" else (0,), dtype=torch.float32, device=dev)
+        kr = torch.empty((B, lk) if scope == "row" else (0,), dtype=torch.float32, device=dev)
+        e_i = torch.empty(0, dtype=torch.int32, device=dev)
+        e_f = torch.empty(0, dtype=torch.float32, device=dev)
+        S.quant_qk_rms_rope_int8_cuda(qd, kd, q8, k8, qs, ks, qnd, knd, frd, qr, kr, e_i, e_f,
+                                      1e-6, rot, 64, 16, 64, 1 if layout == "HND" else 0,
+                                      1 if scope == "row" else 0, split, False)
+        torch.cuda.synchronize()
+        fx[f"qkrope_{name}"] = {
+            "q": bits(q), "k": bits(k), "qn": bits(qn), "kn": bits(kn), "freqs": bits(fr),
+            "params": np.array([rot, int(split), int(scope == "row"), int(dt == torch.float16),
+                                int(layout == "NHD")], np.int64),
+            "q8": bits(q8), "qs": bits(qs), "k8": bits(k8), "ks": bits(ks)}
+    return fx
+
+
 def main(out_dir: Path, only: str = "") -> None:
     out_dir.mkdir(parents=True, exist_ok=True)
+    if only == "qkrope":
+        fx = qkrope_fixtures(torch.device("cuda:0"), R.sage())
+        for name, rec in fx.items():
+            np.savez_compressed(out_dir / f"{name}.npz", **rec)
+        print(f"wrote {len(fx)} fixtures to {out_dir}")
+        return
     if only == "norm":
         fx = norm_fixtures(torch.device("cuda:0"), R.linear())
         for name, rec in fx.items():
