@@ -23,7 +23,7 @@ from .ops import (
     turing_swiglu_int8_convrot_quantize,
     turing_w4a8_linear,
 )
-from . import turing_sage
+from . import checkpoint, turing_sage
 
 __version__ = "0.29.1"
 
