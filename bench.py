@@ -595,14 +595,129 @@ class AttentionRopeWorkload(AttentionWorkload):
                        "those rows and all 32760 keys, then fp32 SDPA")
 
 
+class DiTBlockWorkload:
+    """one Wan2.1-14B-shaped DiT block (dim 5120, 40 heads
+    of 128, FFN 13824, L = 75600 video tokens, 512 text tokens, batch 1) on
+    W8A8 ConvRot linears, the fused Q/K prologue and Sage INT8 attention,
+    tensor-parallel over the torchrun ranks (comfyui_turing_utils_kernel.
+    dit_block).  Metric: block tokens/s = L / block time, max over ranks."""
+    name = "dit_block"
+    unit = "tokens/s"
+    unit_scale = 1.0
+    scaling = "strong"
+    n_events = 4          # step start, self-attention start, end, step end
+    dominant = "sage_attn"
+
+    def __init__(self, device, world=1, rank=0, tokens=None, cpu_only=False):
+        from comfyui_turing_utils_kernel import dit_block as db
+
+        self.db = db
+        self.cfg = db.BlockConfig()
+        self.L, self.Lc = tokens or 75600, 512
+        self.world, self.rank = world, rank
+        self.plan = db.shard_plan(self.cfg, world, rank)
+        self.ops = db.block_ops(self.cfg, self.L, self.Lc)  # whole block, all ranks
+        self.work = float(self.L)                             # tokens per step
+        self.config = {"workload": "Wan2.1-14B DiT block (BASELINE configs[4])",
+                       "dim": self.cfg.dim, "heads": self.cfg.heads, "head_dim": self.cfg.head_dim,
+                       "ffn": self.cfg.ffn, "tokens": self.L, "text_tokens": self.Lc, "batch": 1,
+                       "block_tops_per_step": round(self.ops / 1e12, 2),
+                       "linears": "W8A8 ConvRot, per-channel weights", "attention": "Sage INT8",
+                       "norms": "LayerNorm+AdaLN; row RMSNorm + RoPE fused into Q/K INT8"}
+        if cpu_only:
+            return
+        import torch.distributed as tdist
+
+        self.weights = db.make_weights(self.cfg, self.plan, seed=0, device=device)
+        g = torch.Generator(device=device).manual_seed(1)
+        self.x = torch.randn((self.L, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
+        self.ctx = torch.randn((self.Lc, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
+        self.freqs = db.rope_freqs(self.L, self.cfg.head_dim, seed=2, device=device)
+        self.kops = db.KernelOps()
+        self.block = db.DiTBlock(self.cfg, self.weights, self.plan, self.kops,
+                                 group=tdist.group.WORLD if world > 1 else None)
+        self.host = [t.cpu().pin_memory() for t in (self.x, self.ctx)]
+        self.out_host = torch.empty_like(self.host[0]).pin_memory()
+        self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
+        self.d2h_bytes = self.out_host.numel() * 2
+        before = self.kops.launches
+        self.block.forward(self.x, self.ctx, self.freqs)
+        self.launches_per_step = self.kops.launches - before
+
+    def parallelism(self, world):
+        return (f"tensor parallel x{world}: heads {list(self.plan.heads)}, FFN columns "
+                f"{list(self.plan.ffn)}; NCCL all-reduce after O, cross-O and FFN-down "
+                "(bf16) and of the Q/K row sums of squares (fp32)") if world > 1 else "1 GPU"
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+            self.kops.event_pair = (ev[1], ev[2])
+        out = self.block.forward(self.x, self.ctx, self.freqs)
+        if ev:
+            ev[3].record()
+            self.kops.event_pair = None
+        return out
+
+    def step_e2e(self):
+        dev = self.x.device
+        x, ctx = (t.to(dev, non_blocking=True) for t in self.host)
+        out = self.block.forward(x, ctx, self.freqs)
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+    def roofline(self, dom_ms, peaks):
+        int8_peak = 2.0 * peaks["bf16_tflops"]
+        ops = 4.0 * self.plan.nheads * self.L * self.L * self.cfg.head_dim
+        achieved = ops / (dom_ms * 1e-3) / 1e12
+        return {"kernel": "sage_attn (self-attention of this rank's heads)", "bound": "tensor",
+                "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
+                "frac": round(achieved / int8_peak, 4),
+                "peak_source": f"2 x {peaks['source']} dense bf16 TFLOP/s (MEASURED_PEAKS.json)",
+                "kernel_ms": round(dom_ms, 4)}
+
+    def prepare_cpu(self):
+        d, f, H, D = self.cfg.dim, self.cfg.ffn, self.cfg.heads, self.cfg.head_dim
+        g = torch.Generator().manual_seed(5)
+        # fp32 weights of every linear a token passes (values do not change the time).
+        self.cpu_w = [torch.randn((n, k), generator=g) * 0.02
+                      for n, k in ((3 * d, d), (d, d), (d, d), (d, d), (f, d), (d, f))]
+        self.cpu_kv = [torch.randn((1, H, self.L, D), generator=g) for _ in range(2)]
+        self.cpu_ckv = [torch.randn((1, H, self.Lc, D), generator=g) for _ in range(2)]
+
+    def cpu_reference_step(self, rows: int):
+        """`rows` tokens through the block's fp32 path: every linear, the
+        self-attention of those query rows against all L keys and the
+        cross-attention against the 512 text keys (LayerNorm, GELU and the
+        per-block text K/V projection are under 0.1 % of the work)."""
+        rows = min(rows, 32)
+        d, H, D = self.cfg.dim, self.cfg.heads, self.cfg.head_dim
+        x = torch.randn((rows, d))
+        wqkv, wo, wcq, wco, wup, wdown = self.cpu_w
+        qkv = x @ wqkv.t()
+        q = qkv[:, :d].reshape(rows, H, D).transpose(0, 1)[None]
+        a = torch.nn.functional.scaled_dot_product_attention(q, *self.cpu_kv)
+        x = x + a[0].transpose(0, 1).reshape(rows, d) @ wo.t()
+        cq = (x @ wcq.t()).reshape(rows, H, D).transpose(0, 1)[None]
+        a = torch.nn.functional.scaled_dot_product_attention(cq, *self.cpu_ckv)
+        x = x + a[0].transpose(0, 1).reshape(rows, d) @ wco.t()
+        x = x + torch.nn.functional.gelu(x @ wup.t(), approximate="tanh") @ wdown.t()
+        return x, float(rows)  # tokens
+
+    cpu_sample_desc = ("tokens through the fp32 block path (all linears; self-attention "
+                       "against all 75600 keys; cross-attention against 512 text keys)")
+
+
 WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload,
-             "attention_rope": AttentionRopeWorkload,
+             "attention_rope": AttentionRopeWorkload, "dit_block": DiTBlockWorkload,
              "codebook": CodebookWorkload, "w4a4_ffn": W4A4FFNWorkload}
 
 
-def make_workload(args, device, seed):
+def make_workload(args, device, seed, world=1, rank=0):
     if args.workload in ("attention", "attention_rope"):
         return WORKLOADS[args.workload](device, seed, heads=args.heads)
+    if args.workload == "dit_block":
+        return DiTBlockWorkload(device, world, rank, tokens=args.tokens)
     return WORKLOADS[args.workload](device, seed)
 
 
@@ -656,7 +771,7 @@ def run_ours(args, world, rank, local):
     from comfyui_turing_utils_kernel import _lib
 
     device = torch.device("cuda", local)
-    wl = make_workload(args, device, seed=1000 + rank)
+    wl = make_workload(args, device, seed=1000 + rank, world=world, rank=rank)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     for _ in range(args.warmup):
         wl.step()
@@ -710,27 +825,34 @@ def run_ours(args, world, rank, local):
     if hasattr(wl, "aux_roofline"):
         pro = [ev[0].elapsed_time(ev[1]) for ev in events]
         roof.update(wl.aux_roofline(sum(pro) / len(pro), peaks))
+    unit, scale = getattr(wl, "unit", UNIT), getattr(wl, "unit_scale", 1e12)
+    # Whole-job throughput: independent shards add up (weak scaling); a
+    # tensor-parallel workload's ops are already the whole job's.
+    work = getattr(wl, "work", wl.ops)  # ops (TOPS) or tokens (tokens/s) per step
+    job = work * (1 if getattr(wl, "scaling", "weak") == "strong" else world)
     result = {
         "metric": METRIC,
-        "value": round(world * wl.ops / (ms * 1e-3) / 1e12, 2),
-        "unit": UNIT,
+        "value": round(job / (ms * 1e-3) / scale, 2),
+        "unit": unit,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded; BASELINE shapes and distributions)",
-        "config": dict(wl.config, parallelism=f"independent shards x{world} (no collective)",
+        "config": dict(wl.config, parallelism=wl.parallelism(world) if hasattr(wl, "parallelism")
+                       else f"independent shards x{world} (no collective)",
                        l2="256 MB buffer written between steps; per-step CUDA events exclude it"),
         "impl": "ours",
         "roofline": roof,
-        "e2e": {"value": round(world * wl.ops / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT,
+        "e2e": {"value": round(job / (e2e_ms * 1e-3) / scale, 2), "unit": unit,
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
                 "ms_per_step": round(e2e_ms, 4)},
         "gpu_launches": wl.launches_per_step * args.steps,
+        **({"block_tops": round(wl.ops / (ms * 1e-3) / 1e12, 1)} if wl.name == "dit_block" else {}),
         "clocks": dict(sampler.summary(), region="timed+soak" if soak else "timed"),
         "device_error": dev_err,
     }
@@ -752,7 +874,8 @@ def cpu_baseline(wl, args) -> dict:
         ops += wl.cpu_reference_step(rows)[1]
         reps += 1
     dt = time.perf_counter() - t0
-    return {"value": round(ops / dt / 1e12, 5), "unit": UNIT, "cores": cores, "kind": "port",
+    return {"value": round(ops / dt / getattr(wl, "unit_scale", 1e12), 5),
+            "unit": getattr(wl, "unit", UNIT), "cores": cores, "kind": "port",
             "sample": f"{reps} x {rows} {wl.cpu_sample_desc}",
             "seconds": round(dt, 2)}
 
@@ -760,7 +883,10 @@ def cpu_baseline(wl, args) -> dict:
 def run_reference(args, world, rank, local):
     """CPU reference arm (rank 0 only)."""
     device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
-    wl = make_workload(args, device, seed=1000)
+    if args.workload == "dit_block":
+        wl = DiTBlockWorkload(device, world, rank, tokens=args.tokens, cpu_only=True)
+    else:
+        wl = make_workload(args, device, seed=1000)
     wl.prepare_cpu()
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
@@ -773,18 +899,20 @@ def run_reference(args, world, rank, local):
         _, ops = wl.cpu_reference_step(rows)
         times.append(time.perf_counter() - t0)
         total_ops += ops
-    value = total_ops / sum(times) / 1e12
+    unit, scale = getattr(wl, "unit", UNIT), getattr(wl, "unit_scale", 1e12)
+    value = total_ops / sum(times) / scale
     ms = sum(times) / len(times) * 1e3
     sample = f"{rows} {wl.cpu_sample_desc} per step"
     return {
-        "metric": METRIC, "value": round(value, 5), "unit": UNIT, "n_gpus": world,
+        "metric": METRIC, "value": round(value, 5), "unit": unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "higher_is_better": True, "scaling": getattr(wl, "scaling", "weak"),
+        "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded; BASELINE shapes and distributions)",
         "config": dict(wl.config, parallelism="cpu"), "impl": "reference",
-        "cpu_baseline": {"value": round(value, 5), "unit": UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores, "kind": "port",
                          "sample": sample},
-        "e2e": {"value": round(value, 5), "unit": UNIT, "h2d_bytes_per_step": 0,
+        "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
@@ -799,6 +927,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="dit_block video tokens (default: the config's 75600)")
     ap.add_argument("--heads", type=int, default=None,
                     help="attention heads (default: the config's 40); smaller cases for profiling")
     args = ap.parse_args()

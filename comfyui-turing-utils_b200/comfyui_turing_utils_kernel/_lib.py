@@ -48,6 +48,7 @@ SIGNATURES: dict[str, list] = {
     "tb_quant_qk_rms_rope_int8": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                   _i64, _i64, _i64, _p, _p, _i64, _i64, _i64, _int, _int, _int,
                                   ctypes.c_float, _p],
+    "tb_row_sum_squares": [_p, _p, _i64, _i64, _i64, _i64, _p, _int, _p],
     "tb_segmented_rms_adaln": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _int,
                                ctypes.c_float, _p],
     "tb_layer_norm_adaln": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _p],

@@ -129,7 +129,8 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
            "Q/K norm weights must match the input dtype")
     _check(query_block_size == 64 and query_warp_block_size == 16 and key_block_size == 64,
            "fused Q/K preprocessing requires the production 64/16/64 quantization contract")
-    _check(norm_scope in (0, 1), "norm_scope must be 0 (per head) or 1 (whole row)")
+    _check(norm_scope in (0, 1, 2),
+           "norm_scope must be 0 (per head), 1 (whole row) or 2 (whole row, RRMS given)")
     head_dim = query.size(3)
     _check(head_dim in (64, 128), "fused Q/K preprocessing requires head_dim 64 or 128")
     _check(key.size(3) == head_dim and query.size(0) == key.size(0), "Q/K shapes are incompatible")
@@ -156,7 +157,7 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
                "RoPE batch/sequence broadcasting is incompatible")
         fstr = torch.tensor([freqs.stride(0), freqs.stride(1), freqs.stride(3), freqs.stride(4),
                              freqs.stride(5)], dtype=torch.int64)
-    if norm_scope == 1:
+    if norm_scope in (1, 2):
         _check(query_rrms.is_cuda and key_rrms.is_cuda and query_rrms.dtype == torch.float32
                and key_rrms.dtype == torch.float32, "row RRMS scratch must be float32 CUDA")
         _check(query_rrms.numel() == B * ql and key_rrms.numel() == B * kl,
@@ -176,8 +177,24 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
         call("tb_quant_qk_rms_rope_int8", ptr(query), ptr(key), ptr(query_output),
              ptr(key_output), ptr(query_scale), ptr(key_scale), ptr(query_norm), ptr(key_norm),
              ptr(freqs) if rot_dim > 0 else None,
-             ptr(query_rrms) if norm_scope == 1 else None,
-             ptr(key_rrms) if norm_scope == 1 else None, B, qh, kh, ql, kl, head_dim,
+             ptr(query_rrms) if norm_scope else None,
+             ptr(key_rrms) if norm_scope else None, B, qh, kh, ql, kl, head_dim,
              strides.data_ptr(), None if fstr is None else fstr.data_ptr(), fb, fs, int(rot_dim),
              int(norm_scope), int(bool(split_half)), dtype_code(query), float(epsilon),
              stream_of(query))
+
+
+def row_sum_squares_cuda(input, sums, tensor_layout):
+    """Per-token sum of squares over all heads of a [B, H, L, D] / [B, L, H, D]
+    tensor into sums [B, L] fp32 (tensor-parallel row RMS; norm_scope 2 of
+    quant_qk_rms_rope_int8_cuda takes the resulting RRMS).  Not in the
+    reference, whose fused prologue always owns every head."""
+    B, H, L, D, sb, sh, sl = _geometry(input, int(tensor_layout))
+    _check(D in (64, 128), "head_dim must be 64 or 128")
+    _check(sums.is_cuda and sums.dtype == torch.float32 and sums.is_contiguous()
+           and sums.numel() == B * L, "sums must be a contiguous float32 CUDA [B, L] tensor")
+    st = torch.tensor([sb, sh, sl], dtype=torch.int64)
+    with torch.cuda.device(input.device):
+        call("tb_row_sum_squares", ptr(input), ptr(sums), B, H, L, D, st.data_ptr(),
+             dtype_code(input), stream_of(input))
+

@@ -1,0 +1,382 @@
+"""Wan2.1-style DiT block on this package's kernels, with Megatron tensor
+parallelism over torch.distributed (dim 5120, 40 heads of
+128, FFN 13824, L = 75600 video tokens, 512 text tokens).
+
+The reference plugin supplies this block's pieces but not the block (its
+forward lives in ComfyUI, absent from the reference): the ConvRot quantized
+linears for q/k/v/o, cross-attention and FFN (quantization/dispatch.py,
+fusions.py:45-122 folds tanh-GELU into the FFN-down quantizer), the
+self-attention hand-off with row-scope RMSNorm + interleaved RoPE fused into
+the INT8 Q/K quantizer (adapters/wan.py:55-137), and LayerNorm + AdaLN
+(ops.py:399-418).  The block structure is the published Wan2.1 one:
+
+    h = LN(x) * (1 + scale_msa) + shift_msa
+    x = x + gate_msa * O(attn(RoPE(RMS(Q h)), RoPE(RMS(K h)), V h))
+    h = LN(x) * (1 + scale_c) + shift_c                 (affine cross-attn norm)
+    x = x + O_c(attn(RMS(Q_c h), RMS(K_c ctx), V_c ctx))
+    h = LN(x) * (1 + scale_mlp) + shift_mlp
+    x = x + gate_mlp * Down(GELU_tanh(Up h))
+
+with RMS the RMSNorm over all heads of a token (learned weight).
+
+Tensor parallelism (one process per GPU): column-parallel Q/K/V, cross
+Q/K/V and FFN-up; attention on the rank's own heads; row-parallel O, cross O
+and FFN-down, each followed by one all-reduce of the [L, dim] bf16 partial
+sums; the row-scope RMSNorm of Q and K adds an all-reduce of the per-token
+fp32 sums of squares.  A row-parallel layer's input shard must hold whole
+256-channel ConvRot groups (its Hadamard rotation and per-token INT8 scale
+are taken over the shard), so heads and FFN columns are dealt out in
+256-channel units: 40 heads on 8 ranks = 6,6,6,6,4,4,4,4.
+
+Two op backends share the block and its tensor parallelism: KernelOps (the
+sm_100a kernels; bf16 activations, INT8 ConvRot linears, INT8 attention) and
+TorchOps (fp32 torch with the same dequantized weights and no activation
+quantization: the reference's dequantize-then-compute CPU path composed,
+validate_compatible.py:110-114, 540-546).
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+GROUP = 256  # ConvRot rotation block
+
+
+@dataclasses.dataclass(frozen=True)
+class BlockConfig:
+    dim: int = 5120
+    heads: int = 40
+    head_dim: int = 128
+    ffn: int = 13824
+    eps: float = 1e-6
+
+    def __post_init__(self):
+        if self.heads * self.head_dim != self.dim:
+            raise ValueError("dim must equal heads * head_dim")
+        if self.dim % GROUP or self.ffn % GROUP:
+            raise ValueError("dim and ffn must be multiples of the 256-channel ConvRot group")
+        if self.head_dim not in (64, 128) or GROUP % self.head_dim:
+            raise ValueError("head_dim must be 64 or 128")
+
+
+def split_units(units: int, parts: int) -> list[int]:
+    """units dealt to parts as evenly as possible, the larger shares first."""
+    base, extra = divmod(units, parts)
+    return [base + (1 if r < extra else 0) for r in range(parts)]
+
+
+@dataclasses.dataclass(frozen=True)
+class ShardPlan:
+    world: int
+    rank: int
+    heads: tuple[int, ...]      # heads per rank
+    ffn: tuple[int, ...]        # FFN columns per rank
+
+    @property
+    def head0(self) -> int:
+        return sum(self.heads[: self.rank])
+
+    @property
+    def nheads(self) -> int:
+        return self.heads[self.rank]
+
+    @property
+    def ffn0(self) -> int:
+        return sum(self.ffn[: self.rank])
+
+    @property
+    def nffn(self) -> int:
+        return self.ffn[self.rank]
+
+
+def shard_plan(cfg: BlockConfig, world: int, rank: int) -> ShardPlan:
+    heads_per_unit = GROUP // cfg.head_dim
+    head_units = cfg.heads // heads_per_unit
+    ffn_units = cfg.ffn // GROUP
+    if world > head_units:
+        raise ValueError(f"{world} ranks exceed the {head_units} 256-channel head groups")
+    return ShardPlan(world, rank, tuple(u * heads_per_unit for u in split_units(head_units, world)),
+                     tuple(u * GROUP for u in split_units(ffn_units, world)))
+
+
+# ------------------------------------------------------------- weights --
+
+def hadamard256(device=None, dtype=torch.float32) -> torch.Tensor:
+    """The orthogonal, symmetric 256-point ConvRot rotation kron(M, M, M, M),
+    M = 1/2 [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]]
+    (kernel/csrc/turing/convrot_quant.cu:104-116)."""
+    m = 0.5 * torch.tensor([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]],
+                           dtype=torch.float64)
+    h = m
+    for _ in range(3):
+        h = torch.kron(h, m)
+    return h.to(device=device, dtype=dtype)
+
+
+@dataclasses.dataclass
+class QuantLinear:
+    """A ConvRot W8A8 linear y = x W^T + b: weight rotated per 256-column
+    block (W H, H the rotation above, so that (W H)(H x) = W x) and quantized
+    per output channel to INT8 with a fp32 scale."""
+    weight: torch.Tensor             # int8 [N, K]
+    scale: torch.Tensor              # fp32 [N]
+    bias: Optional[torch.Tensor]     # fp32 [N] or None
+
+    @staticmethod
+    def from_float(w: torch.Tensor, bias: Optional[torch.Tensor]) -> "QuantLinear":
+        n, k = w.shape
+        h = hadamard256(w.device)
+        wr = (w.float().reshape(n, k // GROUP, GROUP) @ h).reshape(n, k)
+        s = wr.abs().amax(dim=1).clamp_min(1e-12) / 127.0
+        q = torch.round(wr / s[:, None]).clamp_(-127, 127).to(torch.int8)
+        return QuantLinear(q.contiguous(), s.contiguous(),
+                           None if bias is None else bias.float().contiguous())
+
+    def dequantized(self) -> torch.Tensor:
+        """The fp32 weight this layer applies to unrotated inputs."""
+        n, k = self.weight.shape
+        w = self.weight.float() * self.scale[:, None]
+        return (w.reshape(n, k // GROUP, GROUP) @ hadamard256(w.device)).reshape(n, k)
+
+
+def _randn(shape, seed: int, device, std: float) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    return torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std
+
+
+@dataclasses.dataclass
+class BlockWeights:
+    qkv: QuantLinear          # rows: q, k, v of the rank's heads
+    o: QuantLinear            # columns: the rank's heads; bias on rank 0 only
+    cq: QuantLinear
+    ckv: QuantLinear          # rows: k, v of the rank's heads (applied to the context)
+    co: QuantLinear
+    up: QuantLinear           # rows: the rank's FFN columns
+    down: QuantLinear         # columns: the rank's FFN columns
+    norm_q: torch.Tensor      # RMSNorm weights of the rank's heads [nheads * head_dim]
+    norm_k: torch.Tensor
+    cnorm_q: torch.Tensor
+    cnorm_k: torch.Tensor
+    modulation: torch.Tensor  # [6, dim]: shift/scale/gate (self-attn), shift/scale/gate (FFN)
+    cross_norm: torch.Tensor  # [2, dim]: shift, scale of the affine cross-attention LayerNorm
+
+
+def make_weights(cfg: BlockConfig, plan: ShardPlan, seed: int = 0, device="cpu",
+                 dtype=torch.bfloat16) -> BlockWeights:
+    """Random-init weights N(0, 0.02), generated whole
+    from per-tensor seeds on every rank and sliced to the rank's shard, then
+    ConvRot W8A8-quantized; AdaLN modulation ~N(0, 1)."""
+    D, d, f = cfg.head_dim, cfg.dim, cfg.ffn
+    hs = slice(plan.head0 * D, (plan.head0 + plan.nheads) * D)
+    fs = slice(plan.ffn0, plan.ffn0 + plan.nffn)
+    root = plan.rank == 0
+
+    def w(i, shape):
+        return _randn(shape, seed * 1000 + i, device, 0.02)
+
+    def col(ws, bs):  # column-parallel: output rows of the rank
+        return QuantLinear.from_float(torch.cat([x[hs] for x in ws]), torch.cat([b[hs] for b in bs]))
+
+    wq, wk, wv, wo = (w(i, (d, d)) for i in range(4))
+    bq, bk, bv, bo = (w(10 + i, (d,)) for i in range(4))
+    cwq, cwk, cwv, cwo = (w(20 + i, (d, d)) for i in range(4))
+    cbq, cbk, cbv, cbo = (w(30 + i, (d,)) for i in range(4))
+    up, down = w(40, (f, d)), w(41, (d, f))
+    bup, bdown = w(42, (f,)), w(43, (d,))
+    norms = [1.0 + w(50 + i, (d,)) for i in range(4)]
+    weights = BlockWeights(
+        qkv=col([wq, wk, wv], [bq, bk, bv]),
+        o=QuantLinear.from_float(wo[:, hs], bo if root else None),
+        cq=col([cwq], [cbq]),
+        ckv=col([cwk, cwv], [cbk, cbv]),
+        co=QuantLinear.from_float(cwo[:, hs], cbo if root else None),
+        up=QuantLinear.from_float(up[fs], bup[fs]),
+        down=QuantLinear.from_float(down[:, fs], bdown if root else None),
+        norm_q=norms[0][hs].to(dtype), norm_k=norms[1][hs].to(dtype),
+        cnorm_q=norms[2][hs].to(dtype), cnorm_k=norms[3][hs].to(dtype),
+        modulation=_randn((6, d), seed * 1000 + 60, device, 1.0).to(dtype),
+        cross_norm=w(61, (2, d)).to(dtype),
+    )
+    return weights
+
+
+def rope_freqs(tokens: int, head_dim: int, seed: int = 0, device="cpu",
+               dtype=torch.bfloat16) -> torch.Tensor:
+    """Per-token 2x2 rotations [1, tokens, 1, head_dim / 2, 2, 2] of random
+    angles (the layout the fused Q/K prologue reads; interleaved pairs)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    ang = torch.rand((1, tokens, 1, head_dim // 2, 1, 1), generator=g, device=device) * 6.283
+    c, s = torch.cos(ang), torch.sin(ang)
+    return torch.cat([torch.cat([c, -s], -1), torch.cat([s, c], -1)], -2).to(dtype)
+
+
+# ------------------------------------------------------------ backends --
+
+class KernelOps:
+    """The sm_100a kernels of this package."""
+
+    def __init__(self):
+        from . import _C
+        from .turing_sage import core, quant
+
+        self._C, self._core, self._quant = _C, core, quant
+        self.launches = 0
+        self.event_pair = None  # CUDA events recorded around the self-attention kernel
+
+    def ln_adaln(self, x, scale, shift, eps):
+        self.launches += 1
+        return self._C.turing_layer_norm_adaln(x[None], scale[None, None], shift[None, None],
+                                               eps)[0]
+
+    def linear(self, x, layer: QuantLinear):
+        self.launches += 2
+        q, s = self._C.turing_bf16_int8_convrot_quantize(x)
+        return self._C.turing_int8_linear(q, layer.weight, s, layer.scale, layer.bias)
+
+    def gelu_linear(self, u, layer: QuantLinear):
+        self.launches += 2
+        q, s = self._C.turing_bf16_gelu_int8_convrot_quantize(u)
+        return self._C.turing_int8_linear(q, layer.weight, s, layer.scale, layer.bias)
+
+    def sum_squares(self, t):
+        self.launches += 1
+        return self._quant.row_sum_squares(t[None], tensor_layout="NHD")[0]
+
+    def attention(self, q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps, mark=False):
+        """q [Lq, H, D], k/v [Lk, H, D] (views) -> [Lq, H*D]."""
+        self.launches += 2 if q_rrms is not None else 3
+        q8, qs, k8, ks = self._quant.rms_rope_per_warp_int8(
+            q[None], k[None], qn, kn, freqs, epsilon=eps, rot_dim=rot_dim, tensor_layout="NHD",
+            norm_scope="row", split_half=False, rotate_qk=False, stabilize_k=False,
+            query_rrms=None if q_rrms is None else q_rrms[None],
+            key_rrms=None if k_rrms is None else k_rrms[None])
+        qk = self._core.PrequantizedQK(q8, qs, k8, ks, "NHD", q.dtype, q.size(-1), False)
+        pre = self._core.prequantize_sageattn_from_qk(qk, v[None])
+        if mark and self.event_pair is not None:
+            self.event_pair[0].record()
+        out = self._core.sageattn_from_prequantized(pre)
+        if mark and self.event_pair is not None:
+            self.event_pair[1].record()
+        return out.reshape(q.size(0), -1)
+
+    @staticmethod
+    def gated_add(x, y, gate):
+        return torch.addcmul(x, y, gate) if gate is not None else x + y
+
+
+class TorchOps:
+    """fp32 torch reference with the dequantized weights."""
+    launches = 0
+
+    def __init__(self):
+        self._w: dict[int, torch.Tensor] = {}
+
+    def _dense(self, layer: QuantLinear):
+        key = id(layer)
+        if key not in self._w:
+            self._w[key] = layer.dequantized()
+        return self._w[key]
+
+    @staticmethod
+    def ln_adaln(x, scale, shift, eps):
+        x = x.float()
+        return torch.nn.functional.layer_norm(x, (x.size(-1),), eps=eps) * (1 + scale.float()) \
+            + shift.float()
+
+    def linear(self, x, layer):
+        y = x.float() @ self._dense(layer).t()
+        return y + layer.bias if layer.bias is not None else y
+
+    def gelu_linear(self, u, layer):
+        return self.linear(torch.nn.functional.gelu(u.float(), approximate="tanh"), layer)
+
+    @staticmethod
+    def sum_squares(t):
+        return t.float().pow(2).sum(dim=(1, 2))
+
+    @staticmethod
+    def attention(q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps, mark=False):
+        def norm_rope(t, w, rrms):
+            n = t.float() * rrms[:, None, None] * w.float().view(1, t.size(1), -1)
+            if rot_dim:
+                f = freqs.float()[0, :, 0]                       # [L, pairs, 2, 2]
+                pairs = n.view(n.size(0), n.size(1), -1, 2)       # [L, H, pairs, 2]
+                n = torch.einsum("lprc,lhpc->lhpr", f, pairs).reshape(n.shape)
+            return n
+        if q_rrms is None:
+            q_rrms = torch.rsqrt(TorchOps.sum_squares(q) / (q.size(1) * q.size(2)) + eps)
+            k_rrms = torch.rsqrt(TorchOps.sum_squares(k) / (k.size(1) * k.size(2)) + eps)
+        qf = norm_rope(q, qn, q_rrms).transpose(0, 1)
+        kf = norm_rope(k, kn, k_rrms).transpose(0, 1)
+        out = torch.nn.functional.scaled_dot_product_attention(qf, kf, v.float().transpose(0, 1))
+        return out.transpose(0, 1).reshape(q.size(0), -1)
+
+    @staticmethod
+    def gated_add(x, y, gate):
+        return x.float() + y * gate.float() if gate is not None else x.float() + y
+
+
+# --------------------------------------------------------------- block --
+
+class DiTBlock:
+    """One Wan2.1-style block on one tensor-parallel rank.  `group` is the
+    torch.distributed process group of the block's ranks (None: one rank)."""
+
+    def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
+                 group=None):
+        self.cfg, self.w, self.plan, self.ops, self.group = cfg, weights, plan, ops, group
+
+    def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
+        if self.plan.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
+        """Row RRMS over the heads of every rank (None: one rank, the fused
+        prologue computes it)."""
+        if self.plan.world == 1 and isinstance(self.ops, KernelOps):
+            return None
+        s = self._all_reduce(self.ops.sum_squares(t).float().contiguous())
+        return torch.rsqrt(s / self.cfg.dim + self.cfg.eps)
+
+    def _attend(self, q, k, v, qn, kn, freqs, rot_dim):
+        return self.ops.attention(q, k, v, qn, kn, freqs, rot_dim, self._rrms(q), self._rrms(k),
+                                  self.cfg.eps, mark=rot_dim > 0)
+
+    def forward(self, x: torch.Tensor, ctx: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
+        """x [L, dim], ctx [Lc, dim], freqs [1, L, 1, head_dim/2, 2, 2] -> [L, dim]."""
+        c, w, ops = self.cfg, self.w, self.ops
+        D, nh = c.head_dim, self.plan.nheads
+        L, Lc = x.size(0), ctx.size(0)
+        m = w.modulation
+        # Self-attention.
+        h = ops.ln_adaln(x, m[1], m[0], c.eps)
+        qkv = ops.linear(h, w.qkv).view(L, 3, nh, D)
+        att = self._attend(qkv[:, 0], qkv[:, 1], qkv[:, 2], w.norm_q, w.norm_k, freqs, D)
+        x = ops.gated_add(x, self._all_reduce(ops.linear(att, w.o)), m[2])
+        # Cross-attention to the context.
+        h = ops.ln_adaln(x, w.cross_norm[1], w.cross_norm[0], c.eps)
+        q = ops.linear(h, w.cq).view(L, nh, D)
+        kv = ops.linear(ctx, w.ckv).view(Lc, 2, nh, D)
+        att = self._attend(q, kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0)
+        x = ops.gated_add(x, self._all_reduce(ops.linear(att, w.co)), None)
+        # Feed-forward.
+        h = ops.ln_adaln(x, m[4], m[3], c.eps)
+        y = ops.gelu_linear(ops.linear(h, w.up), w.down)
+        return ops.gated_add(x, self._all_reduce(y), m[5])
+
+    def ops_count(self, L: int, Lc: int) -> float:
+        """Algorithmic operations of the whole block (all ranks): 2 per
+        multiply-add of every linear and of QK^T and PV."""
+        d, f, H, D = self.cfg.dim, self.cfg.ffn, self.cfg.heads, self.cfg.head_dim
+        lin = 2 * L * d * (3 * d) + 2 * L * d * d + 2 * 2 * L * d * d + 2 * Lc * d * 2 * d \
+            + 2 * 2 * L * d * f
+        attn = 4 * H * L * L * D + 4 * H * L * Lc * D
+        return float(lin + attn)
+
+
+def block_ops(cfg: BlockConfig, L: int, Lc: int) -> float:
+    return DiTBlock(cfg, None, shard_plan(cfg, 1, 0), None).ops_count(L, Lc)

@@ -59,9 +59,12 @@ def per_warp_int8(q: torch.Tensor, k: torch.Tensor, BLKQ: int = 64, WARPQ: int =
 def rms_rope_per_warp_int8(q: torch.Tensor, k: torch.Tensor, q_norm: torch.Tensor,
                            k_norm: torch.Tensor, freqs: torch.Tensor | None, *, epsilon: float,
                            rot_dim: int, tensor_layout: str, norm_scope: str, split_half: bool,
-                           rotate_qk: bool, stabilize_k: bool):
+                           rotate_qk: bool, stabilize_k: bool, query_rrms=None, key_rrms=None):
     """Fused Q/K RMSNorm + RoPE into the production INT8 contract (quant.py:6-92):
-    Q per 16-token warp tile, K per 64-token block, same output shapes."""
+    Q per 16-token warp tile, K per 64-token block, same output shapes.
+    query_rrms / key_rrms ([B, L] fp32, row scope only; not in the
+    reference): per-token reciprocal RMS computed by the caller, e.g. over
+    heads held by several tensor-parallel ranks."""
     if tensor_layout == "HND":
         batch, q_heads, q_tokens, head_dim = q.shape
         _, k_heads, k_tokens, _ = k.shape
@@ -82,7 +85,12 @@ def rms_rope_per_warp_int8(q: torch.Tensor, k: torch.Tensor, q_norm: torch.Tenso
                           device=q.device)
     k_scale = torch.empty((batch, k_heads, (k_tokens + 63) // 64), dtype=torch.float32,
                           device=k.device)
-    if norm_scope == "row":
+    given = query_rrms is not None or key_rrms is not None
+    if given and (norm_scope != "row" or query_rrms is None or key_rrms is None):
+        raise ValueError("query_rrms and key_rrms are given together, with norm_scope='row'")
+    if given:
+        q_rrms, k_rrms = query_rrms.contiguous(), key_rrms.contiguous()
+    elif norm_scope == "row":
         q_rrms = torch.empty((batch, q_tokens), dtype=torch.float32, device=q.device)
         k_rrms = torch.empty((batch, k_tokens), dtype=torch.float32, device=k.device)
     else:
@@ -100,6 +108,15 @@ def rms_rope_per_warp_int8(q: torch.Tensor, k: torch.Tensor, q_norm: torch.Tenso
     _fused.quant_qk_rms_rope_int8_cuda(
         q, k, q_int8, k_int8, q_scale, k_scale, q_norm, k_norm, freqs, q_rrms, k_rrms,
         anchor_indices, anchor_values, float(epsilon), int(rot_dim), 64, 16, 64, layout_id,
-        1 if norm_scope == "row" else 0, bool(split_half), bool(rotate_qk))
+        (2 if given else 1) if norm_scope == "row" else 0, bool(split_half), bool(rotate_qk))
     return q_int8, q_scale, k_int8, k_scale
+
+
+def row_sum_squares(x: torch.Tensor, tensor_layout: str = "HND") -> torch.Tensor:
+    """[B, L] fp32 per-token sum of squares over all heads of x (the partial
+    sums a tensor-parallel rank contributes to a row-scope RMSNorm)."""
+    batch, _, tokens = _geometry(x, tensor_layout)
+    sums = torch.empty((batch, tokens), dtype=torch.float32, device=x.device)
+    _fused.row_sum_squares_cuda(x, sums, 0 if tensor_layout == "NHD" else 1)
+    return sums
 

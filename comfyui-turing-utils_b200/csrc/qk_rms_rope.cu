@@ -138,6 +138,8 @@ struct QkRopeArgs {
   int fast_freqs;           // interleaved, f_p == 4, f_r == 2, f_c == 1, 16-byte rows
   float eps;
   int row_scope;
+  int rrms_given;           // row scope with the RRMS supplied by the caller
+  int sum_only;             // row pass: write the sum of squares, not the RRMS
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -475,27 +477,30 @@ __global__ void __launch_bounds__(kQkThreads) row_rrms_kernel(const QkRopeArgs a
     }
     const float total = ((ws[0] + ws[4]) + (ws[2] + ws[6])) + ((ws[1] + ws[5]) + (ws[3] + ws[7]));
     if (lane == 0 && tok < L)
-      a.rrms[which][static_cast<int64_t>(batch) * L + tok] = __frsqrt_rn(total / n + a.eps);
+      a.rrms[which][static_cast<int64_t>(batch) * L + tok] =
+          a.sum_only ? total : __frsqrt_rn(total / n + a.eps);
   }
 }
 
 }  // namespace
 
+void row_rrms_launch(QkRopeArgs& a, int batch, int head_dim, int dtype, cudaStream_t stream) {
+  const int q_groups = (a.length[0] + kRowTokens - 1) / kRowTokens;
+  const int k_groups = (a.length[1] + kRowTokens - 1) / kRowTokens;
+  const dim3 grid(static_cast<unsigned>(q_groups + k_groups), static_cast<unsigned>(batch));
+#define TB_RR_LAUNCH(T, D) row_rrms_kernel<T, D><<<grid, kQkThreads, 0, stream>>>(a, q_groups)
+  if (dtype == TB_DTYPE_BF16) {
+    if (head_dim == 128) TB_RR_LAUNCH(__nv_bfloat16, 128); else TB_RR_LAUNCH(__nv_bfloat16, 64);
+  } else {
+    if (head_dim == 128) TB_RR_LAUNCH(__half, 128); else TB_RR_LAUNCH(__half, 64);
+  }
+#undef TB_RR_LAUNCH
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
 void qk_rms_rope_launch(QkRopeArgs& a, int batch, int head_dim, int split_half, int dtype,
                         cudaStream_t stream) {
-  if (a.row_scope) {
-    const int q_groups = (a.length[0] + kRowTokens - 1) / kRowTokens;
-    const int k_groups = (a.length[1] + kRowTokens - 1) / kRowTokens;
-    const dim3 grid(static_cast<unsigned>(q_groups + k_groups), static_cast<unsigned>(batch));
-#define TB_RR_LAUNCH(T, D) row_rrms_kernel<T, D><<<grid, kQkThreads, 0, stream>>>(a, q_groups)
-    if (dtype == TB_DTYPE_BF16) {
-      if (head_dim == 128) TB_RR_LAUNCH(__nv_bfloat16, 128); else TB_RR_LAUNCH(__nv_bfloat16, 64);
-    } else {
-      if (head_dim == 128) TB_RR_LAUNCH(__half, 128); else TB_RR_LAUNCH(__half, 64);
-    }
-#undef TB_RR_LAUNCH
-    TB_CUDA_CHECK(cudaGetLastError());
-  }
+  if (a.row_scope && !a.rrms_given) row_rrms_launch(a, batch, head_dim, dtype, stream);
   // Heads per task: about 8, balanced over the head count, so the per-token
   // rotations and row RRMS are loaded once per 8 heads and the ring has a few
   // heads to run ahead on.
@@ -547,8 +552,8 @@ extern "C" int tb_quant_qk_rms_rope_int8(
     TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16, "Q/K must be float16 or bfloat16");
     TB_REQUIRE(head_dim == 64 || head_dim == 128,
                "fused Q/K preprocessing requires head_dim 64 or 128");
-    TB_REQUIRE(norm_scope == 0 || norm_scope == 1,
-               "norm_scope must be 0 (per head) or 1 (whole row)");
+    TB_REQUIRE(norm_scope >= 0 && norm_scope <= 2,
+               "norm_scope must be 0 (per head), 1 (whole row) or 2 (whole row, RRMS given)");
     TB_REQUIRE(rot_dim >= 0 && rot_dim <= head_dim && rot_dim % 2 == 0,
                "rot_dim must be even and within head_dim");
     TB_REQUIRE(rot_dim == 0 || (freqs && freq_strides),
@@ -600,7 +605,8 @@ extern "C" int tb_quant_qk_rms_rope_int8(
     }
     a.rot_dim = static_cast<int>(rot_dim);
     a.eps = epsilon;
-    a.row_scope = norm_scope;
+    a.row_scope = norm_scope ? 1 : 0;
+    a.rrms_given = norm_scope == 2;
     // Loads that the kernel skips at run time (no RoPE, head-scope norm) must
     // still name readable memory: the compiler may issue a guarded load ahead
     // of its guard (for example when hoisting it out of the per-head loop), so
@@ -616,3 +622,32 @@ extern "C" int tb_quant_qk_rms_rope_int8(
                            dtype, static_cast<cudaStream_t>(stream));
   });
 }
+
+extern "C" int tb_row_sum_squares(const void* input, float* sums, int64_t batch, int64_t heads,
+                                  int64_t length, int64_t head_dim, const int64_t* strides,
+                                  int dtype, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(input && sums && strides, "input, sums and strides must be given");
+    TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16, "input must be float16 or bfloat16");
+    TB_REQUIRE(head_dim == 64 || head_dim == 128, "head_dim must be 64 or 128");
+    TB_REQUIRE(batch > 0 && heads > 0 && length > 0 && batch <= 65535 && length <= INT32_MAX &&
+                   heads <= INT32_MAX,
+               "dimensions must be positive and within the CUDA kernel range");
+    for (int i = 0; i < 3; ++i)
+      TB_REQUIRE(strides[i] % 8 == 0, "strides must be multiples of 8 elements (16-byte packs)");
+    TB_REQUIRE((reinterpret_cast<uintptr_t>(input) & 15u) == 0, "input must be 16-byte aligned");
+    tb::require_sm100();
+    tb::QkRopeArgs a{};
+    a.in[0] = a.in[1] = input;
+    a.heads[0] = a.heads[1] = static_cast<int>(heads);
+    a.length[0] = static_cast<int>(length);
+    a.length[1] = 0;  // one tensor: the second half of the grid is empty
+    a.s_b[0] = strides[0]; a.s_h[0] = strides[1]; a.s_l[0] = strides[2];
+    a.rrms[0] = a.rrms[1] = sums;
+    a.row_scope = 1;
+    a.sum_only = 1;
+    tb::row_rrms_launch(a, static_cast<int>(batch), static_cast<int>(head_dim), dtype,
+                        static_cast<cudaStream_t>(stream));
+  });
+}
+

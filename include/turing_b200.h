@@ -181,7 +181,8 @@ TB_API int tb_int4_linear(const int8_t *activation_packed, const int8_t *weight_
  * 2x2 rotations from freqs [freq_batches, freq_sequence, 1, rot_dim/2, 2, 2]
  * (freq_strides: batch, sequence, pair, row, col in elements; split_half
  * pairs (p, p + rot_dim/2), else (2p, 2p+1)), then INT8 quantization with the
- * Sage scale layout: Q per 16-token tile into query_scale [B, Hq, ceil(Lq/64)*4],
+ * Sage scale layout (norm_scope 2: whole row with query_rrms / key_rrms
+ * supplied by the caller, see tb_row_sum_squares): Q per 16-token tile into query_scale [B, Hq, ceil(Lq/64)*4],
  * K per 64-token block into key_scale [B, Hk, ceil(Lk/64)]; codes clamped to
  * +-127.  strides (elements, 16 values): q (b, h, l), k (b, h, l), q_out
  * (b, h, l), k_out (b, h, l), q_scale (b, h), k_scale (b, h); the last
@@ -200,6 +201,17 @@ TB_API int tb_quant_qk_rms_rope_int8(const void *query, const void *key, int8_t 
                                      int64_t freq_batches, int64_t freq_sequence, int64_t rot_dim,
                                      int norm_scope, int split_half, int dtype, float epsilon,
                                      tb_stream_t stream);
+
+/* Per-token sum of squares over all heads of one Q or K tensor (elements
+ * (b, h, l, 0..head_dim) at b*strides[0] + h*strides[1] + l*strides[2]) into
+ * sums [batch, length] fp32, summed in the same order as the row-scope RMS of
+ * tb_quant_qk_rms_rope_int8.  For tensor parallelism: each rank sums its own
+ * heads, the sums are all-reduced, and the RRMS = rsqrt(sum / (H*D) + eps) is
+ * passed to tb_quant_qk_rms_rope_int8 with norm_scope 2.  No counterpart in
+ * the reference (its RMS pass, qk_preprocess.cu:203-251, writes the RRMS). */
+TB_API int tb_row_sum_squares(const void *input, float *sums, int64_t batch, int64_t heads,
+                              int64_t length, int64_t head_dim, const int64_t *strides, int dtype,
+                              tb_stream_t stream);
 
 /* ---------------------------------------------------- norm + AdaLN ---- */
 
