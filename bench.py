@@ -4,6 +4,12 @@
 
 Workloads (synthetic seeded inputs of the stated shapes
 and distributions — the reference benchmarks on no public dataset):
+  dit_block  configs[4] (default): one Wan2.1-14B-shaped DiT block, dim 5120,
+             40 heads x 128, FFN 13824, L = 75600, 512 text tokens, W8A8
+             ConvRot linears, Sage INT8 self- and cross-attention, AdaLN;
+             tensor + sequence parallel over the torchrun ranks (NCCL).
+             Metric: block tokens/s (L / block time, max over ranks),
+             strong scaling.
   attention  configs[1]: Sage INT8 attention B=1, H=40, L=32760, D=128, HND,
              Q/K/V bf16 ~N(0,1), K + per-channel offset ~N(0,2), K mean
              smoothing, Q per 16-token warp tiles, K per 64-token blocks.
@@ -21,11 +27,13 @@ and distributions — the reference benchmarks on no public dataset):
              fused dequant/bias/bf16 epilogue.
   codebook   configs[2]: W4A8 grouped-codebook linear, X [8192, 5120].
   w4a4_ffn   configs[3]: W4A4 ConvRot FFN pair over 32760 tokens.
-Metric: INT8 TOPS (whole job, all ranks) = algorithmic ops / device time.
+Metric of the other workloads: INT8 TOPS (whole job, all ranks) = algorithmic
+ops / device time.
 
-Multi-GPU (torchrun): every rank runs its own independent copy of the
-workload (its own batch shard); there is no data-path collective, so scaling
-is weak.  Time = max over ranks of the per-rank device time.
+Multi-GPU (torchrun): dit_block splits one block over the ranks (strong
+scaling); every other workload runs an independent copy per rank (its own
+batch shard, no data-path collective, weak scaling).  Time = max over ranks of
+the per-rank device time.
 
 --impl reference times the reference's CPU implementation of the same step
 (the torch fp32 dequantize-then-matmul / dequantize-then-attention path of
@@ -630,7 +638,11 @@ class DiTBlockWorkload:
 
         self.weights = db.make_weights(self.cfg, self.plan, seed=0, device=device)
         g = torch.Generator(device=device).manual_seed(1)
-        self.x = torch.randn((self.L, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
+        x = torch.randn((self.L, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
+        # Sequence parallel: each rank holds (and is timed on) its own tokens.
+        rows = db.local_rows(self.L, world, rank, db.token_chunks(self.L, world))
+        self.x = x[rows.to(device)].contiguous()
+        del x
         self.ctx = torch.randn((self.Lc, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
         self.freqs = db.rope_freqs(self.L, self.cfg.head_dim, seed=2, device=device)
         self.kops = db.KernelOps()
@@ -641,19 +653,21 @@ class DiTBlockWorkload:
         self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
         self.d2h_bytes = self.out_host.numel() * 2
         before = self.kops.launches
-        self.block.forward(self.x, self.ctx, self.freqs)
+        self.block.forward(self.x, self.ctx, self.freqs, L=self.L)
         self.launches_per_step = self.kops.launches - before
 
     def parallelism(self, world):
-        return (f"tensor parallel x{world}: heads {list(self.plan.heads)}, FFN columns "
-                f"{list(self.plan.ffn)}; NCCL all-reduce after O, cross-O and FFN-down "
-                "(bf16) and of the Q/K row sums of squares (fp32)") if world > 1 else "1 GPU"
+        return (f"tensor + sequence parallel x{world}: heads {list(self.plan.heads)}, FFN "
+                f"columns {list(self.plan.ffn)}; each rank owns {self.x.size(0)} tokens; NCCL "
+                "all-gather of the INT8 activations before Q/K/V, cross-Q and FFN-up, "
+                "reduce-scatter (bf16) after O, cross-O and FFN-down, chunked to overlap the "
+                "linears; all-reduce of the Q/K row sums of squares") if world > 1 else "1 GPU"
 
     def step(self, ev=None):
         if ev:
             ev[0].record()
             self.kops.event_pair = (ev[1], ev[2])
-        out = self.block.forward(self.x, self.ctx, self.freqs)
+        out = self.block.forward(self.x, self.ctx, self.freqs, L=self.L)
         if ev:
             ev[3].record()
             self.kops.event_pair = None
@@ -662,7 +676,7 @@ class DiTBlockWorkload:
     def step_e2e(self):
         dev = self.x.device
         x, ctx = (t.to(dev, non_blocking=True) for t in self.host)
-        out = self.block.forward(x, ctx, self.freqs)
+        out = self.block.forward(x, ctx, self.freqs, L=self.L)
         self.out_host.copy_(out, non_blocking=True)
         return out
 
@@ -722,7 +736,10 @@ def make_workload(args, device, seed, world=1, rank=0):
 
 
 def default_workload() -> str:
-    return "attention" if "attention" in WORKLOADS else "linear"
+    # The metric's multi-GPU part is DiT-block tokens/s at 1/2/4/8 GPUs
+    # (BASELINE configs[4]); the block contains the attention of configs[1] and
+    # the W8A8 linears of configs[0] at full size.
+    return "dit_block"
 
 
 # ----------------------------------------------------------------- runners --

@@ -40,8 +40,10 @@ def _as_f32_vec(t: torch.Tensor) -> torch.Tensor:
 # ------------------------------------------------------------------ linears
 
 def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=None,
-                       tile_policy=0):
-    """bindings.cpp:371-421."""
+                       tile_policy=0, out=None):
+    """bindings.cpp:371-421.  out (not in the reference): an existing bf16
+    [M, N] destination with unit column stride, e.g. a row block of a larger
+    buffer; its row stride is passed as the GEMM's ldo."""
     activation = activation.contiguous()
     weight = weight.contiguous()
     activation_scale = _as_f32_vec(activation_scale)
@@ -70,9 +72,17 @@ def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=
     n = weight.size(0)
     with torch.cuda.device(activation.device):
         _require_blackwell(activation.device, "turing_int8_linear")
-        out = torch.empty((m, n), dtype=torch.bfloat16, device=activation.device)
+        if out is None:
+            out = torch.empty((m, n), dtype=torch.bfloat16, device=activation.device)
+        else:
+            _check(out.dtype == torch.bfloat16 and out.device == activation.device
+                   and tuple(out.shape) == (m, n) and out.stride(1) == 1
+                   and out.stride(0) >= n and out.stride(0) % 8 == 0
+                   and out.data_ptr() % 16 == 0,
+                   "out must be a 16-byte aligned bf16 [M, N] CUDA view with unit column stride "
+                   "and a row stride that is a multiple of 8")
         call("tb_int8_linear", ptr(activation), ptr(weight), ptr(activation_scale),
-             ptr(weight_scale), ptr(bias), ptr(out), m, n, k, n, int(tile_policy),
+             ptr(weight_scale), ptr(bias), ptr(out), m, n, k, out.stride(0), int(tile_policy),
              stream_of(activation))
     return out
 

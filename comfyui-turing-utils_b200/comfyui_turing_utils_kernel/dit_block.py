@@ -21,9 +21,11 @@ with RMS the RMSNorm over all heads of a token (learned weight).
 
 Tensor parallelism (one process per GPU): column-parallel Q/K/V, cross
 Q/K/V and FFN-up; attention on the rank's own heads; row-parallel O, cross O
-and FFN-down, each followed by one all-reduce of the [L, dim] bf16 partial
-sums; the row-scope RMSNorm of Q and K adds an all-reduce of the per-token
-fp32 sums of squares.  A row-parallel layer's input shard must hold whole
+and FFN-down; with sequence parallelism between them (DiTBlock): the INT8
+activations are all-gathered before each column-parallel linear and the
+row-parallel [L, dim] bf16 partial sums reduce-scattered back to their token
+owners, chunk by chunk to overlap the linears; the row-scope RMSNorm of Q and
+K adds an all-reduce of the per-token fp32 sums of squares.  A row-parallel layer's input shard must hold whole
 256-channel ConvRot groups (its Hadamard rotation and per-token INT8 scale
 are taken over the shard), so heads and FFN columns are dealt out in
 256-channel units: 40 heads on 8 ranks = 6,6,6,6,4,4,4,4.
@@ -214,6 +216,10 @@ def rope_freqs(tokens: int, head_dim: int, seed: int = 0, device="cpu",
 
 
 # ------------------------------------------------------------ backends --
+#
+# A backend turns a [rows, K] activation into the form its linears take
+# (`quantize`: a list of row-aligned tensors, which the block may all-gather
+# across ranks) and applies a QuantLinear to that form (`linear_q`).
 
 class KernelOps:
     """The sm_100a kernels of this package."""
@@ -231,15 +237,19 @@ class KernelOps:
         return self._C.turing_layer_norm_adaln(x[None], scale[None, None], shift[None, None],
                                                eps)[0]
 
-    def linear(self, x, layer: QuantLinear):
-        self.launches += 2
-        q, s = self._C.turing_bf16_int8_convrot_quantize(x)
-        return self._C.turing_int8_linear(q, layer.weight, s, layer.scale, layer.bias)
+    def quantize(self, x):
+        """ConvRot INT8 codes [rows, K] and per-token scales [rows, 1]."""
+        self.launches += 1
+        return list(self._C.turing_bf16_int8_convrot_quantize(x))
 
-    def gelu_linear(self, u, layer: QuantLinear):
-        self.launches += 2
-        q, s = self._C.turing_bf16_gelu_int8_convrot_quantize(u)
-        return self._C.turing_int8_linear(q, layer.weight, s, layer.scale, layer.bias)
+    def gelu_quantize(self, u):
+        self.launches += 1
+        return list(self._C.turing_bf16_gelu_int8_convrot_quantize(u))
+
+    def linear_q(self, act, layer: QuantLinear, out=None):
+        self.launches += 1
+        return self._C.turing_int8_linear(act[0], layer.weight, act[1], layer.scale, layer.bias,
+                                          out=out)
 
     def sum_squares(self, t):
         self.launches += 1
@@ -263,12 +273,14 @@ class KernelOps:
         return out.reshape(q.size(0), -1)
 
     @staticmethod
-    def gated_add(x, y, gate):
-        return torch.addcmul(x, y, gate) if gate is not None else x + y
+    def gated_add_(x, y, gate):
+        """x += gate * y in place (x's dtype)."""
+        return x.addcmul_(y, gate) if gate is not None else x.add_(y)
 
 
 class TorchOps:
-    """fp32 torch reference with the dequantized weights."""
+    """fp32 torch reference with the dequantized weights (activations are not
+    quantized)."""
     launches = 0
 
     def __init__(self):
@@ -286,12 +298,21 @@ class TorchOps:
         return torch.nn.functional.layer_norm(x, (x.size(-1),), eps=eps) * (1 + scale.float()) \
             + shift.float()
 
-    def linear(self, x, layer):
-        y = x.float() @ self._dense(layer).t()
-        return y + layer.bias if layer.bias is not None else y
+    @staticmethod
+    def quantize(x):
+        return [x.float()]
 
-    def gelu_linear(self, u, layer):
-        return self.linear(torch.nn.functional.gelu(u.float(), approximate="tanh"), layer)
+    @staticmethod
+    def gelu_quantize(u):
+        return [torch.nn.functional.gelu(u.float(), approximate="tanh")]
+
+    def linear_q(self, act, layer, out=None):
+        y = act[0] @ self._dense(layer).t()
+        y = y + layer.bias if layer.bias is not None else y
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
     @staticmethod
     def sum_squares(t):
@@ -315,24 +336,101 @@ class TorchOps:
         return out.transpose(0, 1).reshape(q.size(0), -1)
 
     @staticmethod
-    def gated_add(x, y, gate):
-        return x.float() + y * gate.float() if gate is not None else x.float() + y
+    def gated_add_(x, y, gate):
+        return x.addcmul_(y.to(x.dtype), gate.to(x.dtype)) if gate is not None \
+            else x.add_(y.to(x.dtype))
 
 
 # --------------------------------------------------------------- block --
 
+def token_chunks(L: int, world: int, max_chunks: int = 4) -> int:
+    """Number of token chunks C for the sequence-parallel layout: the largest
+    C <= max_chunks with L divisible by C * world (1 on one rank)."""
+    if world == 1:
+        return 1
+    if L % world:
+        raise ValueError(f"{L} tokens do not split evenly over {world} ranks")
+    return max(c for c in range(1, max_chunks + 1) if L % (c * world) == 0)
+
+
+def local_rows(L: int, world: int, rank: int, chunks: int) -> torch.Tensor:
+    """Token indices a rank owns in the sequence-parallel layout: in each of
+    the `chunks` equal token chunks, the rank's 1/world slice."""
+    piece = L // (chunks * world)
+    return torch.cat([torch.arange(c * (L // chunks) + rank * piece,
+                                   c * (L // chunks) + (rank + 1) * piece) for c in range(chunks)])
+
+
 class DiTBlock:
-    """One Wan2.1-style block on one tensor-parallel rank.  `group` is the
-    torch.distributed process group of the block's ranks (None: one rank)."""
+    """One Wan2.1-style block on one tensor-parallel rank.
+
+    Sequence-parallel layout (Megatron-SP): between the attention / FFN
+    sub-blocks every rank holds only its own tokens of x (`local_rows`), runs
+    LayerNorm+AdaLN, the ConvRot quantizer and the residual adds on them, and
+    all-gathers the INT8 codes and scales (half the bytes of bf16) before each
+    column-parallel linear; each row-parallel linear's [tokens, dim] partial
+    sums are reduce-scattered back to the token owners.  Both collectives run
+    chunk by chunk on NCCL's stream so the linear of one token chunk overlaps
+    the exchange of the next.  `group` is the process group (None: one rank).
+    """
 
     def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
-                 group=None):
+                 group=None, max_chunks: int = 4):
         self.cfg, self.w, self.plan, self.ops, self.group = cfg, weights, plan, ops, group
+        self.max_chunks = max_chunks
 
+    # ----- collectives (identity on one rank)
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.plan.world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
+
+    def _column(self, h_local: torch.Tensor, layer: QuantLinear, L: int, C: int,
+                act=None) -> torch.Tensor:
+        """Column-parallel linear of the full sequence from the local tokens:
+        quantize locally, all-gather the codes per chunk, multiply per chunk."""
+        ops, N = self.ops, self.plan.world
+        act = ops.quantize(h_local) if act is None else act
+        if N == 1:
+            return ops.linear_q(act, layer)
+        piece = L // (C * N)
+        gathered, works = [], []
+        for c in range(C):
+            parts = []
+            for t in act:
+                full = torch.empty((L // C,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+                works.append(dist.all_gather_into_tensor(
+                    full, t[c * piece:(c + 1) * piece].contiguous(), group=self.group,
+                    async_op=True))
+                parts.append(full)
+            gathered.append(parts)
+        rows = L // C
+        dtype = torch.bfloat16 if isinstance(ops, KernelOps) else torch.float32
+        out = torch.empty((L, layer.weight.size(0)), dtype=dtype, device=act[0].device)
+        for c in range(C):
+            for wk in works[c * len(act):(c + 1) * len(act)]:
+                wk.wait()
+            ops.linear_q(gathered[c], layer, out=out[c * rows:(c + 1) * rows])
+        return out
+
+    def _row_into(self, x_local: torch.Tensor, act, layer: QuantLinear, gate, L: int, C: int):
+        """Row-parallel linear of the full sequence, reduce-scattered per chunk
+        to the token owners and added to x_local (x += gate * y)."""
+        ops, N = self.ops, self.plan.world
+        if N == 1:
+            ops.gated_add_(x_local, ops.linear_q(act, layer), gate)
+            return
+        rows = L // C
+        piece = rows // N
+        pending = []
+        for c in range(C):
+            y = ops.linear_q([t[c * rows:(c + 1) * rows] for t in act], layer)
+            out = torch.empty((piece, y.size(1)), dtype=y.dtype, device=y.device)
+            pending.append((dist.reduce_scatter_tensor(out, y, group=self.group, async_op=True),
+                            out, c, y))
+        for wk, out, c, _ in pending:
+            wk.wait()
+            ops.gated_add_(x_local[c * piece:(c + 1) * piece], out, gate)
 
     def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
         """Row RRMS over the heads of every rank (None: one rank, the fused
@@ -346,27 +444,32 @@ class DiTBlock:
         return self.ops.attention(q, k, v, qn, kn, freqs, rot_dim, self._rrms(q), self._rrms(k),
                                   self.cfg.eps, mark=rot_dim > 0)
 
-    def forward(self, x: torch.Tensor, ctx: torch.Tensor, freqs: torch.Tensor) -> torch.Tensor:
-        """x [L, dim], ctx [Lc, dim], freqs [1, L, 1, head_dim/2, 2, 2] -> [L, dim]."""
+    def forward(self, x_local: torch.Tensor, ctx: torch.Tensor, freqs: torch.Tensor,
+                L: Optional[int] = None) -> torch.Tensor:
+        """x_local: this rank's tokens of x (`local_rows`; all of x on one
+        rank), ctx [Lc, dim] (every rank), freqs [1, L, 1, head_dim/2, 2, 2].
+        Returns this rank's tokens of the block output."""
         c, w, ops = self.cfg, self.w, self.ops
         D, nh = c.head_dim, self.plan.nheads
-        L, Lc = x.size(0), ctx.size(0)
+        L = x_local.size(0) * self.plan.world if L is None else L
+        C = token_chunks(L, self.plan.world, self.max_chunks)
+        Lc = ctx.size(0)
         m = w.modulation
+        x = x_local.clone()
         # Self-attention.
-        h = ops.ln_adaln(x, m[1], m[0], c.eps)
-        qkv = ops.linear(h, w.qkv).view(L, 3, nh, D)
+        qkv = self._column(ops.ln_adaln(x, m[1], m[0], c.eps), w.qkv, L, C).view(L, 3, nh, D)
         att = self._attend(qkv[:, 0], qkv[:, 1], qkv[:, 2], w.norm_q, w.norm_k, freqs, D)
-        x = ops.gated_add(x, self._all_reduce(ops.linear(att, w.o)), m[2])
-        # Cross-attention to the context.
-        h = ops.ln_adaln(x, w.cross_norm[1], w.cross_norm[0], c.eps)
-        q = ops.linear(h, w.cq).view(L, nh, D)
-        kv = ops.linear(ctx, w.ckv).view(Lc, 2, nh, D)
-        att = self._attend(q, kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0)
-        x = ops.gated_add(x, self._all_reduce(ops.linear(att, w.co)), None)
+        del qkv
+        self._row_into(x, ops.quantize(att), w.o, m[2], L, C)
+        # Cross-attention to the context (every rank holds the whole context).
+        q = self._column(ops.ln_adaln(x, w.cross_norm[1], w.cross_norm[0], c.eps), w.cq, L, C)
+        kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)
+        att = self._attend(q.view(L, nh, D), kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0)
+        self._row_into(x, ops.quantize(att), w.co, None, L, C)
         # Feed-forward.
-        h = ops.ln_adaln(x, m[4], m[3], c.eps)
-        y = ops.gelu_linear(ops.linear(h, w.up), w.down)
-        return ops.gated_add(x, self._all_reduce(y), m[5])
+        u = self._column(ops.ln_adaln(x, m[4], m[3], c.eps), w.up, L, C)
+        self._row_into(x, ops.gelu_quantize(u), w.down, m[5], L, C)
+        return x
 
     def ops_count(self, L: int, Lc: int) -> float:
         """Algorithmic operations of the whole block (all ranks): 2 per

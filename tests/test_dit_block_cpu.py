@@ -32,6 +32,15 @@ def test_shard_plan_matches_convrot_groups():
         db.shard_plan(cfg, 32, 0)
 
 
+def test_sequence_parallel_layout():
+    assert db.token_chunks(75600, 8) == 3 and db.token_chunks(75600, 1) == 1
+    rows = [db.local_rows(96, 2, r, 4) for r in range(2)]
+    assert sorted(torch.cat(rows).tolist()) == list(range(96))
+    assert rows[0][:12].tolist() == list(range(12)) and rows[1][:12].tolist() == list(range(12, 24))
+    with pytest.raises(ValueError):
+        db.token_chunks(75601, 2)
+
+
 def test_ops_count_matches_config():
     assert abs(db.block_ops(db.BlockConfig(), 75600, 512) / 1e12 - 163.08) < 0.01
 
@@ -52,15 +61,18 @@ def _free_port() -> int:
 
 
 def _block_out(world: int, rank: int):
+    """(full x, this rank's token indices, this rank's output tokens)."""
     torch.manual_seed(0)
     plan = db.shard_plan(SMALL, world, rank)
     w = db.make_weights(SMALL, plan, seed=3)
     g = torch.Generator().manual_seed(9)
-    x = torch.randn((96, SMALL.dim), generator=g)
+    L = 96
+    x = torch.randn((L, SMALL.dim), generator=g)
     ctx = torch.randn((16, SMALL.dim), generator=g)
-    freqs = db.rope_freqs(96, SMALL.head_dim, seed=4, dtype=torch.float32)
+    freqs = db.rope_freqs(L, SMALL.head_dim, seed=4, dtype=torch.float32)
+    rows = db.local_rows(L, world, rank, db.token_chunks(L, world))
     block = db.DiTBlock(SMALL, w, plan, db.TorchOps(), group=None)
-    return x, block.forward(x, ctx, freqs)
+    return x, rows, block.forward(x[rows], ctx, freqs, L=L)
 
 
 def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
@@ -68,8 +80,8 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _, out = _block_out(world, rank)
-        torch.save(out, Path(out_dir) / f"out{rank}.pt")
+        _, rows, out = _block_out(world, rank)
+        torch.save((rows, out), Path(out_dir) / f"out{rank}.pt")
     finally:
         torch.distributed.destroy_process_group()
 
@@ -78,12 +90,15 @@ def _rank_main(rank: int, world: int, port: int, out_dir: str) -> None:
 def test_tensor_parallel_block_equals_one_rank(tmp_path):
     import torch.multiprocessing as mp
 
-    x, single = _block_out(1, 0)
+    x, _, single = _block_out(1, 0)
     mp.start_processes(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
                        start_method="spawn", join=True)
-    outs = [torch.load(tmp_path / f"out{r}.pt") for r in range(2)]
-    assert torch.equal(outs[0], outs[1])          # every rank ends with the full output
-    delta_tp, delta_1 = outs[0] - x, single - x
+    full = torch.full_like(x, float("nan"))
+    for r in range(2):
+        rows, out = torch.load(tmp_path / f"out{r}.pt")
+        full[rows] = out
+    assert not torch.isnan(full).any()            # the ranks' tokens cover the sequence once
+    delta_tp, delta_1 = full - x, single - x
     rel = (delta_tp - delta_1).norm() / delta_1.norm()
     # Row-parallel weights are quantized per shard (their own per-channel
     # scales over the shard's columns), so the two runs differ by weight
