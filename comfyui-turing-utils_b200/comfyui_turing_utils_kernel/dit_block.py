@@ -60,8 +60,8 @@ class BlockConfig:
             raise ValueError("dim must equal heads * head_dim")
         if self.dim % GROUP or self.ffn % GROUP:
             raise ValueError("dim and ffn must be multiples of the 256-channel ConvRot group")
-        if self.head_dim not in (64, 128) or GROUP % self.head_dim:
-            raise ValueError("head_dim must be 64 or 128")
+        if self.head_dim != 128:
+            raise ValueError("head_dim must be 128 (the attention kernel's tile width)")
 
 
 def split_units(units: int, parts: int) -> list[int]:
@@ -74,8 +74,13 @@ def split_units(units: int, parts: int) -> list[int]:
 class ShardPlan:
     world: int
     rank: int
-    heads: tuple[int, ...]      # heads per rank
+    heads: tuple[int, ...]      # O-projection input heads per rank (whole 256-channel groups)
     ffn: tuple[int, ...]        # FFN columns per rank
+    attn: tuple[int, ...] = ()  # attention heads per rank (default: as `heads`)
+
+    def __post_init__(self):
+        if not self.attn:
+            object.__setattr__(self, "attn", self.heads)
 
     @property
     def head0(self) -> int:
@@ -86,6 +91,14 @@ class ShardPlan:
         return self.heads[self.rank]
 
     @property
+    def attn0(self) -> int:
+        return sum(self.attn[: self.rank])
+
+    @property
+    def nattn(self) -> int:
+        return self.attn[self.rank]
+
+    @property
     def ffn0(self) -> int:
         return sum(self.ffn[: self.rank])
 
@@ -93,15 +106,47 @@ class ShardPlan:
     def nffn(self) -> int:
         return self.ffn[self.rank]
 
+    def head_moves(self) -> list[tuple[int, int, int, int]]:
+        """(source rank, destination rank, first head, head count) of every
+        block of attention outputs that must move to the rank whose O shard
+        holds it (both plans are contiguous head ranges in rank order)."""
+        moves = []
+        a = [sum(self.attn[:r]) for r in range(self.world + 1)]
+        o = [sum(self.heads[:r]) for r in range(self.world + 1)]
+        for src in range(self.world):
+            for dst in range(self.world):
+                lo, hi = max(a[src], o[dst]), min(a[src + 1], o[dst + 1])
+                if src != dst and hi > lo:
+                    moves.append((src, dst, lo, hi - lo))
+        return moves
+
+
+def _interleave(shares: list[int]) -> list[int]:
+    """Descending shares reordered big, small, big, small, ... so that each
+    larger share sits beside a smaller one."""
+    s = sorted(shares, reverse=True)
+    out = []
+    while s:
+        out.append(s.pop(0))
+        if s:
+            out.append(s.pop())
+    return out
+
 
 def shard_plan(cfg: BlockConfig, world: int, rank: int) -> ShardPlan:
+    """O-projection heads in 256-channel units, larger and smaller shares
+    alternating; attention heads split evenly when the head count allows
+    (then each larger O shard takes the missing heads from its neighbour's
+    attention output), else equal to the O shards."""
     heads_per_unit = GROUP // cfg.head_dim
     head_units = cfg.heads // heads_per_unit
     ffn_units = cfg.ffn // GROUP
     if world > head_units:
         raise ValueError(f"{world} ranks exceed the {head_units} 256-channel head groups")
-    return ShardPlan(world, rank, tuple(u * heads_per_unit for u in split_units(head_units, world)),
-                     tuple(u * GROUP for u in split_units(ffn_units, world)))
+    heads = tuple(u * heads_per_unit for u in _interleave(split_units(head_units, world)))
+    attn = tuple([cfg.heads // world] * world) if cfg.heads % world == 0 else heads
+    return ShardPlan(world, rank, heads, tuple(u * GROUP for u in split_units(ffn_units, world)),
+                     attn)
 
 
 # ------------------------------------------------------------- weights --
@@ -151,14 +196,14 @@ def _randn(shape, seed: int, device, std: float) -> torch.Tensor:
 
 @dataclasses.dataclass
 class BlockWeights:
-    qkv: QuantLinear          # rows: q, k, v of the rank's heads
-    o: QuantLinear            # columns: the rank's heads; bias on rank 0 only
+    qkv: QuantLinear          # rows: q, k, v of the rank's attention heads
+    o: QuantLinear            # columns: the rank's O-projection heads; bias on rank 0 only
     cq: QuantLinear
     ckv: QuantLinear          # rows: k, v of the rank's heads (applied to the context)
     co: QuantLinear
     up: QuantLinear           # rows: the rank's FFN columns
     down: QuantLinear         # columns: the rank's FFN columns
-    norm_q: torch.Tensor      # RMSNorm weights of the rank's heads [nheads * head_dim]
+    norm_q: torch.Tensor      # RMSNorm weights of the rank's attention heads [nattn * head_dim]
     norm_k: torch.Tensor
     cnorm_q: torch.Tensor
     cnorm_k: torch.Tensor
@@ -172,7 +217,8 @@ def make_weights(cfg: BlockConfig, plan: ShardPlan, seed: int = 0, device="cpu",
     from per-tensor seeds on every rank and sliced to the rank's shard, then
     ConvRot W8A8-quantized; AdaLN modulation ~N(0, 1)."""
     D, d, f = cfg.head_dim, cfg.dim, cfg.ffn
-    hs = slice(plan.head0 * D, (plan.head0 + plan.nheads) * D)
+    hs = slice(plan.attn0 * D, (plan.attn0 + plan.nattn) * D)     # attention heads
+    os_ = slice(plan.head0 * D, (plan.head0 + plan.nheads) * D)   # O-projection heads
     fs = slice(plan.ffn0, plan.ffn0 + plan.nffn)
     root = plan.rank == 0
 
@@ -191,10 +237,10 @@ def make_weights(cfg: BlockConfig, plan: ShardPlan, seed: int = 0, device="cpu",
     norms = [1.0 + w(50 + i, (d,)) for i in range(4)]
     weights = BlockWeights(
         qkv=col([wq, wk, wv], [bq, bk, bv]),
-        o=QuantLinear.from_float(wo[:, hs], bo if root else None),
+        o=QuantLinear.from_float(wo[:, os_], bo if root else None),
         cq=col([cwq], [cbq]),
         ckv=col([cwk, cwv], [cbk, cbv]),
-        co=QuantLinear.from_float(cwo[:, hs], cbo if root else None),
+        co=QuantLinear.from_float(cwo[:, os_], cbo if root else None),
         up=QuantLinear.from_float(up[fs], bup[fs]),
         down=QuantLinear.from_float(down[:, fs], bdown if root else None),
         norm_q=norms[0][hs].to(dtype), norm_k=norms[1][hs].to(dtype),
@@ -255,22 +301,37 @@ class KernelOps:
         self.launches += 1
         return self._quant.row_sum_squares(t[None], tensor_layout="NHD")[0]
 
-    def attention(self, q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps, mark=False):
-        """q [Lq, H, D], k/v [Lk, H, D] (views) -> [Lq, H*D]."""
-        self.launches += 2 if q_rrms is not None else 3
+    def qk_prepare(self, q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps):
+        """Normalize, rotate and quantize q [Lq, H, D] and k [Lk, H, D] (views)
+        once; v [Lk, H, D] may be a strided view (unit channel stride)."""
+        self.launches += 1 if q_rrms is not None else 2
         q8, qs, k8, ks = self._quant.rms_rope_per_warp_int8(
             q[None], k[None], qn, kn, freqs, epsilon=eps, rot_dim=rot_dim, tensor_layout="NHD",
             norm_scope="row", split_half=False, rotate_qk=False, stabilize_k=False,
             query_rrms=None if q_rrms is None else q_rrms[None],
             key_rrms=None if k_rrms is None else k_rrms[None])
-        qk = self._core.PrequantizedQK(q8, qs, k8, ks, "NHD", q.dtype, q.size(-1), False)
-        pre = self._core.prequantize_sageattn_from_qk(qk, v[None])
+        return (q8, qs, k8, ks, v[None])
+
+    def attend_rows(self, state, r0: int, r1: int, mark=False):
+        """Attention of query rows [r0, r1) (r0 a multiple of 16) of a
+        prepared state -> [r1 - r0, H * D] in V's dtype."""
+        q8, qs, k8, ks, v = state
+        self.launches += 1
+        if (r0, r1) != (0, q8.size(1)):
+            q8 = q8[:, r0:r1]
+            tiles = (r1 - r0 + 63) // 64 * 4
+            t0 = r0 // 16
+            part = qs[:, :, t0:t0 + tiles]
+            if part.size(2) < tiles:  # the last 64-token block of the sequence
+                part = torch.nn.functional.pad(part, (0, tiles - part.size(2)), value=1.0)
+            qs = part
         if mark and self.event_pair is not None:
             self.event_pair[0].record()
-        out = self._core.sageattn_from_prequantized(pre)
+        out = self._core.sageattn_prequantized(q8.contiguous(), qs.contiguous(), k8, ks, v,
+                                               tensor_layout="NHD")
         if mark and self.event_pair is not None:
             self.event_pair[1].record()
-        return out.reshape(q.size(0), -1)
+        return out.reshape(r1 - r0, -1)
 
     @staticmethod
     def gated_add_(x, y, gate):
@@ -319,7 +380,7 @@ class TorchOps:
         return t.float().pow(2).sum(dim=(1, 2))
 
     @staticmethod
-    def attention(q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps, mark=False):
+    def qk_prepare(q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps):
         def norm_rope(t, w, rrms):
             n = t.float() * rrms[:, None, None] * w.float().view(1, t.size(1), -1)
             if rot_dim:
@@ -330,10 +391,14 @@ class TorchOps:
         if q_rrms is None:
             q_rrms = torch.rsqrt(TorchOps.sum_squares(q) / (q.size(1) * q.size(2)) + eps)
             k_rrms = torch.rsqrt(TorchOps.sum_squares(k) / (k.size(1) * k.size(2)) + eps)
-        qf = norm_rope(q, qn, q_rrms).transpose(0, 1)
-        kf = norm_rope(k, kn, k_rrms).transpose(0, 1)
-        out = torch.nn.functional.scaled_dot_product_attention(qf, kf, v.float().transpose(0, 1))
-        return out.transpose(0, 1).reshape(q.size(0), -1)
+        return (norm_rope(q, qn, q_rrms).transpose(0, 1), norm_rope(k, kn, k_rrms).transpose(0, 1),
+                v.float().transpose(0, 1))
+
+    @staticmethod
+    def attend_rows(state, r0, r1, mark=False):
+        qf, kf, vf = state
+        out = torch.nn.functional.scaled_dot_product_attention(qf[:, r0:r1], kf, vf)
+        return out.transpose(0, 1).reshape(r1 - r0, -1)
 
     @staticmethod
     def gated_add_(x, y, gate):
@@ -344,13 +409,16 @@ class TorchOps:
 # --------------------------------------------------------------- block --
 
 def token_chunks(L: int, world: int, max_chunks: int = 4) -> int:
-    """Number of token chunks C for the sequence-parallel layout: the largest
-    C <= max_chunks with L divisible by C * world (1 on one rank)."""
+    """Number of token chunks C of the sequence-parallel layout and of the
+    block's pipeline: the largest C <= max_chunks with L divisible by
+    C * world and chunk starts on 16-token boundaries (query tiles of the
+    attention), preferring C > 1 on several ranks; 1 on one rank."""
     if world == 1:
         return 1
     if L % world:
         raise ValueError(f"{L} tokens do not split evenly over {world} ranks")
-    return max(c for c in range(1, max_chunks + 1) if L % (c * world) == 0)
+    ok = [c for c in range(1, max_chunks + 1) if L % (c * world) == 0 and (L // c) % 16 == 0]
+    return max(ok) if ok else 1
 
 
 def local_rows(L: int, world: int, rank: int, chunks: int) -> torch.Tensor:
@@ -369,9 +437,15 @@ class DiTBlock:
     LayerNorm+AdaLN, the ConvRot quantizer and the residual adds on them, and
     all-gathers the INT8 codes and scales (half the bytes of bf16) before each
     column-parallel linear; each row-parallel linear's [tokens, dim] partial
-    sums are reduce-scattered back to the token owners.  Both collectives run
-    chunk by chunk on NCCL's stream so the linear of one token chunk overlaps
-    the exchange of the next.  `group` is the process group (None: one rank).
+    sums are reduce-scattered back to the token owners.
+
+    The block runs as stages over C token chunks, each stage issuing its work
+    for every chunk before the next stage waits on any chunk's collective, so
+    a chunk's all-gather / reduce-scatter (on NCCL's stream) overlaps the
+    following chunks' attention and linears: self-attention is taken per
+    query chunk after one Q/K prologue over the whole sequence; cross-
+    attention and the FFN are independent per token.  `group` is the process
+    group (None: one rank).
     """
 
     def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
@@ -385,52 +459,60 @@ class DiTBlock:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
         return t
 
-    def _column(self, h_local: torch.Tensor, layer: QuantLinear, L: int, C: int,
-                act=None) -> torch.Tensor:
-        """Column-parallel linear of the full sequence from the local tokens:
-        quantize locally, all-gather the codes per chunk, multiply per chunk."""
-        ops, N = self.ops, self.plan.world
-        act = ops.quantize(h_local) if act is None else act
-        if N == 1:
-            return ops.linear_q(act, layer)
-        piece = L // (C * N)
-        gathered, works = [], []
-        for c in range(C):
-            parts = []
-            for t in act:
-                full = torch.empty((L // C,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-                works.append(dist.all_gather_into_tensor(
-                    full, t[c * piece:(c + 1) * piece].contiguous(), group=self.group,
-                    async_op=True))
-                parts.append(full)
-            gathered.append(parts)
-        rows = L // C
-        dtype = torch.bfloat16 if isinstance(ops, KernelOps) else torch.float32
-        out = torch.empty((L, layer.weight.size(0)), dtype=dtype, device=act[0].device)
-        for c in range(C):
-            for wk in works[c * len(act):(c + 1) * len(act)]:
-                wk.wait()
-            ops.linear_q(gathered[c], layer, out=out[c * rows:(c + 1) * rows])
-        return out
+    def _gather(self, act: list) -> tuple[list, list]:
+        """Start all-gathering one chunk's local rows of each tensor in act."""
+        if self.plan.world == 1:
+            return act, []
+        out, works = [], []
+        for t in act:
+            full = torch.empty((t.size(0) * self.plan.world,) + tuple(t.shape[1:]),
+                               dtype=t.dtype, device=t.device)
+            works.append(dist.all_gather_into_tensor(full, t.contiguous(), group=self.group,
+                                                     async_op=True))
+            out.append(full)
+        return out, works
 
-    def _row_into(self, x_local: torch.Tensor, act, layer: QuantLinear, gate, L: int, C: int):
-        """Row-parallel linear of the full sequence, reduce-scattered per chunk
-        to the token owners and added to x_local (x += gate * y)."""
-        ops, N = self.ops, self.plan.world
-        if N == 1:
-            ops.gated_add_(x_local, ops.linear_q(act, layer), gate)
-            return
-        rows = L // C
-        piece = rows // N
-        pending = []
-        for c in range(C):
-            y = ops.linear_q([t[c * rows:(c + 1) * rows] for t in act], layer)
-            out = torch.empty((piece, y.size(1)), dtype=y.dtype, device=y.device)
-            pending.append((dist.reduce_scatter_tensor(out, y, group=self.group, async_op=True),
-                            out, c, y))
-        for wk, out, c, _ in pending:
+    def _scatter(self, y: torch.Tensor):
+        """Start reduce-scattering one chunk's [rows, dim] partial sums."""
+        if self.plan.world == 1:
+            return y, None
+        out = torch.empty((y.size(0) // self.plan.world, y.size(1)), dtype=y.dtype,
+                          device=y.device)
+        return out, (dist.reduce_scatter_tensor(out, y, group=self.group, async_op=True), y)
+
+    @staticmethod
+    def _wait(works):
+        for wk in works:
             wk.wait()
-            ops.gated_add_(x_local[c * piece:(c + 1) * piece], out, gate)
+
+    def _to_o_heads(self, att: torch.Tensor) -> torch.Tensor:
+        """[rows, nattn * D] attention output of this rank's attention heads ->
+        [rows, nheads * D] input of its O shard: blocks of heads move between
+        ranks point to point (plan.head_moves)."""
+        p, D = self.plan, self.cfg.head_dim
+        moves = p.head_moves()
+        if not moves:
+            return att
+        rows = att.size(0)
+        ops, keep, recv = [], [], []
+        for src, dst, h, n in moves:
+            if src == p.rank:
+                blk = att[:, (h - p.attn0) * D:(h - p.attn0 + n) * D].contiguous()
+                keep.append(blk)
+                ops.append(dist.P2POp(dist.isend, blk, dst, group=self.group))
+            elif dst == p.rank:
+                buf = torch.empty((rows, n * D), dtype=att.dtype, device=att.device)
+                recv.append((h, buf))
+                ops.append(dist.P2POp(dist.irecv, buf, src, group=self.group))
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+        out = torch.empty((rows, p.nheads * D), dtype=att.dtype, device=att.device)
+        lo, hi = max(p.attn0, p.head0), min(p.attn0 + p.nattn, p.head0 + p.nheads)
+        if hi > lo:
+            out[:, (lo - p.head0) * D:(hi - p.head0) * D] = att[:, (lo - p.attn0) * D:(hi - p.attn0) * D]
+        for h, buf in recv:
+            out[:, (h - p.head0) * D:(h - p.head0) * D + buf.size(1)] = buf
+        return out
 
     def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
         """Row RRMS over the heads of every rank (None: one rank, the fused
@@ -440,35 +522,85 @@ class DiTBlock:
         s = self._all_reduce(self.ops.sum_squares(t).float().contiguous())
         return torch.rsqrt(s / self.cfg.dim + self.cfg.eps)
 
-    def _attend(self, q, k, v, qn, kn, freqs, rot_dim):
-        return self.ops.attention(q, k, v, qn, kn, freqs, rot_dim, self._rrms(q), self._rrms(k),
-                                  self.cfg.eps, mark=rot_dim > 0)
-
     def forward(self, x_local: torch.Tensor, ctx: torch.Tensor, freqs: torch.Tensor,
                 L: Optional[int] = None) -> torch.Tensor:
         """x_local: this rank's tokens of x (`local_rows`; all of x on one
         rank), ctx [Lc, dim] (every rank), freqs [1, L, 1, head_dim/2, 2, 2].
         Returns this rank's tokens of the block output."""
-        c, w, ops = self.cfg, self.w, self.ops
-        D, nh = c.head_dim, self.plan.nheads
-        L = x_local.size(0) * self.plan.world if L is None else L
-        C = token_chunks(L, self.plan.world, self.max_chunks)
+        c, w, ops, N = self.cfg, self.w, self.ops, self.plan.world
+        D, nh = c.head_dim, self.plan.nattn
+        L = x_local.size(0) * N if L is None else L
+        C = token_chunks(L, N, self.max_chunks)
+        rows, piece = L // C, L // (C * N)
         Lc = ctx.size(0)
         m = w.modulation
         x = x_local.clone()
-        # Self-attention.
-        qkv = self._column(ops.ln_adaln(x, m[1], m[0], c.eps), w.qkv, L, C).view(L, 3, nh, D)
-        att = self._attend(qkv[:, 0], qkv[:, 1], qkv[:, 2], w.norm_q, w.norm_k, freqs, D)
-        del qkv
-        self._row_into(x, ops.quantize(att), w.o, m[2], L, C)
-        # Cross-attention to the context (every rank holds the whole context).
-        q = self._column(ops.ln_adaln(x, w.cross_norm[1], w.cross_norm[0], c.eps), w.cq, L, C)
+        xs = [x[i * piece:(i + 1) * piece] for i in range(C)]      # views of x
+        full_dtype = torch.bfloat16 if isinstance(ops, KernelOps) else torch.float32
+
+        # Q/K/V of the whole sequence: per chunk LayerNorm+AdaLN, quantize,
+        # all-gather, GEMM into the chunk's rows.
+        gathered = [self._gather(ops.quantize(ops.ln_adaln(xi, m[1], m[0], c.eps))) for xi in xs]
+        qkv = torch.empty((L, 3 * nh * D), dtype=full_dtype, device=x.device)
+        for i, (act, works) in enumerate(gathered):
+            self._wait(works)
+            ops.linear_q(act, w.qkv, out=qkv[i * rows:(i + 1) * rows])
+        del gathered
+        qkv = qkv.view(L, 3, nh, D)
+        q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+        state = ops.qk_prepare(q, k, v, w.norm_q, w.norm_k, freqs, D, self._rrms(q),
+                               self._rrms(k), c.eps)
+        # Self-attention per query chunk -> O -> reduce-scatter.
+        pending = []
+        for i in range(C):
+            att = ops.attend_rows(state, i * rows, (i + 1) * rows, mark=i == C - 1)
+            pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(att)), w.o)))
+        del state, qkv, q, k, v
+
+        # Cross-attention: the context's K/V once, then per chunk.
         kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)
-        att = self._attend(q.view(L, nh, D), kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0)
-        self._row_into(x, ops.quantize(att), w.co, None, L, C)
-        # Feed-forward.
-        u = self._column(ops.ln_adaln(x, m[4], m[3], c.eps), w.up, L, C)
-        self._row_into(x, ops.gelu_quantize(u), w.down, m[5], L, C)
+        k_rrms = self._rrms(kv[:, 0])
+        gathered = []
+        for i, (y, job) in enumerate(pending):
+            if job is not None:
+                job[0].wait()
+            ops.gated_add_(xs[i], y, m[2])
+            gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], w.cross_norm[1],
+                                                                   w.cross_norm[0], c.eps))))
+        # Q of every chunk first, so the cross-rank RMS of all chunks is one
+        # all-reduce (a collective queues behind the chunks' gathers).
+        qcs = []
+        for i, (act, works) in enumerate(gathered):
+            self._wait(works)
+            qcs.append(ops.linear_q(act, w.cq).view(rows, nh, D))
+        q_rrms = [None] * C
+        if N > 1 or not isinstance(ops, KernelOps):
+            sums = self._all_reduce(torch.cat([ops.sum_squares(qc).float() for qc in qcs]))
+            q_rrms = list(torch.rsqrt(sums / c.dim + c.eps).split(rows))
+        pending = []
+        for i, qc in enumerate(qcs):
+            st = ops.qk_prepare(qc, kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0,
+                                q_rrms[i], k_rrms, c.eps)
+            att = ops.attend_rows(st, 0, rows)
+            pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(att)), w.co)))
+        del qcs
+
+        # Feed-forward per chunk.
+        gathered = []
+        for i, (y, job) in enumerate(pending):
+            if job is not None:
+                job[0].wait()
+            ops.gated_add_(xs[i], y, None)
+            gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], m[4], m[3], c.eps))))
+        pending = []
+        for i, (act, works) in enumerate(gathered):
+            self._wait(works)
+            u = ops.linear_q(act, w.up)
+            pending.append(self._scatter(ops.linear_q(ops.gelu_quantize(u), w.down)))
+        for i, (y, job) in enumerate(pending):
+            if job is not None:
+                job[0].wait()
+            ops.gated_add_(xs[i], y, m[5])
         return x
 
     def ops_count(self, L: int, Lc: int) -> float:
