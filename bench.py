@@ -730,8 +730,9 @@ class DiTBlockWorkload:
 
     def roofline(self, dom_ms, peaks):
         int8_peak = 2.0 * peaks["bf16_tflops"]
-        # The timed launch is the last query chunk of this rank's heads.
-        rows = self.L // self.db.token_chunks(self.L, self.world)
+        # The timed launch is the last self-attention launch of this rank's heads.
+        a0, a1 = self.db.attention_launches(self.L)[-1]
+        rows = a1 - a0
         ops = 4.0 * self.plan.nattn * rows * self.L * self.cfg.head_dim
         achieved = ops / (dom_ms * 1e-3) / 1e12
         return {"kernel": f"sage_attn ({self.plan.nattn} heads x {rows} query rows x {self.L} keys)",

@@ -312,9 +312,10 @@ class KernelOps:
             key_rrms=None if k_rrms is None else k_rrms[None])
         return (q8, qs, k8, ks, v[None])
 
-    def attend_rows(self, state, r0: int, r1: int, mark=False):
+    def attend_rows(self, state, r0: int, r1: int, mark=False, out=None):
         """Attention of query rows [r0, r1) (r0 a multiple of 16) of a
-        prepared state -> [r1 - r0, H * D] in V's dtype."""
+        prepared state -> [r1 - r0, H * D] in V's dtype (into `out`, a
+        row block of a larger buffer, when given)."""
         q8, qs, k8, ks, v = state
         self.launches += 1
         if (r0, r1) != (0, q8.size(1)):
@@ -327,11 +328,12 @@ class KernelOps:
             qs = part
         if mark and self.event_pair is not None:
             self.event_pair[0].record()
-        out = self._core.sageattn_prequantized(q8.contiguous(), qs.contiguous(), k8, ks, v,
-                                               tensor_layout="NHD")
+        res = self._core.sageattn_prequantized(
+            q8.contiguous(), qs.contiguous(), k8, ks, v, tensor_layout="NHD",
+            output=None if out is None else out.view(1, r1 - r0, q8.size(2), q8.size(3)))
         if mark and self.event_pair is not None:
             self.event_pair[1].record()
-        return out.reshape(r1 - r0, -1)
+        return res.reshape(r1 - r0, -1)
 
     @staticmethod
     def gated_add_(x, y, gate):
@@ -395,10 +397,14 @@ class TorchOps:
                 v.float().transpose(0, 1))
 
     @staticmethod
-    def attend_rows(state, r0, r1, mark=False):
+    def attend_rows(state, r0, r1, mark=False, out=None):
         qf, kf, vf = state
-        out = torch.nn.functional.scaled_dot_product_attention(qf[:, r0:r1], kf, vf)
-        return out.transpose(0, 1).reshape(r1 - r0, -1)
+        res = torch.nn.functional.scaled_dot_product_attention(qf[:, r0:r1], kf, vf)
+        res = res.transpose(0, 1).reshape(r1 - r0, -1)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
 
     @staticmethod
     def gated_add_(x, y, gate):
@@ -419,6 +425,19 @@ def token_chunks(L: int, world: int, max_chunks: int = 4) -> int:
         raise ValueError(f"{L} tokens do not split evenly over {world} ranks")
     ok = [c for c in range(1, max_chunks + 1) if L % (c * world) == 0 and (L // c) % 16 == 0]
     return max(ok) if ok else 1
+
+
+def attention_launches(L: int, sms: int = 148, tile: int = 256,
+                       split: Optional[int] = None) -> list[tuple[int, int]]:
+    """Query-row ranges of the self-attention launches: two, split at a
+    multiple of sms * tile rows when that is near L/2 (each launch then fills
+    whole waves of the attention kernel's 256-row CTAs on every head count;
+    L = 75600 splits at 37888), else one launch."""
+    if split is None:
+        split = sms * tile
+        if abs(2 * split - L) * 8 > L:
+            return [(0, L)]
+    return [(0, split), (split, L)] if 0 < split < L else [(0, L)]
 
 
 def local_rows(L: int, world: int, rank: int, chunks: int) -> torch.Tensor:
@@ -449,9 +468,9 @@ class DiTBlock:
     """
 
     def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
-                 group=None, max_chunks: int = 4):
+                 group=None, max_chunks: int = 4, attn_split: Optional[int] = None):
         self.cfg, self.w, self.plan, self.ops, self.group = cfg, weights, plan, ops, group
-        self.max_chunks = max_chunks
+        self.max_chunks, self.attn_split = max_chunks, attn_split
 
     # ----- collectives (identity on one rank)
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
@@ -550,12 +569,19 @@ class DiTBlock:
         q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
         state = ops.qk_prepare(q, k, v, w.norm_q, w.norm_k, freqs, D, self._rrms(q),
                                self._rrms(k), c.eps)
-        # Self-attention per query chunk -> O -> reduce-scatter.
-        pending = []
-        for i in range(C):
-            att = ops.attend_rows(state, i * rows, (i + 1) * rows, mark=i == C - 1)
-            pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(att)), w.o)))
-        del state, qkv, q, k, v
+        # Self-attention in wave-aligned launches; every chunk whose rows are
+        # done goes through O and starts its reduce-scatter while the next
+        # attention launch runs.
+        att = torch.empty((L, nh * D), dtype=full_dtype, device=x.device)
+        pending, done = [], 0
+        for a0, a1 in attention_launches(L, split=self.attn_split):
+            ops.attend_rows(state, a0, a1, mark=a1 == L, out=att[a0:a1])
+            while done < C and (done + 1) * rows <= a1:
+                blk = att[done * rows:(done + 1) * rows]
+                pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(blk)),
+                                                          w.o)))
+                done += 1
+        del state, qkv, q, k, v, att
 
         # Cross-attention: the context's K/V once, then per chunk.
         kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)

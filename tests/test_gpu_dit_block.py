@@ -40,12 +40,15 @@ def _compare(out, ref, x):
     return rel, cos
 
 
-@pytest.mark.parametrize("cfg,L,Lc", [(SMALL, 300, 40), (db.BlockConfig(), 640, 64)])
-def test_block_matches_fp32_reference(cfg, L, Lc):
+@pytest.mark.parametrize("cfg,L,Lc,split", [(SMALL, 300, 40, None), (db.BlockConfig(), 640, 64, None),
+                                            (SMALL, 600, 40, 256)])
+def test_block_matches_fp32_reference(cfg, L, Lc, split):
+    """split: self-attention in two launches (rows [0, split) and
+    [split, L)), the O projection of finished rows between them."""
     plan = db.shard_plan(cfg, 1, 0)
     w = db.make_weights(cfg, plan, seed=3, device="cuda")
     x, ctx, freqs = _inputs(cfg, L, Lc)
-    out = db.DiTBlock(cfg, w, plan, db.KernelOps()).forward(x, ctx, freqs)
+    out = db.DiTBlock(cfg, w, plan, db.KernelOps(), attn_split=split).forward(x, ctx, freqs)
     assert out.dtype == torch.bfloat16 and out.shape == x.shape
     ref = db.DiTBlock(cfg, w, plan, db.TorchOps()).forward(x.float(), ctx, freqs.float())
     rel, cos = _compare(out, ref, x)
