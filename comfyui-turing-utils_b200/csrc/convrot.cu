@@ -65,6 +65,15 @@ __device__ __forceinline__ float round_to_elem(float v) {
   return elem_to_f32<T>(f32_to_elem_bits<T>(v));
 }
 
+// Two floats rounded to T and packed (lo in bits 0..15), with the hardware
+// cvt.rn: the same round-to-nearest-even as f32_to_elem_bits, and NaN gives
+// the canonical NaN 0x7fff as the reference's float_to_bf16_rn_bits does.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_elem(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return pack_bf16x2(lo, hi);
+  else return pack_f16x2(lo, hi);
+}
+
 template <typename T>
 __device__ __forceinline__ float dtype_finite_max();
 template <>
@@ -105,16 +114,60 @@ __device__ __forceinline__ void butterfly4(float& x0, float& x1, float& x2, floa
   x3 = y3;
 }
 
+// Two independent butterflies at once on packed f32x2 registers (lane 0 =
+// the first butterfly): every packed add / sub / mul rounds each lane as its
+// scalar form does, so the results are the scalar butterfly4's bit for bit.
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpk(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t padd(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t psub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t phalf(uint64_t a) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(0x3F0000003F000000ull));
+  return r;
+}
+__device__ __forceinline__ void butterfly4x2(float& a0, float& a1, float& a2, float& a3,
+                                             float& b0, float& b1, float& b2, float& b3) {
+  const uint64_t x0 = pk(a0, b0), x1 = pk(a1, b1), x2 = pk(a2, b2), x3 = pk(a3, b3);
+  const uint64_t s01 = padd(x0, x1);
+  const uint64_t d01 = psub(x0, x1);
+  const uint64_t y0 = phalf(psub(padd(s01, x2), x3));
+  const uint64_t y1 = phalf(padd(psub(s01, x2), x3));
+  const uint64_t y2 = phalf(padd(padd(d01, x2), x3));
+  const uint64_t y3 = phalf(padd(psub(x2, d01), x3));
+  unpk(y0, a0, b0);
+  unpk(y1, a1, b1);
+  unpk(y2, a2, b2);
+  unpk(y3, a3, b3);
+}
+
 // Stage on 4 consecutive registers (S=1 in layout A, S=16 in layout B).
 __device__ __forceinline__ void stage_contig(float (&v)[16]) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q) butterfly4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  for (int q = 0; q < 4; q += 2)
+    butterfly4x2(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3],
+                 v[4 * q + 4], v[4 * q + 5], v[4 * q + 6], v[4 * q + 7]);
 }
 
 // Stage on registers 4 apart (S=4 in layout A, S=64 in layout B).
 __device__ __forceinline__ void stage_strided(float (&v)[16]) {
 #pragma unroll
-  for (int p = 0; p < 4; ++p) butterfly4(v[p], v[p + 4], v[p + 8], v[p + 12]);
+  for (int p = 0; p < 4; p += 2)
+    butterfly4x2(v[p], v[p + 4], v[p + 8], v[p + 12], v[p + 1], v[p + 5], v[p + 9], v[p + 13]);
 }
 
 // Loads the 16 activated fp32 inputs of lane l (elements col..col+15).
@@ -229,15 +282,25 @@ __device__ __forceinline__ void quantize16_store(const uint32_t (&h)[8], float r
     }
     *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
   } else {
-    uint32_t out[4] = {0u, 0u, 0u, 0u};
+    // d = T(v * rcp) two at a time; then clamp to [-128, 127] (fmaxf maps NaN
+    // to -128, as the reference's fminf(127, fmaxf(-128, NaN)) does), and
+    // adding 1.5 * 2^23 rounds to the nearest integer, ties to even, exactly
+    // as __float2int_rn, leaving the code two's-complement in the low byte.
+    uint32_t cb[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t bits = (i & 1) ? (h[i >> 1] >> 16) : (h[i >> 1] & 0xffffu);
-      const float v = elem_to_f32<T>(bits);
-      const float d = round_to_elem<T>(__fmul_rn(v, rcp_rounded));
-      const int q = __float2int_rn(fminf(127.0f, fmaxf(-128.0f, d)));
-      out[i >> 2] |= (static_cast<uint32_t>(q) & 0xffu) << (8 * (i & 3));
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t d2 = pack2_elem<T>(__fmul_rn(elem_to_f32<T>(h[i] & 0xffffu), rcp_rounded),
+                                        __fmul_rn(elem_to_f32<T>(h[i] >> 16), rcp_rounded));
+      cb[2 * i] = __float_as_uint(__fadd_rn(
+          fminf(127.0f, fmaxf(-128.0f, elem_to_f32<T>(d2 & 0xffffu))), 12582912.0f));
+      cb[2 * i + 1] = __float_as_uint(__fadd_rn(
+          fminf(127.0f, fmaxf(-128.0f, elem_to_f32<T>(d2 >> 16))), 12582912.0f));
     }
+    uint32_t out[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      out[w] = __byte_perm(__byte_perm(cb[4 * w], cb[4 * w + 1], 0x0040),
+                           __byte_perm(cb[4 * w + 2], cb[4 * w + 3], 0x0040), 0x5410);
     *reinterpret_cast<uint4*>(dst) = make_uint4(out[0], out[1], out[2], out[3]);
   }
 }
@@ -285,9 +348,13 @@ __global__ void __launch_bounds__(512) convrot_rowbuffer_kernel(RowQuantParams p
     float amax = 0.0f;
     uint16_t* dst = rowbuf + static_cast<size_t>(r) * k + g * kGroup + l;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      amax = fmaxf(amax, fabsf(v[j]));
-      if (active) dst[16 * j] = static_cast<uint16_t>(f32_to_elem_bits<T>(v[j]));
+    for (int j = 0; j < 16; j += 2) {
+      amax = fmaxf(amax, fmaxf(fabsf(v[j]), fabsf(v[j + 1])));
+      const uint32_t two = pack2_elem<T>(v[j], v[j + 1]);
+      if (active) {
+        dst[16 * j] = static_cast<uint16_t>(two & 0xffffu);
+        dst[16 * (j + 1)] = static_cast<uint16_t>(two >> 16);
+      }
     }
     // Non-negative floats order like their bit patterns.
 #pragma unroll
