@@ -59,6 +59,13 @@ constexpr uint32_t kSBase = 256;
 #define TB_ATTN_POLY_MASK 0x0000u
 #endif
 constexpr uint32_t kPolyPairMask = TB_ATTN_POLY_MASK;
+// 1: a block's second 32 score columns load from TMEM while the first 32 are
+// exponentiated.
+#ifndef TB_ATTN_SPLIT_LD
+#define TB_ATTN_SPLIT_LD 1
+#endif
+constexpr bool kSplitLd = TB_ATTN_SPLIT_LD != 0;
+
 
 struct AttnParams {
   int B, Hq, Hk, Lq, Lk, groups;  // groups = Hq / Hk
@@ -233,12 +240,15 @@ __device__ __forceinline__ uint32_t pack_pair(uint64_t p2) {
 // reference, in place as exp_block, with the integer row max of the raw
 // scores accumulated in the same loop (the ALU work of the max hides under
 // the exponentials).  Returns that max.
-template <typename TV>
+template <typename TV, bool WAIT_HI>
 __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
                                              uint64_t (&sum2)[2]) {
   int m[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
 #pragma unroll
   for (int i = 0; i < kBlockN / 2; ++i) {
+    // Pairs 0..15 read columns 0..31 and write v[0..15]; the load of columns
+    // 32..63 (still in flight when WAIT_HI) is waited for before pair 16.
+    if (WAIT_HI && i == kBlockN / 4) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
     m[i & 3] = __vimax3_s32(m[i & 3], static_cast<int>(v[2 * i]), static_cast<int>(v[2 * i + 1]));
     const uint64_t x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
     const uint64_t p2 = ((kPolyPairMask >> (i & 15)) & 1u) ? exp2_poly_pair(x2) : ex2_pair(x2);
@@ -474,8 +484,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int valid = key_end - key0;  // may be <= 0 (fully masked)
       uint32_t v[kBlockN];
       tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(v));
+      if (kSplitLd) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v));
       tmem_ld32(s_tmem + 32, *reinterpret_cast<uint32_t(*)[32]>(v + 32));
-      tmem_wait_ld();
+      if (!kSplitLd) tmem_wait_ld();
+      bool hi_pending = kSplitLd;  // columns 32..63 still loading
       // Warp-uniform: full blocks take the paths without per-key selects.
       const bool all_full = __all_sync(0xffffffffu, valid >= kBlockN);
       const uint64_t cx2 = f2_pack(c, c);
@@ -489,7 +501,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // not wait for the row max.  If any row's max moved past it, the
         // scores are read again and the block takes the general path.
         const float bb = fmaf(-12582912.0f, c, -m_ref);
-        const int mx = exp_block_max<TV>(v, cx2, f2_pack(bb, bb), sum2);
+        const int mx = exp_block_max<TV, kSplitLd>(v, cx2, f2_pack(bb, bb), sum2);
+        hi_pending = false;
         done = !__any_sync(0xffffffffu, i2f_exact(mx) * c > m_ref + 8.0f);
         if (!done) {
           sum2[0] = sum2[1] = 0ull;
@@ -499,6 +512,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!done) {
+        if (hi_pending) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
         if (!all_full) {
           // Ragged last block or causal diagonal: masked keys never win the
           // max and get p = 0 below.
