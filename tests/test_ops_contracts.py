@@ -86,3 +86,64 @@ def test_production_per_warp_scale_shapes():
           mock.patch.object(quant._fused, "quant_per_block_int8_cuda")):
         q_int8, q_scale, k_int8, k_scale = quant.per_warp_int8(q, k)
     assert q_scale.shape == (2, 4, 8) and k_scale.shape == (2, 2, 2)
+
+
+def test_fused_qk_preprocessor_has_fake_tensor_contract():
+    """turing_utils::qk_rms_rope_int8 on meta tensors (reference
+    tests/test_turing_sage_quant.py:22-50): production Q per-warp and K
+    per-block scale shapes."""
+    from comfyui_turing_utils_kernel.turing_sage.custom_ops import qk_rms_rope_int8
+
+    q = torch.empty((2, 4, 129, 128), dtype=torch.bfloat16, device="meta")
+    k = torch.empty((2, 2, 129, 128), dtype=torch.bfloat16, device="meta")
+    qn = torch.empty((128,), dtype=torch.bfloat16, device="meta")
+    kn = torch.empty((128,), dtype=torch.bfloat16, device="meta")
+    f = torch.empty((1, 129, 1, 64, 2, 2), dtype=torch.bfloat16, device="meta")
+    q8, qs, k8, ks = qk_rms_rope_int8(q, k, qn, kn, f, 1e-6, 128, "HND", "head", True, True, True)
+    assert q8.shape == q.shape and q8.dtype == torch.int8
+    assert qs.shape == (2, 4, 12) and qs.dtype == torch.float32
+    assert k8.shape == k.shape and k8.dtype == torch.int8
+    assert ks.shape == (2, 2, 3) and ks.dtype == torch.float32
+    nq = torch.empty((2, 129, 4, 128), dtype=torch.bfloat16, device="meta")
+    nk = torch.empty((2, 70, 2, 128), dtype=torch.bfloat16, device="meta")
+    _, nqs, _, nks = qk_rms_rope_int8(nq, nk, qn, kn, f, 1e-6, 0, "NHD", "row", False, False, False)
+    assert nqs.shape == (2, 4, 12) and nks.shape == (2, 2, 2)
+
+
+def test_fused_qk_preprocessor_is_a_fullgraph_leaf():
+    from comfyui_turing_utils_kernel.turing_sage.custom_ops import qk_rms_rope_int8
+
+    q = torch.empty((1, 4, 129, 64), dtype=torch.float16, device="meta")
+    k = torch.empty((1, 2, 129, 64), dtype=torch.float16, device="meta")
+    w = torch.empty((64,), dtype=torch.float16, device="meta")
+    f = torch.empty((0,), dtype=torch.float16, device="meta")
+    compiled = torch.compile(
+        lambda a, b, c, d, e: qk_rms_rope_int8(a, b, c, d, e, 1e-6, 0, "HND", "head", False,
+                                               False, False),
+        backend="eager", fullgraph=True)
+    q8, qs, k8, ks = compiled(q, k, w, w, f)
+    assert q8.shape == q.shape and qs.shape == (1, 4, 12) and ks.shape == (1, 2, 3)
+
+
+def test_fused_qk_wrapper_passes_the_production_contract():
+    """The wrapper calls the native entry with the 64/16/64 tile contract,
+    the layout id and the norm scope id (2 when the caller gives the RRMS)."""
+    q = torch.empty((2, 129, 4, 128), dtype=torch.bfloat16)
+    k = torch.empty((2, 129, 2, 128), dtype=torch.bfloat16)
+    w = torch.empty((4 * 128,), dtype=torch.bfloat16)
+    kw = torch.empty((2 * 128,), dtype=torch.bfloat16)
+    with mock.patch.object(quant._fused, "quant_qk_rms_rope_int8_cuda") as native:
+        q8, qs, k8, ks = quant.rms_rope_per_warp_int8(
+            q, k, w, kw, None, epsilon=1e-6, rot_dim=0, tensor_layout="NHD", norm_scope="row",
+            split_half=True, rotate_qk=False, stabilize_k=False)
+    args = native.call_args.args
+    assert args[0] is q and args[2] is q8 and args[4] is qs and args[5] is ks
+    assert args[9].shape == (2, 129) and args[10].shape == (2, 129)   # row RRMS scratch
+    assert args[13:] == (1e-6, 0, 64, 16, 64, 0, 1, True, False)
+    rq, rk = torch.ones((2, 129)), torch.ones((2, 129))
+    with mock.patch.object(quant._fused, "quant_qk_rms_rope_int8_cuda") as native:
+        quant.rms_rope_per_warp_int8(q, k, w, kw, None, epsilon=1e-6, rot_dim=0,
+                                     tensor_layout="NHD", norm_scope="row", split_half=False,
+                                     rotate_qk=False, stabilize_k=False, query_rrms=rq,
+                                     key_rrms=rk)
+    assert native.call_args.args[19] == 2 and native.call_args.args[9] is rq
