@@ -194,3 +194,33 @@ def test_no_watchdog_errors():
     from comfyui_turing_utils_kernel import _lib
 
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("layout,D", [("HND", 128), ("NHD", 64)])
+def test_row_sum_squares_and_given_rrms_match_row_scope(layout, D):
+    """The tensor-parallel route: per-token sums of squares over the heads
+    (tb_row_sum_squares, the row pass's reduction order), RRMS formed on the
+    host as the correctly rounded 1/sqrt(sum / (H*D) + eps), then the prologue
+    with that RRMS (norm_scope 2) — the same codes and scales as the row-scope
+    prologue that computes its own RRMS."""
+    g = torch.Generator().manual_seed(D + len(layout))
+    H, L = 5, 150
+    shape = (2, H, L, D) if layout == "HND" else (2, L, H, D)
+    q = (torch.randn(shape, generator=g) * 1.3).to(torch.bfloat16).cuda()
+    k = (torch.randn(shape, generator=g) * 0.9).to(torch.bfloat16).cuda()
+    wq = (torch.rand((H * D,), generator=g) + 0.5).to(torch.bfloat16).cuda()
+    wk = (torch.rand((H * D,), generator=g) + 0.5).to(torch.bfloat16).cuda()
+    fr = _freqs(1, L, D // 2, 7, torch.bfloat16).cuda()
+    kw = dict(epsilon=1e-6, rot_dim=D, tensor_layout=layout, norm_scope="row", split_half=False,
+              rotate_qk=False, stabilize_k=False)
+    own = quant.rms_rope_per_warp_int8(q, k, wq, wk, fr, **kw)
+
+    def rrms(t):
+        s = quant.row_sum_squares(t, tensor_layout=layout).cpu().numpy()
+        x = (s / np.float32(H * D)).astype(np.float32) + np.float32(1e-6)
+        return torch.from_numpy((1.0 / np.sqrt(x.astype(np.float64))).astype(np.float32)).cuda()
+
+    given = quant.rms_rope_per_warp_int8(q, k, wq, wk, fr, query_rrms=rrms(q), key_rrms=rrms(k),
+                                         **kw)
+    for a, b in zip(own, given):
+        assert torch.equal(a, b)
