@@ -616,7 +616,8 @@ class DiTBlockWorkload:
     n_events = 4          # step start, self-attention start, end, step end
     dominant = "sage_attn"
 
-    def __init__(self, device, world=1, rank=0, tokens=None, cpu_only=False, use_graph=True):
+    def __init__(self, device, world=1, rank=0, tokens=None, cpu_only=False, use_graph=True,
+                 max_chunks=4):
         from comfyui_turing_utils_kernel import dit_block as db
 
         self.db = db
@@ -647,7 +648,9 @@ class DiTBlockWorkload:
         self.freqs = db.rope_freqs(self.L, self.cfg.head_dim, seed=2, device=device)
         self.kops = db.KernelOps()
         self.block = db.DiTBlock(self.cfg, self.weights, self.plan, self.kops,
-                                 group=tdist.group.WORLD if world > 1 else None)
+                                 group=tdist.group.WORLD if world > 1 else None,
+                                 max_chunks=max_chunks)
+        self.config["token_chunks"] = db.token_chunks(self.L, world, max_chunks)
         self.host = [t.cpu().pin_memory() for t in (self.x, self.ctx)]
         self.out_host = torch.empty_like(self.host[0]).pin_memory()
         self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
@@ -784,7 +787,7 @@ def make_workload(args, device, seed, world=1, rank=0):
         return WORKLOADS[args.workload](device, seed, heads=args.heads)
     if args.workload == "dit_block":
         return DiTBlockWorkload(device, world, rank, tokens=args.tokens,
-                                use_graph=not args.no_graph)
+                                use_graph=not args.no_graph, max_chunks=args.chunks)
     return WORKLOADS[args.workload](device, seed)
 
 
@@ -998,6 +1001,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunks", type=int, default=4,
+                    help="dit_block: most token chunks of the multi-GPU pipeline")
     ap.add_argument("--no-graph", action="store_true",
                     help="dit_block: launch the block eagerly instead of replaying a CUDA graph")
     ap.add_argument("--tokens", type=int, default=None,

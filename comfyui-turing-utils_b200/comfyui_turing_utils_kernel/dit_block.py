@@ -458,13 +458,16 @@ class DiTBlock:
     column-parallel linear; each row-parallel linear's [tokens, dim] partial
     sums are reduce-scattered back to the token owners.
 
-    The block runs as stages over C token chunks, each stage issuing its work
-    for every chunk before the next stage waits on any chunk's collective, so
-    a chunk's all-gather / reduce-scatter (on NCCL's stream) overlaps the
-    following chunks' attention and linears: self-attention is taken per
-    query chunk after one Q/K prologue over the whole sequence; cross-
-    attention and the FFN are independent per token.  `group` is the process
-    group (None: one rank).
+    The block runs as stages over C token chunks (`token_chunks`), each stage
+    issuing its work for every chunk before the next stage waits on any
+    chunk's collective, so a chunk's all-gather / reduce-scatter (on NCCL's
+    stream) overlaps the following chunks' linears.  Self-attention runs as
+    wave-aligned launches over query rows (`attention_launches`) after one
+    Q/K prologue over the whole sequence; a chunk whose rows are finished goes
+    through O and starts its reduce-scatter under the next launch.  Cross-
+    attention and the FFN are independent per token and run per chunk.
+    `group` is the process group (None: one rank); `attn_split` overrides the
+    query row at which self-attention splits (tests).
     """
 
     def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
