@@ -40,6 +40,7 @@ struct GemmParams {
   int m, n, k;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int num_tiles;
+  int group_m;   // M-blocks per tile group (tile_coords)
   const float* a_scale;  // [m]
   const float* w_scale;  // [n]
   const float* bias;     // [n] or null
@@ -57,11 +58,19 @@ struct __align__(8) GemmShared {
   int abort_flag;
 };
 
+// Tiles run in groups of group_m M-blocks; inside a group the M-block varies
+// fastest, then the N-block.  The group's A rows (group_m * 128 * K bytes,
+// sized to stay in L2) are then reused across every N-block instead of
+// streaming all of A from HBM once per N-block, which is what an M-fastest
+// order does once A outgrows L2.  The last group may hold fewer M-blocks.
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& m0, int& n0) {
-  const int mb = tile % p.num_m_blocks;
-  const int nb = tile / p.num_m_blocks;
-  m0 = mb * kBM;
-  n0 = nb * kBN;
+  const int per_group = p.group_m * p.num_n_blocks;
+  const int g = tile / per_group;
+  const int first_m = g * p.group_m;
+  const int rows = min(p.group_m, p.num_m_blocks - first_m);
+  const int local = tile - g * per_group;
+  m0 = (first_m + local % rows) * kBM;
+  n0 = (local / rows) * kBN;
 }
 
 // Waits without honouring the abort flag: used on the exit path to drain
@@ -306,6 +315,11 @@ void gemm_i8_launch(const int8_t* a, const int8_t* w, int64_t m, int64_t n, int6
   p.num_n_blocks = static_cast<int>((n + kBN - 1) / kBN);
   p.num_k_blocks = static_cast<int>((k + kBK - 1) / kBK);
   p.num_tiles = p.num_m_blocks * p.num_n_blocks;
+  // About 24 MB of A rows per group: with the weight (B) that the group
+  // sweeps, it fits the 126 MB L2.
+  constexpr int64_t kGroupABytes = 24ll << 20;
+  const int64_t gm = kGroupABytes / (static_cast<int64_t>(kBM) * k);
+  p.group_m = static_cast<int>(gm < 1 ? 1 : (gm > p.num_m_blocks ? p.num_m_blocks : gm));
   p.a_scale = a_scale;
   p.w_scale = w_scale;
   p.bias = bias;
