@@ -21,6 +21,11 @@ and distributions — the reference benchmarks on no public dataset):
              per-token rotations, INT8 Q/K in one pass, then the attention.
              Step = prologue + attention; the prologue is reported against
              the HBM roofline beside the attention's.
+  w8a8_attention
+             configs[1] shape through the dense W8A8-PV backend (the loader's
+             default): randomized-Hadamard Q/K INT8 with the conditional K
+             anchor, channel-wise INT8 V, P as u8 codes.  Step = the three
+             quantizers + attention.
   linear     configs[0]: ConvRot W8A8 linear, X [4096, 5120] bf16 with 0.5%
              outlier channels x20, W [13824, 5120] int8, per-channel scales,
              bf16 bias.  Step = ConvRot INT8 quantize + tcgen05 GEMM with the
@@ -603,6 +608,43 @@ class AttentionRopeWorkload(AttentionWorkload):
                        "those rows and all 32760 keys, then fp32 SDPA")
 
 
+class W8A8AttentionWorkload(AttentionWorkload):
+    """configs[1] attention through the dense W8A8-PV path (the loader's
+    default ``w8a8`` backend, turing_sage/core.py:656-708): rotated and
+    anchored INT8 Q/K, channel-wise INT8 V, P packed to u8 codes."""
+    name = "w8a8_attention"
+    config = dict(AttentionWorkload.config,
+                  workload="w8a8_pv_attention (BASELINE configs[1] shape, dense W8A8 backend)",
+                  k_smoothing="anchor row (conditional)", q_quant="int8 per 16-token warp tile, "
+                  "randomized Hadamard", k_quant="int8 per 64-token block, randomized Hadamard",
+                  pv="u8 P codes x int8 V codes (exact, fp16 tensor path), fp32 accumulation")
+
+    def __init__(self, device, seed, heads=None):
+        super().__init__(device, seed, heads=heads)
+        self.name = "w8a8_attention" if heads in (None, 40) else f"w8a8_attention_h{heads}"
+        # K anchor, rotated Q/K, V amax, V codes, V scale, attention.
+        self.launches_per_step = 6
+
+    def step(self, ev=None):
+        if ev:
+            ev[0].record()
+        pre = self.core.prequantize_sol_sageattn(self.q, self.k, self.v, use_w8a8=True,
+                                                 force_dense=True)
+        if ev:
+            ev[1].record()
+        out = self.core.sol_sparse_sageattn_from_prequantized(pre)
+        if ev:
+            ev[2].record()
+        return out
+
+    def step_e2e(self):
+        dev = self.q.device
+        q, k, v = (t.to(dev, non_blocking=True) for t in self.host)
+        out = self.ts.w8a8attn(q, k, v, tensor_layout="HND")
+        self.out_host.copy_(out, non_blocking=True)
+        return out
+
+
 class DiTBlockWorkload:
     """one Wan2.1-14B-shaped DiT block (dim 5120, 40 heads
     of 128, FFN 13824, L = 75600 video tokens, 512 text tokens, batch 1) on
@@ -778,12 +820,13 @@ class DiTBlockWorkload:
 
 
 WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload,
-             "attention_rope": AttentionRopeWorkload, "dit_block": DiTBlockWorkload,
+             "attention_rope": AttentionRopeWorkload, "w8a8_attention": W8A8AttentionWorkload,
+             "dit_block": DiTBlockWorkload,
              "codebook": CodebookWorkload, "w4a4_ffn": W4A4FFNWorkload}
 
 
 def make_workload(args, device, seed, world=1, rank=0):
-    if args.workload in ("attention", "attention_rope"):
+    if args.workload in ("attention", "attention_rope", "w8a8_attention"):
         return WORKLOADS[args.workload](device, seed, heads=args.heads)
     if args.workload == "dit_block":
         return DiTBlockWorkload(device, world, rank, tokens=args.tokens,

@@ -7,6 +7,8 @@ and written in place, as in the reference.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from ._lib import TB_LAYOUT_HND, TB_LAYOUT_NHD, call, dtype_code, ptr, stream_of
@@ -198,3 +200,62 @@ def row_sum_squares_cuda(input, sums, tensor_layout):
         call("tb_row_sum_squares", ptr(input), ptr(sums), B, H, L, D, st.data_ptr(),
              dtype_code(input), stream_of(input))
 
+
+
+def _rotated(query, key, query_output, key_output, query_scale, key_scale, anchor_indices,
+             query_block_size, query_warp_block_size, key_block_size, tensor_layout):
+    for name, t in (("query", query), ("key", key), ("query_output", query_output),
+                    ("key_output", key_output), ("query_scale", query_scale),
+                    ("key_scale", key_scale)):
+        _check(t.is_cuda, f"{name} must be a CUDA tensor")
+    _check(query_output.dtype == torch.int8 and key_output.dtype == torch.int8,
+           "Q/K outputs must be int8")
+    _check(query_scale.dtype == torch.float32 and key_scale.dtype == torch.float32,
+           "Q/K scales must be float32")
+    _check(query_output.is_contiguous() and key_output.is_contiguous()
+           and query_scale.is_contiguous() and key_scale.is_contiguous(),
+           "Q/K outputs and scales must be contiguous")
+    _check(query.dtype == key.dtype,
+           "Query and key must have the same data type")
+    _check(query.size(0) == key.size(0), "Query and key batch size must match")
+    _check(query.size(3) == key.size(3), "Query and key head_dim must match")
+    _check((int(query_block_size), int(query_warp_block_size), int(key_block_size)) == (64, 16, 64),
+           "the sm_100a rotated quantizer takes the production 64/16/64 tiles")
+    layout = int(tensor_layout)
+    B, Hq, Lq, D, qb, qh, ql = _geometry(query, layout)
+    _, Hk, Lk, _, kb, kh, kl = _geometry(key, layout)
+    _check(tuple(query_output.shape) == tuple(query.shape)
+           and tuple(key_output.shape) == tuple(key.shape), "Q/K output shapes must match inputs")
+    _check(tuple(query_scale.shape) == (B, Hq, (Lq + 63) // 64 * 4), "query_scale shape mismatch")
+    _check(tuple(key_scale.shape) == (B, Hk, (Lk + 63) // 64), "key_scale shape mismatch")
+    if anchor_indices is not None:
+        _check(anchor_indices.is_cuda and anchor_indices.dtype == torch.int32
+               and anchor_indices.is_contiguous() and tuple(anchor_indices.shape) == (B, Hk),
+               "K anchor scratch must be a contiguous int32 [B, Hk] CUDA tensor")
+        _check(anchor_indices.device == key.device,
+               "K anchor scratch must be on the same CUDA device as K")
+    _, _, _, _, qob, qoh, qol = _geometry(query_output, layout)
+    _, _, _, _, kob, koh, kol = _geometry(key_output, layout)
+    strides = (ctypes.c_int64 * 12)(qb, qh, ql, kb, kh, kl, qob, qoh, qol, kob, koh, kol)
+    with torch.cuda.device(query.device):
+        call("tb_quant_qk_int8_rotated", ptr(query), ptr(key), ptr(query_output), ptr(key_output),
+             ptr(query_scale), ptr(key_scale), ptr(anchor_indices), B, Hq, Hk, Lq, Lk, D,
+             strides, dtype_code(query), stream_of(query))
+
+
+def quant_qk_per_warp_int8_rotated_cuda(query, key, query_output, key_output, query_scale,
+                                        key_scale, query_block_size, query_warp_block_size,
+                                        key_block_size, tensor_layout):
+    """Randomized-Hadamard Q/K INT8 without K anchoring (fused.cu:1252-1268)."""
+    _rotated(query, key, query_output, key_output, query_scale, key_scale, None,
+             query_block_size, query_warp_block_size, key_block_size, tensor_layout)
+
+
+def quant_qk_per_warp_int8_rotated_anchored_cuda(query, key, query_output, key_output,
+                                                 query_scale, key_scale, anchor_indices,
+                                                 query_block_size, query_warp_block_size,
+                                                 key_block_size, tensor_layout):
+    """Randomized-Hadamard Q/K INT8 with the conditional K anchor
+    (fused.cu:1270-1287); anchor_indices receives the chosen rows (or -1)."""
+    _rotated(query, key, query_output, key_output, query_scale, key_scale, anchor_indices,
+             query_block_size, query_warp_block_size, key_block_size, tensor_layout)

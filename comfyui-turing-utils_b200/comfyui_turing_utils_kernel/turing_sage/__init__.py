@@ -7,8 +7,8 @@ import importlib
 
 import torch
 
-from .quant import (per_warp_int8, quantize_key_per_block, quantize_query_per_warp,
-                    rms_rope_per_warp_int8)
+from .quant import (per_warp_int8, per_warp_int8_hadamard, quantize_key_per_block,
+                    quantize_query_per_warp, rms_rope_per_warp_int8)
 
 
 def available() -> bool:
@@ -36,12 +36,20 @@ def fused_qk_preprocessing_available() -> bool:
     return hasattr(module, "quant_qk_rms_rope_int8_cuda")
 
 
+def w8a8_available() -> bool:
+    """True when the dense W8A8-PV attention is present (turing_sage/__init__.py:52-62
+    of the reference probes the extension for quantize_v_int8_sm75)."""
+    if not available():
+        return False
+    module = importlib.import_module("comfyui_turing_utils_kernel._sage_qattn_sm75")
+    return hasattr(module, "quantize_v_int8_sm75")
+
+
 # The plugin probes these before choosing a backend (turing_sage/__init__.py:25-145 of the
-# reference).  The sparse (Sol/SLA), W8A8-PV, varlen and VAE overlap kernels are not part of
-# this package, so each probe answers False and the plugin keeps the plain Sage INT8 backend.
+# reference).  The sparse (Sol/SLA), varlen and VAE overlap kernels are not part of this
+# package, so each of these probes answers False.
 sparse_available = _not_built
 sla_available = _not_built
-w8a8_available = _not_built
 w8a8_varlen_available = _not_built
 split_prequantization_available = _not_built
 overlap_blend_available = _not_built
@@ -89,11 +97,51 @@ def sageattn_from_prequantized(*args, **kwargs):
     return _impl(*args, **kwargs)
 
 
+def w8a8attn(*args, **kwargs):
+    """Dense W8A8-PV attention (turing_sage/__init__.py:304-307)."""
+    from .core import w8a8attn as _impl
+
+    return _impl(*args, **kwargs)
+
+
+def w8a8attn_compiled(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                      tensor_layout: str = "HND", is_causal: bool = False,
+                      sm_scale: float | None = None, key_tile_tokens: int = 0,
+                      rotate_qk: bool = True, stabilize_k: bool = True):
+    """torch.compile leaf (turing_sage/__init__.py:310-334)."""
+    from .custom_ops import w8a8_attention
+
+    return w8a8_attention(q, k, v, tensor_layout, bool(is_causal),
+                          float(sm_scale) if sm_scale is not None else -1.0,
+                          int(key_tile_tokens), bool(rotate_qk), bool(stabilize_k))
+
+
+def prequantize_sol_sageattn(*args, **kwargs):
+    from .core import prequantize_sol_sageattn as _impl
+
+    return _impl(*args, **kwargs)
+
+
+def prequantize_sol_sageattn_from_qk(*args, **kwargs):
+    from .core import prequantize_sol_sageattn_from_qk as _impl
+
+    return _impl(*args, **kwargs)
+
+
+def sol_sparse_sageattn_from_prequantized(*args, **kwargs):
+    from .core import sol_sparse_sageattn_from_prequantized as _impl
+
+    return _impl(*args, **kwargs)
+
+
 from . import custom_ops  # noqa: E402,F401  (registers the turing_utils:: sage custom ops)
 
 __all__ = ["available", "fused_qk_preprocessing_available", "overlap_accumulate_available",
-           "overlap_blend_available", "per_warp_int8", "prequantize_rms_rope_qk", "prequantize_sageattn",
-           "prequantize_sageattn_from_qk", "quantize_key_per_block", "rms_rope_per_warp_int8",
-           "quantize_query_per_warp", "sageattn", "sageattn_compiled",
-           "sageattn_from_prequantized", "sla_available", "sparse_available",
-           "split_prequantization_available", "w8a8_available", "w8a8_varlen_available"]
+           "overlap_blend_available", "per_warp_int8", "per_warp_int8_hadamard",
+           "prequantize_rms_rope_qk", "prequantize_sageattn", "prequantize_sageattn_from_qk",
+           "prequantize_sol_sageattn", "prequantize_sol_sageattn_from_qk",
+           "quantize_key_per_block", "rms_rope_per_warp_int8", "quantize_query_per_warp",
+           "sageattn", "sageattn_compiled", "sageattn_from_prequantized", "sla_available",
+           "sol_sparse_sageattn_from_prequantized", "sparse_available",
+           "split_prequantization_available", "w8a8_available", "w8a8_varlen_available",
+           "w8a8attn", "w8a8attn_compiled"]

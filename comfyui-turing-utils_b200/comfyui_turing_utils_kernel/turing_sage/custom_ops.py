@@ -1,4 +1,5 @@
-"""``turing_utils::sage_attention`` (turing_sage/custom_ops.py:137-167) and
+"""``turing_utils::sage_attention`` (turing_sage/custom_ops.py:137-167),
+``turing_utils::w8a8_attention`` (custom_ops.py:170-210) and
 ``turing_utils::qk_rms_rope_int8`` (custom_ops.py:63-130) custom ops: same
 schemas and fake implementations, backed by the sm_100a kernels."""
 from __future__ import annotations
@@ -52,3 +53,21 @@ def _qk_rms_rope_int8_fake(query, key, query_norm, key_norm, freqs, epsilon, rot
     return (torch.empty_like(query, dtype=torch.int8), query_scale,
             torch.empty_like(key, dtype=torch.int8), key_scale)
 
+
+
+@torch.library.custom_op("turing_utils::w8a8_attention", mutates_args=())
+def w8a8_attention(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                   tensor_layout: str, is_causal: bool, sm_scale: float, key_tile_tokens: int,
+                   rotate_qk: bool, stabilize_k: bool) -> torch.Tensor:
+    from .core import w8a8attn
+
+    return w8a8attn(query, key, value, tensor_layout=tensor_layout, is_causal=is_causal,
+                    sm_scale=sm_scale if sm_scale > 0.0 else None,
+                    key_tile_tokens=key_tile_tokens, rotate_qk=rotate_qk,
+                    stabilize_k=stabilize_k)
+
+
+@w8a8_attention.register_fake
+def _w8a8_attention_fake(query, key, value, tensor_layout, is_causal, sm_scale, key_tile_tokens,
+                         rotate_qk, stabilize_k):
+    return torch.empty_like(query)

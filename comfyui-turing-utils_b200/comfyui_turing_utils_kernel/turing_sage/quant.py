@@ -120,3 +120,27 @@ def row_sum_squares(x: torch.Tensor, tensor_layout: str = "HND") -> torch.Tensor
     _fused.row_sum_squares_cuda(x, sums, 0 if tensor_layout == "NHD" else 1)
     return sums
 
+
+
+def per_warp_int8_hadamard(q: torch.Tensor, k: torch.Tensor, BLKQ: int = 64, WARPQ: int = 16,
+                           BLKK: int = 64, tensor_layout: str = "HND", stabilize_k: bool = True):
+    """Fuse the shared randomized Hadamard transform into Q/K quantization
+    (quant.py:182-243): Q per 16-row warp tile, K per 64-key block, K first
+    centred on its anchor row when stabilize_k and the anchor test passes."""
+    batch, q_heads, q_tokens = _geometry(q, tensor_layout)
+    _, kv_heads, kv_tokens = _geometry(k, tensor_layout)
+    q_int8 = torch.empty(q.shape, dtype=torch.int8, device=q.device)
+    k_int8 = torch.empty(k.shape, dtype=torch.int8, device=k.device)
+    q_scale = torch.empty((batch, q_heads, ((q_tokens + BLKQ - 1) // BLKQ) * (BLKQ // WARPQ)),
+                          device=q.device, dtype=torch.float32)
+    k_scale = torch.empty((batch, kv_heads, (kv_tokens + BLKK - 1) // BLKK), device=q.device,
+                          dtype=torch.float32)
+    layout_id = 0 if tensor_layout == "NHD" else 1
+    if stabilize_k:
+        anchor_indices = torch.empty((batch, kv_heads), dtype=torch.int32, device=q.device)
+        _fused.quant_qk_per_warp_int8_rotated_anchored_cuda(
+            q, k, q_int8, k_int8, q_scale, k_scale, anchor_indices, BLKQ, WARPQ, BLKK, layout_id)
+    else:
+        _fused.quant_qk_per_warp_int8_rotated_cuda(q, k, q_int8, k_int8, q_scale, k_scale, BLKQ,
+                                                   WARPQ, BLKK, layout_id)
+    return q_int8, q_scale, k_int8, k_scale

@@ -223,25 +223,6 @@ int tb_token_mean(const void* input, int dtype, void* mean, int64_t B, int64_t H
 }  // extern "C"
 
 // ------------------------------------------------------------ attention ----
-namespace tb {
-struct AttnArgs {
-  const int8_t* q;
-  const int8_t* k;
-  const void* v;
-  int v_dtype;
-  void* out;
-  int out_dtype;
-  const float* q_scale;
-  const float* k_scale;
-  float* lse;
-  int64_t B, Hq, Hk, Lq, Lk, D;
-  int64_t q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl, o_sb, o_sh, o_sl;
-  int64_t q_tiles_scale, k_tiles_scale;
-  int causal;
-  float sm_scale;
-};
-void sage_attn_launch(const AttnArgs& a, cudaStream_t stream);
-}  // namespace tb
 
 extern "C" int tb_qk_int8_sv_f16_accum_f32_attn(
     const int8_t* q, const int8_t* k, const void* v, int v_dtype, void* out, int out_dtype,
@@ -282,6 +263,79 @@ extern "C" int tb_qk_int8_sv_f16_accum_f32_attn(
     a.k_tiles_scale = (Lk + 63) / 64;
     a.causal = is_causal;
     a.sm_scale = sm_scale;
+    tb::sage_attn_launch(a, static_cast<cudaStream_t>(stream));
+  });
+}
+
+// ------------------------------------------------------ W8A8-PV attention ----
+
+extern "C" int tb_quant_qk_int8_rotated(const void* query, const void* key, int8_t* query_out,
+                                        int8_t* key_out, float* query_scale, float* key_scale,
+                                        int32_t* anchors, int64_t batch, int64_t query_heads,
+                                        int64_t key_heads, int64_t query_length,
+                                        int64_t key_length, int64_t head_dim,
+                                        const int64_t* strides, int dtype, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(query && key && strides, "query and key must be CUDA tensors");
+    tb::require_sm100();
+    tb::rot_quant_launch(query, key, query_out, key_out, query_scale, key_scale, anchors, batch,
+                         query_heads, key_heads, query_length, key_length, head_dim, strides,
+                         dtype, static_cast<cudaStream_t>(stream));
+  });
+}
+
+extern "C" int tb_quantize_v_int8(const void* value, int dtype, void* codes_f16,
+                                  int8_t* codes_channel_major, float* scale, int64_t batch,
+                                  int64_t heads, int64_t length, int64_t head_dim,
+                                  int64_t padded_length, const int64_t* strides,
+                                  tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(value && strides, "value must be a CUDA tensor");
+    tb::require_sm100();
+    tb::v_quant_launch(value, dtype, static_cast<uint16_t*>(codes_f16), codes_channel_major, scale,
+                       batch, heads, length, head_dim, padded_length, strides[0], strides[1],
+                       strides[2], static_cast<cudaStream_t>(stream));
+  });
+}
+
+extern "C" int tb_w8a8_attn(const int8_t* q, const int8_t* k, const void* v_codes,
+                            const float* v_scale, void* out, int out_dtype, const float* q_scale,
+                            const float* k_scale, int64_t B, int64_t Hq, int64_t Hk, int64_t Lq,
+                            int64_t Lk, int64_t D, const int64_t* strides, int is_causal,
+                            float sm_scale, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(q && k && v_codes && v_scale && out && q_scale && k_scale && strides,
+               "query, key, value codes, output and scales must be CUDA tensors");
+    TB_REQUIRE(B > 0 && Hq > 0 && Hk > 0 && Lq > 0 && Lk > 0, "empty Q/K sequences are not supported");
+    TB_REQUIRE(Hq % Hk == 0, "prequantized Sol W8A8 Q heads must be divisible by KV heads");
+    TB_REQUIRE(Lq <= INT32_MAX && Lk <= INT32_MAX, "sequence length exceeds the kernel range");
+    TB_REQUIRE(is_causal == 0 || is_causal == 1, "is_causal must be 0 or 1");
+    tb::require_sm100();
+    tb::AttnArgs a{};
+    a.q = q;
+    a.k = k;
+    a.v = v_codes;
+    a.v_dtype = TB_DTYPE_F16;
+    a.out = out;
+    a.out_dtype = out_dtype;
+    a.q_scale = q_scale;
+    a.k_scale = k_scale;
+    a.lse = nullptr;
+    a.B = B;
+    a.Hq = Hq;
+    a.Hk = Hk;
+    a.Lq = Lq;
+    a.Lk = Lk;
+    a.D = D;
+    a.q_sb = strides[0]; a.q_sh = strides[1]; a.q_sl = strides[2];
+    a.k_sb = strides[3]; a.k_sh = strides[4]; a.k_sl = strides[5];
+    a.v_sb = strides[6]; a.v_sh = strides[7]; a.v_sl = strides[8];
+    a.o_sb = strides[9]; a.o_sh = strides[10]; a.o_sl = strides[11];
+    a.q_tiles_scale = (Lq + 63) / 64 * 4;
+    a.k_tiles_scale = (Lk + 63) / 64;
+    a.causal = is_causal;
+    a.sm_scale = sm_scale;
+    a.v_scale = v_scale;
     tb::sage_attn_launch(a, static_cast<cudaStream_t>(stream));
   });
 }

@@ -37,6 +37,16 @@
 // TMEM columns: O0 [0,128) O1 [128,256) and S(t, b) at 256 + 128 t + 64 b;
 // P_t(j) is written as packed 16-bit pairs over the first 32 columns of its
 // S buffer.
+//
+// W8A8 variant (dense W8A8-PV, kernel/csrc/turing/sage/sol_sparse_cuda_sm75.cu:
+// 1197-1320, attn_utils.cuh:465-625, 793-841): the reference point is the
+// exact running max m = max_j fma(max_t s_t, c_j, -log2 255), so that
+// p = 2^fma(s, c, -m) lies in (0, 255]; P enters PV as its u8 code rni(p)
+// and V as its per-channel INT8 code, both carried as exact fp16 integers;
+// d sums the unrounded p and the epilogue multiplies by the V channel scale.
+// Every product and every 16-key partial sum of PV is an integer below 2^24,
+// so the fp16 tensor path computes the reference's u8 x s8 products exactly;
+// the fp32 accumulator in TMEM takes the rescale that an INT32 one could not.
 // Every wait is bounded (tb_common.cuh).
 #include "tb_capi_internal.h"
 #include "tb_tu.cuh"
@@ -78,6 +88,7 @@ struct AttnParams {
   float* lse;                     // [B, Hq, Lq] base-2 or null
   float sm_scale_log2;            // sm_scale * log2(e)
   int causal;
+  const float* v_scale;           // W8A8: [B, Hk, D] channel scales of the V codes
 };
 
 template <int D>
@@ -236,13 +247,23 @@ __device__ __forceinline__ uint32_t pack_pair(uint64_t p2) {
   return r;
 }
 
+// W8A8 P code of a pair: rni_sat_u8(p) as exact fp16 values (p reaches 255.5
+// only when |m| >= 2^16).
+__device__ __forceinline__ uint32_t u8_code_pair(uint64_t p2) {
+  const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t r2 = f2_add(p2, rnd2);
+  const uint64_t c2 = f2_pack(fminf(f2_lo(r2), 12583167.0f), fminf(f2_hi(r2), 12583167.0f));
+  return pack_pair<__half>(f2_sub(c2, rnd2));
+}
+
 // The fast path of a full block: p = exp2(s * c - m_ref) against the current
 // reference, in place as exp_block, with the integer row max of the raw
 // scores accumulated in the same loop (the ALU work of the max hides under
-// the exponentials).  Returns that max.
-template <typename TV, bool WAIT_HI>
+// the exponentials).  Returns that max.  W8A8 as in exp_block.
+template <typename TV, bool WAIT_HI, bool W8A8>
 __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
                                              uint64_t (&sum2)[2]) {
+  const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
   int m[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
 #pragma unroll
   for (int i = 0; i < kBlockN / 2; ++i) {
@@ -250,10 +271,14 @@ __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx
     // 32..63 (still in flight when WAIT_HI) is waited for before pair 16.
     if (WAIT_HI && i == kBlockN / 4) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
     m[i & 3] = __vimax3_s32(m[i & 3], static_cast<int>(v[2 * i]), static_cast<int>(v[2 * i + 1]));
-    const uint64_t x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
-    const uint64_t p2 = ((kPolyPairMask >> (i & 15)) & 1u) ? exp2_poly_pair(x2) : ex2_pair(x2);
+    uint64_t x2;
+    if constexpr (W8A8) x2 = f2_fma(f2_sub(magic_pair(v[2 * i], v[2 * i + 1]), rnd2), cx2, bx2);
+    else x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
+    const uint64_t p2 =
+        (!W8A8 && ((kPolyPairMask >> (i & 15)) & 1u)) ? exp2_poly_pair(x2) : ex2_pair(x2);
     sum2[i & 1] = f2_add(sum2[i & 1], p2);
-    v[i] = pack_pair<TV>(p2);
+    if constexpr (W8A8) v[i] = u8_code_pair(p2);
+    else v[i] = pack_pair<TV>(p2);
   }
   return max(max(m[0], m[1]), max(m[2], m[3]));
 }
@@ -261,23 +286,35 @@ __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx
 // p = exp2(s * c - m_ref) for the 64 scores of a block, in place: packed pair
 // i (16-bit P) overwrites v[i], whose score was consumed by pair i / 2.  The
 // row sum of p accumulates in sum2.  MASKED zeroes keys >= valid; it is
-// instantiated separately so full blocks carry no per-key selects.
-template <typename TV, bool MASKED>
+// instantiated separately so full blocks carry no per-key selects.  (The
+// reference scores masked keys -5e6, attn_utils.cuh:407-461, which gives them
+// 2^(-5e6 c - m): exactly 0 in fp32 unless c < ~2.6e-5, i.e. unless Q/K scales
+// are degenerate; there the reference's output carries the padding's mass and
+// this kernel's does not.)
+//
+// W8A8: x = fma(s, c, -m) with s the exact float of the score (bx2 = -m) and
+// P = the fp16 of rni_sat_u8(p) (the sum takes the unrounded p).
+template <typename TV, bool MASKED, bool W8A8>
 __device__ __forceinline__ void exp_block(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
                                           int valid, uint64_t (&sum2)[2]) {
+  const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
 #pragma unroll
   for (int i = 0; i < kBlockN / 2; ++i) {
-    const uint64_t x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
-    uint64_t p2 = ((kPolyPairMask >> (i & 15)) & 1u) ? exp2_poly_pair(x2) : ex2_pair(x2);
+    uint64_t x2;
+    if constexpr (W8A8) x2 = f2_fma(f2_sub(magic_pair(v[2 * i], v[2 * i + 1]), rnd2), cx2, bx2);
+    else x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
+    uint64_t p2 = (!W8A8 && ((kPolyPairMask >> (i & 15)) & 1u)) ? exp2_poly_pair(x2) : ex2_pair(x2);
     if constexpr (MASKED) {
       p2 = f2_pack(2 * i < valid ? f2_lo(p2) : 0.0f, 2 * i + 1 < valid ? f2_hi(p2) : 0.0f);
     }
     sum2[i & 1] = f2_add(sum2[i & 1], p2);
-    v[i] = pack_pair<TV>(p2);
+    if constexpr (W8A8) v[i] = u8_code_pair(p2);
+    else v[i] = pack_pair<TV>(p2);
   }
 }
 
-template <int D, typename TV, bool CAUSAL>
+// TV: 16-bit type of P and V in the PV contraction; TO: output type.
+template <int D, typename TV, typename TO, bool CAUSAL, bool W8A8>
 __global__ void __launch_bounds__(kThreads, 1)
     sage_attn_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
@@ -496,14 +533,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // integer addition to the float bits) and b = -(1.5 * 2^23 * c) - m_ref:
       // one packed FMA per key pair.
       bool done = false;
+      bool need_rescale = false;  // some row of the warp moved its reference point
+      float f = 1.0f;             // this row's rescale factor 2^(m_old - m_new)
       if (all_full && __all_sync(0xffffffffu, m_ref != -INFINITY)) {
         // Usual case: the reference point stands, so the exponentials need
-        // not wait for the row max.  If any row's max moved past it, the
-        // scores are read again and the block takes the general path.
-        const float bb = fmaf(-12582912.0f, c, -m_ref);
-        const int mx = exp_block_max<TV, kSplitLd>(v, cx2, f2_pack(bb, bb), sum2);
+        // not wait for the row max.  If any row's max moved past it (W8A8:
+        // past the exact running max, so P stays <= 255 and the codes are
+        // the reference's), the scores are read again and the block takes
+        // the general path.
+        const float bb = W8A8 ? -m_ref : fmaf(-12582912.0f, c, -m_ref);
+        const int mx = exp_block_max<TV, kSplitLd, W8A8>(v, cx2, f2_pack(bb, bb), sum2);
         hi_pending = false;
-        done = !__any_sync(0xffffffffu, i2f_exact(mx) * c > m_ref + 8.0f);
+        done = !__any_sync(0xffffffffu, W8A8 ? fmaf(i2f_exact(mx), c, -7.9943534f) > m_ref
+                                             : i2f_exact(mx) * c > m_ref + 8.0f);
         if (!done) {
           sum2[0] = sum2[1] = 0ull;
           tmem_ld32(s_tmem, *reinterpret_cast<uint32_t(*)[32]>(v));
@@ -532,45 +574,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           a[q] = max(m, static_cast<int>(w[15]));
         }
         const int mx = max(__vimax3_s32(a[0], a[1], a[2]), a[3]);
-        const float m_blk = mx != INT32_MIN ? i2f_exact(mx) * c : -INFINITY;
-        // New reference point when the row max grew by more than 2^8; rows
-        // that already had one rescale O and d once PV(j - 1) is done: the
-        // commit of S_t(j + 1), issued right after PV(j - 1), marks it, and
-        // o_done (phase 0) marks PV(n_kv - 2) when no S_t(j + 1) exists.
-        const bool move = m_blk > m_ref + 8.0f;
+        // W8A8 keeps the reference's offset point fma(max, c, -log2 255).
+        const float m_blk = mx == INT32_MIN ? -INFINITY
+                            : W8A8          ? fmaf(i2f_exact(mx), c, -7.9943534f)
+                                            : i2f_exact(mx) * c;
+        // New reference point when the row max grew by more than 2^8 (W8A8:
+        // at all); rows that already had one scale d now and O below, after
+        // P(j) is stored, so the exponentials overlap the wait for PV(j - 1).
+        const bool move = W8A8 ? m_blk > m_ref : m_blk > m_ref + 8.0f;
         const bool rescale = move && j > 0 && m_ref != -INFINITY;
-        if (__any_sync(0xffffffffu, rescale)) {
-          const bool waited =
-              j + 1 < n_kv
-                  ? mbar_wait(&bar->s_full[t][(j + 1) & 1], static_cast<uint32_t>((j + 1) >> 1) & 1u,
-                              abort_flag, kDevWaitTimeoutSoftmax)
-                  : mbar_wait(&bar->o_done[t], 0u, abort_flag, kDevWaitTimeoutSoftmax);
-          ok = __all_sync(0xffffffffu, waited);
-          if (!ok) break;
-          tc_fence_after();
-          const float f = rescale ? ex2(m_ref - m_blk) : 1.0f;
-          dsum *= f;
-#pragma unroll 1
-          for (int cc = 0; cc < D / 16; ++cc) {
-            uint32_t o[16];
-            tmem_ld16(o_tmem + cc * 16, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st16(o_tmem + cc * 16, o);
-          }
-          tmem_wait_st();
-        }
+        need_rescale = __any_sync(0xffffffffu, rescale);
+        f = rescale ? ex2(m_ref - m_blk) : 1.0f;
+        dsum *= f;
         if (move) m_ref = m_blk;
         const float nm = (m_ref == -INFINITY) ? 0.0f : -m_ref;
-        const float bb = fmaf(-12582912.0f, c, nm);
+        const float bb = W8A8 ? nm : fmaf(-12582912.0f, c, nm);
         const uint64_t bx2 = f2_pack(bb, bb);
-        if (all_full) exp_block<TV, false>(v, cx2, bx2, valid, sum2);
-        else exp_block<TV, true>(v, cx2, bx2, valid, sum2);
+        if (all_full) exp_block<TV, false, W8A8>(v, cx2, bx2, valid, sum2);
+        else exp_block<TV, true, W8A8>(v, cx2, bx2, valid, sum2);
       }
       tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(v));
       const uint64_t s01 = f2_add(sum2[0], sum2[1]);
       dsum += f2_lo(s01) + f2_hi(s01);
+      if (need_rescale) {
+        // O holds PV(0..j-1) once PV(j - 1) is done: the commit of
+        // S_t(j + 1), issued right after PV(j - 1), marks it, and o_done
+        // (phase 0) marks PV(n_kv - 2) when no S_t(j + 1) exists.  PV(j)
+        // waits for this warp's p_full arrival below.
+        const bool waited =
+            j + 1 < n_kv
+                ? mbar_wait(&bar->s_full[t][(j + 1) & 1], static_cast<uint32_t>((j + 1) >> 1) & 1u,
+                            abort_flag, kDevWaitTimeoutSoftmax)
+                : mbar_wait(&bar->o_done[t], 0u, abort_flag, kDevWaitTimeoutSoftmax);
+        ok = __all_sync(0xffffffffu, waited);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int cc = 0; cc < D / 16; ++cc) {
+          uint32_t o[16];
+          tmem_ld16(o_tmem + cc * 16, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st16(o_tmem + cc * 16, o);
+        }
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -582,22 +630,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       tc_fence_after();
       const float inv = dsum > 0.0f ? 1.0f / dsum : 0.0f;
-      TV* orow = static_cast<TV*>(p.out) + b * p.o_sb + h * p.o_sh +
+      TO* orow = static_cast<TO*>(p.out) + b * p.o_sb + h * p.o_sh +
                  static_cast<int64_t>(row) * p.o_sl;
+      const float* vs = W8A8 ? p.v_scale + static_cast<int64_t>(b * p.Hk + hk) * D : nullptr;
 #pragma unroll 1
       for (int cc = 0; cc < D / 16; ++cc) {
         uint32_t o[16];
         tmem_ld16(o_tmem + cc * 16, o);
         tmem_wait_ld();
+        float f[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) f[i] = __uint_as_float(o[i]) * inv;
+        if constexpr (W8A8) {
+          // (O / d) * v_scale[c] (attn_utils.cuh:923-965 order).
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 s4 = __ldg(reinterpret_cast<const float4*>(vs + cc * 16 + i));
+            f[i] *= s4.x;
+            f[i + 1] *= s4.y;
+            f[i + 2] *= s4.z;
+            f[i + 3] *= s4.w;
+          }
+        }
         if (row < p.Lq) {
-          uint4 w0 = make_uint4(pack2<TV>(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv),
-                                pack2<TV>(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv),
-                                pack2<TV>(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv),
-                                pack2<TV>(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv));
-          uint4 w1 = make_uint4(pack2<TV>(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv),
-                                pack2<TV>(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv),
-                                pack2<TV>(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv),
-                                pack2<TV>(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv));
+          uint4 w0 = make_uint4(pack2<TO>(f[0], f[1]), pack2<TO>(f[2], f[3]),
+                                pack2<TO>(f[4], f[5]), pack2<TO>(f[6], f[7]));
+          uint4 w1 = make_uint4(pack2<TO>(f[8], f[9]), pack2<TO>(f[10], f[11]),
+                                pack2<TO>(f[12], f[13]), pack2<TO>(f[14], f[15]));
           *reinterpret_cast<uint4*>(orow + cc * 16) = w0;
           *reinterpret_cast<uint4*>(orow + cc * 16 + 8) = w1;
         }
@@ -632,28 +691,21 @@ void make_map_4d(CUtensorMap* map, CUtensorMapDataType dt, const void* base, int
 
 }  // namespace
 
-struct AttnArgs {
-  const int8_t* q;
-  const int8_t* k;
-  const void* v;
-  int v_dtype;
-  void* out;
-  int out_dtype;
-  const float* q_scale;
-  const float* k_scale;
-  float* lse;
-  int64_t B, Hq, Hk, Lq, Lk, D;
-  int64_t q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl, o_sb, o_sh, o_sl;
-  int64_t q_tiles_scale, k_tiles_scale;
-  int causal;
-  float sm_scale;
-};
-
 void sage_attn_launch(const AttnArgs& a, cudaStream_t stream) {
+  const bool w8a8 = a.v_scale != nullptr;
   TB_REQUIRE(a.D == 128, "the sm_100a Sage attention kernel takes head_dim 128 (pad 64 < D < 128)");
-  TB_REQUIRE(a.v_dtype == a.out_dtype, "value and output dtypes must match");
-  TB_REQUIRE(a.v_dtype == TB_DTYPE_BF16 || a.v_dtype == TB_DTYPE_F16,
-             "value must be float16 or bfloat16");
+  if (w8a8) {
+    TB_REQUIRE(a.v_dtype == TB_DTYPE_F16, "W8A8 V codes must be the fp16 codes of the V quantizer");
+    TB_REQUIRE(a.out_dtype == TB_DTYPE_BF16 || a.out_dtype == TB_DTYPE_F16,
+               "output must be float16 or bfloat16");
+    TB_REQUIRE(a.lse == nullptr, "the W8A8 attention returns no log-sum-exp");
+    TB_REQUIRE((reinterpret_cast<uintptr_t>(a.v_scale) & 15u) == 0,
+               "V scale must be 16-byte aligned");
+  } else {
+    TB_REQUIRE(a.v_dtype == a.out_dtype, "value and output dtypes must match");
+    TB_REQUIRE(a.v_dtype == TB_DTYPE_BF16 || a.v_dtype == TB_DTYPE_F16,
+               "value must be float16 or bfloat16");
+  }
   TB_REQUIRE(a.Hq % a.Hk == 0, "num_qo_heads must be divisible by num_kv_heads");
   TB_REQUIRE(a.B <= 65535 && a.Hq <= 65535, "batch/head count exceeds the grid range");
   TB_REQUIRE(a.q_sl % 16 == 0 && a.q_sh % 16 == 0 && a.q_sb % 16 == 0 && a.k_sl % 16 == 0 &&
@@ -694,20 +746,31 @@ void sage_attn_launch(const AttnArgs& a, cudaStream_t stream) {
   p.lse = a.lse;
   p.sm_scale_log2 = a.sm_scale * 1.4426950408889634f;
   p.causal = a.causal;
+  p.v_scale = a.v_scale;
   const size_t smem = AttnSmem<D>::kDataBytes + sizeof(AttnBarriers) + 1024;
   dim3 grid(static_cast<unsigned>((a.Lq + kBlockM * kQTiles - 1) / (kBlockM * kQTiles)),
             static_cast<unsigned>(a.Hq), static_cast<unsigned>(a.B));
-#define TB_ATTN_LAUNCH(TV, CAUSAL)                                                      \
+#define TB_ATTN_LAUNCH(TV, TO, CAUSAL, W8A8)                                            \
   {                                                                                     \
-    auto kern = sage_attn_kernel<D, TV, CAUSAL>;                                        \
+    auto kern = sage_attn_kernel<D, TV, TO, CAUSAL, W8A8>;                              \
     TB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                        static_cast<int>(smem)));                        \
     kern<<<grid, kThreads, smem, stream>>>(tq, tk, tv, p);                              \
   }
-  if (a.v_dtype == TB_DTYPE_BF16) {
-    if (a.causal) TB_ATTN_LAUNCH(__nv_bfloat16, true) else TB_ATTN_LAUNCH(__nv_bfloat16, false)
+  if (w8a8) {
+    if (a.out_dtype == TB_DTYPE_BF16) {
+      if (a.causal) TB_ATTN_LAUNCH(__half, __nv_bfloat16, true, true)
+      else TB_ATTN_LAUNCH(__half, __nv_bfloat16, false, true)
+    } else {
+      if (a.causal) TB_ATTN_LAUNCH(__half, __half, true, true)
+      else TB_ATTN_LAUNCH(__half, __half, false, true)
+    }
+  } else if (a.v_dtype == TB_DTYPE_BF16) {
+    if (a.causal) TB_ATTN_LAUNCH(__nv_bfloat16, __nv_bfloat16, true, false)
+    else TB_ATTN_LAUNCH(__nv_bfloat16, __nv_bfloat16, false, false)
   } else {
-    if (a.causal) TB_ATTN_LAUNCH(__half, true) else TB_ATTN_LAUNCH(__half, false)
+    if (a.causal) TB_ATTN_LAUNCH(__half, __half, true, false)
+    else TB_ATTN_LAUNCH(__half, __half, false, false)
   }
 #undef TB_ATTN_LAUNCH
   TB_CUDA_CHECK(cudaGetLastError());

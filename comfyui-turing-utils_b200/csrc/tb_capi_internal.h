@@ -71,7 +71,35 @@ void encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, int rank, co
                        const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                        CUtensorMapSwizzle swizzle);
 
+// Attention launch arguments (sage_attn.cu).  v_scale == null: Sage (16-bit
+// V of the output dtype); else W8A8-PV (fp16 V codes, [B, Hk, D] scales).
+struct AttnArgs {
+  const int8_t* q;
+  const int8_t* k;
+  const void* v;
+  int v_dtype;
+  void* out;
+  int out_dtype;
+  const float* q_scale;
+  const float* k_scale;
+  float* lse;
+  int64_t B, Hq, Hk, Lq, Lk, D;
+  int64_t q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl, o_sb, o_sh, o_sl;
+  int64_t q_tiles_scale, k_tiles_scale;
+  int causal;
+  float sm_scale;
+  const float* v_scale;
+};
+
 // Kernels implemented in the other translation units.
+void sage_attn_launch(const AttnArgs& a, cudaStream_t stream);
+void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out, float* q_scale,
+                      float* k_scale, int32_t* anchors, int64_t B, int64_t Hq, int64_t Hk,
+                      int64_t Lq, int64_t Lk, int64_t D, const int64_t* strides, int dtype,
+                      cudaStream_t stream);
+void v_quant_launch(const void* v, int dtype, uint16_t* codes_f16, int8_t* codes_cm, float* scale,
+                    int64_t B, int64_t H, int64_t L, int64_t D, int64_t Lpad, int64_t sb,
+                    int64_t sh, int64_t sl, cudaStream_t stream);
 void convrot_quantize_impl(const void* input, int dtype, int64_t rows, int64_t k, int act,
                            int int4, int staged, void* rotated, float* partial, int8_t* out,
                            float* scales, cudaStream_t stream);

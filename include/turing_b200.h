@@ -305,6 +305,60 @@ TB_API int tb_qk_int8_sv_f16_accum_f32_attn(const int8_t *q, const int8_t *k, co
                                             int qk_quant_gran, float sm_scale,
                                             tb_stream_t stream);
 
+/* ----------------------------------------------- W8A8-PV attention ---- */
+
+/* Randomized-Hadamard INT8 Q/K of the W8A8 attention: each token row of D = 64
+ * or 128 channels becomes H_D diag(sign) x / sqrt(D) (the reference's sign
+ * vector and butterfly order), then Q is quantized per 16-token tile into
+ * query_scale [B, Hq, ceil(Lq/64)*4] and K per 64-token block into key_scale
+ * [B, Hk, ceil(Lk/64)], amax floor 1e-7, scale = amax / 127, codes
+ * rni(x * 127 / amax).  anchors: int32 [B, Hk] scratch, or NULL; when given,
+ * each (batch, kv head) first picks its K anchor row (or -1) from nine sampled
+ * keys and that row is subtracted from every key before the rotation.
+ * strides (elements, 12 values): q (b, h, l), k (b, h, l), q_out (b, h, l),
+ * k_out (b, h, l); last dimension contiguous, Q/K rows 16-byte aligned, the
+ * INT8 outputs 8-byte aligned.  dtype BF16 / F16.  Replaces
+ * quant_qk_per_warp_int8_rotated_anchored_cuda (anchors given) and
+ * quant_qk_per_warp_int8_rotated_cuda (NULL) (kernel/csrc/turing/sage/
+ * fused.h:55-78, fused.cu:1252-1287 with the kernels at :201-639). */
+TB_API int tb_quant_qk_int8_rotated(const void *query, const void *key, int8_t *query_out,
+                                    int8_t *key_out, float *query_scale, float *key_scale,
+                                    int32_t *anchors, int64_t batch, int64_t query_heads,
+                                    int64_t key_heads, int64_t query_length, int64_t key_length,
+                                    int64_t head_dim, const int64_t *strides, int dtype,
+                                    tb_stream_t stream);
+
+/* Channel-wise INT8 V: per (batch, head, channel) scale = max(amax over the
+ * tokens / 127, 1e-12) into scale [B, H, D] fp32 (also the kernels' amax
+ * scratch while they run), codes rni(v / scale).  Outputs (at least one):
+ * codes_f16 [B, H, L, D] contiguous fp16 holding the integer codes exactly
+ * (the operand of tb_w8a8_attn), and/or codes_channel_major int8
+ * [B, H, D, padded_length] (padded_length a multiple of 64 >= L, padding 0;
+ * the reference's layout without its sm75 16-token fragment permutation).
+ * strides: v (b, h, l) in elements; D = 64 or 128; dtype BF16 / F16.
+ * Replaces attn_cuda_sm75.h:112-114 quantize_v_int8_sm75
+ * (quant_v_int8_cuda_sm75.cu:58-246). */
+TB_API int tb_quantize_v_int8(const void *value, int dtype, void *codes_f16,
+                              int8_t *codes_channel_major, float *scale, int64_t batch,
+                              int64_t heads, int64_t length, int64_t head_dim,
+                              int64_t padded_length, const int64_t *strides, tb_stream_t stream);
+
+/* Dense W8A8-PV attention: INT8 Q/K with per-warp Q / per-block K scales (as
+ * tb_qk_int8_sv_f16_accum_f32_attn, HND or strided), V as the fp16 codes of
+ * tb_quantize_v_int8 with v_scale [B, Hk, D]; per row the softmax reference
+ * point is the exact running max minus log2 255, P = rni(2^(s c - m)) in
+ * [0, 255] multiplies the V codes exactly, d sums the unrounded p, and
+ * out = O / d * v_scale (out_dtype BF16 / F16).  strides: q, k, v_codes, out
+ * (b, h, l) in elements; D = 128 (pad 64 < D < 128).  Replaces the dense
+ * (force_dense) path of attn_cuda_sm75.h:61-83
+ * sol_sparse_online_w8a8_prequantized_attn (sol_sparse_cuda_sm75.cu:709-1394,
+ * 2767-2932). */
+TB_API int tb_w8a8_attn(const int8_t *q, const int8_t *k, const void *v_codes,
+                        const float *v_scale, void *out, int out_dtype, const float *q_scale,
+                        const float *k_scale, int64_t B, int64_t Hq, int64_t Hk, int64_t Lq,
+                        int64_t Lk, int64_t D, const int64_t *strides, int is_causal,
+                        float sm_scale, tb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -67,6 +67,12 @@ def lib() -> ctypes.CDLL:
         L.orc_qk_rms_rope.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _i64, _int, _int, _int, _int, ctypes.c_float, _ptr,
                                       _ptr]
+        L.orc_k_anchor.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _ptr]
+        L.orc_rot_quant.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ptr,
+                                    _ptr, _ptr]
+        L.orc_quant_v.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr]
+        L.orc_w8a8_attn.argtypes = [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64,
+                                    _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _ptr]
         L.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
         L.orc_e4m3_to_f32.restype = ctypes.c_float
         for name in ("orc_f32_to_bf16", "orc_bf16_to_f32", "orc_f32_to_f16", "orc_f16_to_f32"):
@@ -293,6 +299,116 @@ def qk_rms_rope_int8(x_bits: np.ndarray, norm_bits: np.ndarray, freqs_bits, *, t
     if layout == "NHD":
         out = np.ascontiguousarray(out.transpose(0, 2, 1, 3))
     return out, scale
+
+
+def _hnd(x_bits, layout):
+    x = _c(x_bits, np.uint16)
+    if layout == "NHD":
+        return np.ascontiguousarray(x.transpose(0, 2, 1, 3))
+    if layout != "HND":
+        raise ValueError(f"Unknown tensor layout: {layout}")
+    return x
+
+
+def k_anchor(k_bits: np.ndarray, *, layout: str = "HND", fp16: bool = False) -> np.ndarray:
+    """K stabilization anchor row per (batch, kv head), or -1
+    (DetectKAnchorKernel, sage/fused.cu:406-556).  Returns int32 [B, Hk]."""
+    k = _hnd(k_bits, layout)
+    B, H, L, D = k.shape
+    out = np.empty((B, H), np.int32)
+    lib().orc_k_anchor(_p(k), int(fp16), B * H, L, D, L * D, D, _p(out))
+    return out
+
+
+def rot_quant(x_bits: np.ndarray, tile_tokens: int, *, layout: str = "HND", fp16: bool = False,
+              anchor: np.ndarray | None = None, block: int | None = None):
+    """Randomized-Hadamard per-tile INT8 (quant_int8_tile, sage/fused.cu:260-398)
+    of a [B, H, L, D] (HND) / [B, L, H, D] (NHD) tensor with D = 64 or 128.
+    tile_tokens 16 (Q, per-warp layout: pass block=64) or 64 (K).  anchor:
+    optional int32 [B, H] rows subtracted first (K).  Returns (codes int8 in the
+    input layout, scale fp32 [B, H, tiles])."""
+    x = _hnd(x_bits, layout)
+    B, H, L, D = x.shape
+    if D not in (64, 128):
+        raise ValueError("rot_quant takes the kernel head dim 64 or 128 (pad first)")
+    tiles = (L + tile_tokens - 1) // tile_tokens
+    if block is not None:
+        tiles = (L + block - 1) // block * (block // tile_tokens)
+    out = np.empty(x.shape, np.int8)
+    scale = np.empty((B, H, tiles), np.float32)
+    a = None if anchor is None else _c(anchor, np.int32).reshape(B * H)
+    lib().orc_rot_quant(_p(x), int(fp16), B * H, L, D, L * D, D, tile_tokens, tiles,
+                        None if a is None else _p(a), _p(out), _p(scale))
+    if layout == "NHD":
+        out = np.ascontiguousarray(out.transpose(0, 2, 1, 3))
+    return out, scale
+
+
+def per_warp_int8_hadamard(q_bits, k_bits, *, layout: str = "HND", fp16: bool = False,
+                           stabilize_k: bool = True):
+    """Q per 16 rows and K per 64 rows, both rotated, K anchored when
+    stabilize_k (turing_sage/quant.py:182-243).  Returns (q8, q_scale, k8,
+    k_scale, anchors or None)."""
+    anchors = k_anchor(k_bits, layout=layout, fp16=fp16) if stabilize_k else None
+    q8, qs = rot_quant(q_bits, 16, layout=layout, fp16=fp16, block=64)
+    k8, ks = rot_quant(k_bits, 64, layout=layout, fp16=fp16, anchor=anchors)
+    return q8, qs, k8, ks, anchors
+
+
+def quant_v(v_bits: np.ndarray, *, layout: str = "HND", fp16: bool = False):
+    """Channel-wise INT8 V (quant_v_int8_cuda_sm75.cu:58-164).  Returns (codes
+    int8 [B, H, D, ceil(L/64)*64] channel-major, un-permuted; scale fp32
+    [B, H, D])."""
+    v = _hnd(v_bits, layout)
+    B, H, L, D = v.shape
+    lpad = (L + 63) // 64 * 64
+    codes = np.empty((B, H, D, lpad), np.int8)
+    scale = np.empty((B, H, D), np.float32)
+    lib().orc_quant_v(_p(v), int(fp16), B * H, L, D, L * D, D, lpad, _p(codes), _p(scale))
+    return codes, scale
+
+
+def w8a8_attn(q8, k8, v8, v_scale, q_scale, k_scale, *, sm_scale: float,
+              is_causal: bool = False) -> np.ndarray:
+    """Dense W8A8-PV attention (sol_sparse_cuda_sm75.cu:1197-1320) on HND INT8
+    Q/K, channel-major INT8 V [B, Hk, D, Lpad] and their scales.  Returns the
+    fp32 output [B, Hq, Lq, D] before the final rounding."""
+    q8, k8, v8 = _c(q8, np.int8), _c(k8, np.int8), _c(v8, np.int8)
+    B, Hq, Lq, D = q8.shape
+    Hk, Lk = k8.shape[1], k8.shape[2]
+    qs, ks, vs = _c(q_scale, np.float32), _c(k_scale, np.float32), _c(v_scale, np.float32)
+    out = np.empty((B, Hq, Lq, D), np.float32)
+    lib().orc_w8a8_attn(_p(q8), _p(k8), _p(v8), _p(vs), _p(qs), _p(ks), B, Hq, Hk, Lq, Lk, D,
+                        v8.shape[3], qs.shape[2], ks.shape[2], float(sm_scale),
+                        int(bool(is_causal)), _p(out))
+    return out
+
+
+def w8a8attn(q_bits, k_bits, v_bits, *, layout: str = "HND", fp16: bool = False,
+             sm_scale: float | None = None, is_causal: bool = False, rotate_qk: bool = True,
+             stabilize_k: bool = True) -> np.ndarray:
+    """The whole dense W8A8 path (turing_sage/core.py:656-708 with
+    prequantize_sol_sageattn :842-914): head dim padded to 64 / 128, rotated
+    (anchored) or plain per-warp Q/K INT8, channel-wise INT8 V, W8A8-PV
+    attention, output rounded to the input dtype.  Returns output bits
+    (uint16) in the input layout with the original head dim."""
+    q, k, v = (_hnd(t, layout) for t in (q_bits, k_bits, v_bits))
+    D = q.shape[-1]
+    kd = 64 if D <= 64 else 128
+    if D < kd:
+        q, k, v = (np.pad(t, ((0, 0), (0, 0), (0, 0), (0, kd - D))) for t in (q, k, v))
+    if rotate_qk:
+        q8, qs, k8, ks, _ = per_warp_int8_hadamard(q, k, fp16=fp16, stabilize_k=stabilize_k)
+    else:
+        q8, qs = sage_quant(q, 16, fp16=fp16, block=64)
+        k8, ks = sage_quant(k, 64, fp16=fp16)
+    v8, vs = quant_v(v, fp16=fp16)
+    scale = float(sm_scale) if sm_scale is not None else D ** -0.5
+    o = w8a8_attn(q8, k8, v8, vs, qs, ks, sm_scale=scale, is_causal=is_causal)
+    bits = (f32_to_f16 if fp16 else f32_to_bf16)(o)[..., :D]
+    if layout == "NHD":
+        bits = bits.transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(bits)
 
 
 def q_scale_shape(B, H, L, block=64, warp=16):

@@ -547,6 +547,279 @@ void orc_qk_rms_rope(const uint16_t *x, const uint16_t *norm, const uint16_t *fr
     free(nrm);
 }
 
+/* ------------------------------------------------ W8A8-PV attention ---- */
+
+/* Sign of channel c in the shared randomized Hadamard transform of Q and K
+ * (kernel/csrc/turing/sage/fused.cu:201-213): bit c of the 128-bit sign word,
+ * clear = negate.  The table is part of the format: Q/K codes depend on it. */
+static const uint32_t kRotSigns[4] = {0x1035997bu, 0x8087f5eeu, 0xee2e4e1au, 0x71132418u};
+
+static inline int rot_negative(int c) { return ((kRotSigns[c >> 5] >> (c & 31)) & 1u) == 0u; }
+
+/* In-place randomized Walsh-Hadamard transform of one D-channel row (D = 64 or
+ * 128) in the reference's operation order (fused.cu:215-258): signs, then the
+ * butterflies of channel bits 0, 1, 2 (inside an 8-channel pack) and 3.. (across
+ * packs), each stage lo' = lo + hi, hi' = lo - hi, then one multiply by
+ * 1/sqrt(D) (0.125 or 0.08838834764831845f). */
+static void rot_row(float *v, int D) {
+    for (int c = 0; c < D; ++c)
+        if (rot_negative(c)) v[c] = -v[c];
+    for (int span = 1; span < D; span <<= 1) {
+        for (int base = 0; base < D; base += 2 * span) {
+            for (int o = 0; o < span; ++o) {
+                const float lo = v[base + o], hi = v[base + o + span];
+                v[base + o] = lo + hi;
+                v[base + o + span] = lo - hi;
+            }
+        }
+    }
+    const float norm = D == 64 ? 0.125f : 0.08838834764831845f;
+    for (int c = 0; c < D; ++c) v[c] *= norm;
+}
+
+/* Sum / max over the 32 lanes of a warp by the shfl_down tree (offsets 16, 8,
+ * 4, 2, 1) as lane 0 sees it; lanes without a partner keep their own value. */
+static float warp_tree(const float *lane_vals, int is_max) {
+    float a[32];
+    memcpy(a, lane_vals, sizeof(a));
+    for (int off = 16; off > 0; off >>= 1) {
+        float b[32];
+        for (int i = 0; i < 32; ++i) {
+            const float other = i + off < 32 ? a[i + off] : a[i];
+            b[i] = is_max ? fmaxf(a[i], other) : a[i] + other;
+        }
+        memcpy(a, b, sizeof(a));
+    }
+    return a[0];
+}
+
+/* K stabilization anchor of each (batch, kv head) (DetectKAnchorKernel,
+ * fused.cu:406-556): nine keys at rows s * (L - 1) / 8, the sample nearest
+ * their mean (squared distance of 9 * sample - sum), kept only when centring
+ * on it lowers the energy of the samples and grows their range by at most
+ * 12.5 %.  128 threads, one channel each, warp trees, then the four warps in
+ * order.  anchor[o] = row index or -1. */
+void orc_k_anchor(const uint16_t *k, int fp16, int64_t outer, int64_t L, int64_t D,
+                  int64_t s_outer, int64_t s_tok, int32_t *anchor) {
+    enum { NS = 9, NT = 128 };
+    for (int64_t o = 0; o < outer; ++o) {
+        float samp[NS][128];
+        for (int s = 0; s < NS; ++s) {
+            const int64_t row = (int64_t)s * (L - 1) / (NS - 1);
+            for (int c = 0; c < 128; ++c)
+                samp[s][c] = c < D ? elem(k, o * s_outer + row * s_tok + c, fp16) : 0.0f;
+        }
+        float oe[NT], om[NT], cd[NS][NT];
+        for (int t = 0; t < NT; ++t) {
+            oe[t] = om[t] = 0.0f;
+            for (int c = 0; c < NS; ++c) cd[c][t] = 0.0f;
+            if (t >= D) continue;
+            float sum = 0.0f;
+            for (int s = 0; s < NS; ++s) {
+                const float v = samp[s][t];
+                oe[t] = fmaf(v, v, oe[t]);
+                om[t] = fmaxf(om[t], fabsf(v));
+                sum += v;
+            }
+            for (int c = 0; c < NS; ++c) {
+                const float dist = fmaf(9.0f, samp[c][t], -sum);  /* 9 * x is exact */
+                cd[c][t] = fmaf(dist, dist, cd[c][t]);
+            }
+        }
+        float w_oe[4], w_om[4], w_cd[NS][4];
+        for (int w = 0; w < 4; ++w) {
+            w_oe[w] = warp_tree(oe + 32 * w, 0);
+            w_om[w] = warp_tree(om + 32 * w, 1);
+            for (int c = 0; c < NS; ++c) w_cd[c][w] = warp_tree(cd[c] + 32 * w, 0);
+        }
+        int best = 0;
+        float best_d = 3.402823466e+38F;
+        for (int c = 0; c < NS; ++c) {
+            float d = 0.0f;
+            for (int w = 0; w < 4; ++w) d += w_cd[c][w];
+            if (d < best_d) {
+                best = c;
+                best_d = d;
+            }
+        }
+        float be[NT], bm[NT];
+        for (int t = 0; t < NT; ++t) {
+            be[t] = bm[t] = 0.0f;
+            if (t >= D) continue;
+            for (int s = 0; s < NS; ++s) {
+                const float r = samp[s][t] - samp[best][t];
+                be[t] = fmaf(r, r, be[t]);
+                bm[t] = fmaxf(bm[t], fabsf(r));
+            }
+        }
+        float toe = 0.0f, tom = 0.0f, tbe = 0.0f, tbm = 0.0f;
+        for (int w = 0; w < 4; ++w) {
+            toe += w_oe[w];
+            tom = fmaxf(tom, w_om[w]);
+            tbe += warp_tree(be + 32 * w, 0);
+            tbm = fmaxf(tbm, warp_tree(bm + 32 * w, 1));
+        }
+        const int keep = tbe < toe && tbm <= tom * 1.125f;
+        anchor[o] = keep ? (int32_t)((int64_t)best * (L - 1) / (NS - 1)) : -1;
+    }
+}
+
+/* Randomized-Hadamard per-tile INT8 quantizer (quant_int8_tile, fused.cu:260-398):
+ * per tile of T tokens (16: Q per warp; 64: K per block) the rows, minus the
+ * anchor row when anchor[o] >= 0 (K only), are rotated (rot_row), amax starts
+ * at 1e-7, scale = amax / 127, codes = rni_sat(x * (127 / amax)).  IEEE
+ * divides (the reference's extension uses --use_fast_math).  x and out share
+ * strides; scale is [outer, tiles]. */
+void orc_rot_quant(const uint16_t *x, int fp16, int64_t outer, int64_t L, int64_t D,
+                   int64_t s_outer, int64_t s_tok, int64_t T, int64_t tiles,
+                   const int32_t *anchor, int8_t *out, float *scale) {
+    float *buf = (float *)malloc(sizeof(float) * (size_t)(T * D));
+    float anc[128];
+    for (int64_t o = 0; o < outer; ++o) {
+        const int32_t a = anchor ? anchor[o] : -1;
+        if (a >= 0)
+            for (int64_t c = 0; c < D; ++c) anc[c] = elem(x, o * s_outer + (int64_t)a * s_tok + c, fp16);
+        for (int64_t t = 0; t < tiles; ++t) {
+            float amax = 0.0000001f;
+            for (int64_t i = 0; i < T; ++i) {
+                const int64_t tok = t * T + i;
+                float *v = buf + i * D;
+                if (tok >= L) continue;
+                for (int64_t c = 0; c < D; ++c) {
+                    v[c] = elem(x, o * s_outer + tok * s_tok + c, fp16);
+                    if (a >= 0) v[c] -= anc[c];
+                }
+                rot_row(v, (int)D);
+                for (int64_t c = 0; c < D; ++c) amax = fmaxf(amax, fabsf(v[c]));
+            }
+            scale[o * tiles + t] = amax / 127.0f;
+            const float inv = 127.0f / amax;
+            for (int64_t i = 0; i < T; ++i) {
+                const int64_t tok = t * T + i;
+                if (tok >= L) continue;
+                for (int64_t c = 0; c < D; ++c)
+                    out[o * s_outer + tok * s_tok + c] = cvt_rni_sat_s8(buf[i * D + c] * inv);
+            }
+        }
+    }
+    free(buf);
+}
+
+/* Channel-wise INT8 V (quantize_value_kernel, quant_v_int8_cuda_sm75.cu:58-164):
+ * per (outer, channel) amax over the L tokens, scale = max(amax / 127, 1e-12),
+ * codes = rni_sat(v * (1 / scale)), written channel-major [outer, D, Lpad]
+ * (tokens >= L zero).  The reference also permutes each run of 16 tokens for
+ * its sm75 fragment loads; this layout is the un-permuted one. */
+void orc_quant_v(const uint16_t *v, int fp16, int64_t outer, int64_t L, int64_t D,
+                 int64_t s_outer, int64_t s_tok, int64_t Lpad, int8_t *codes, float *scale) {
+    for (int64_t o = 0; o < outer; ++o) {
+        for (int64_t c = 0; c < D; ++c) {
+            float amax = 0.0f;
+            for (int64_t t = 0; t < L; ++t)
+                amax = fmaxf(amax, fabsf(elem(v, o * s_outer + t * s_tok + c, fp16)));
+            const float sc = fmaxf(amax / 127.0f, 1.0e-12f);
+            const float inv = 1.0f / sc;
+            scale[o * D + c] = sc;
+            int8_t *dst = codes + (o * D + c) * Lpad;
+            for (int64_t t = 0; t < Lpad; ++t)
+                dst[t] = t < L ? cvt_rni_sat_s8(elem(v, o * s_outer + t * s_tok + c, fp16) * inv) : 0;
+        }
+    }
+}
+
+/* cvt.rni.sat.u8.f32 (attn_utils.cuh:588-597). */
+static inline int32_t cvt_rni_sat_u8(float x) {
+    if (isnan(x)) return 0;
+    float r = nearbyintf(x);
+    if (r > 255.0f) r = 255.0f;
+    if (r < 0.0f) r = 0.0f;
+    return (int32_t)r;
+}
+
+/* Dense W8A8-PV attention (sparse_attention_kernel<UseW8A8, ForceDense>,
+ * sol_sparse_cuda_sm75.cu:1197-1320; update_mdo / RS_to_u8 /
+ * compute_int8_sv_permuted / normalize_d, attn_utils.cuh:465-585, 599-622,
+ * 793-841, 923-965).  Per query row and 64-key block j, with
+ * c_j = (sm_scale * log2 e) * q_scale[row / 16] * k_scale[j]:
+ *   m_blk = fma(max_t s_t, c_j, -7.9943534)   (s_t = exact INT32 score;
+ *           masked keys -5e6; 7.9943534 = log2 255)
+ *   m' = max(m, m_blk);  d, O *= 2^(m - m');
+ *   p_t = 2^fma(s_t, c_j, -m') in (0, 255];  P_t = rni_sat_u8(p_t)
+ *         (masked keys: p_t = 0; the reference's -5e6 sentinel gives them
+ *         2^fma(-5e6, c_j, -m'), which is exactly 0 in fp32 unless c_j is
+ *         below ~2.6e-5, i.e. unless the Q/K scales are degenerate);
+ *   d += sum p_t;  O[c] += (float)(sum_t P_t * V8[c, t])   (exact INT32)
+ * and out[c] = O[c] * (1 / d) * v_scale[c] (fp32; the caller rounds to the
+ * output dtype).  m starts at -5e6 and d at 1; exp2f stands for the
+ * reference's ex2.approx.  q/k int8 [B, H, L, D] contiguous; v8 [B, Hk, D,
+ * Lpad]; q_scale [B, Hq, q_tiles] (per 16 rows); k_scale [B, Hk, k_tiles]. */
+void orc_w8a8_attn(const int8_t *q, const int8_t *k, const int8_t *v8, const float *v_scale,
+                   const float *q_scale, const float *k_scale, int64_t B, int64_t Hq, int64_t Hk,
+                   int64_t Lq, int64_t Lk, int64_t D, int64_t Lpad, int64_t q_tiles,
+                   int64_t k_tiles, float sm_scale, int causal, float *out) {
+    const float scale_log2 = sm_scale * 1.44269504088896340736f;
+    const int64_t nblk = (Lk + 63) / 64;
+    float *O = (float *)malloc(sizeof(float) * (size_t)D);
+    for (int64_t b = 0; b < B; ++b) {
+        for (int64_t h = 0; h < Hq; ++h) {
+            const int64_t hk = h / (Hq / Hk);
+            const int8_t *kh = k + (b * Hk + hk) * Lk * D;
+            const int8_t *vh = v8 + (b * Hk + hk) * D * Lpad;
+            const float *ksh = k_scale + (b * Hk + hk) * k_tiles;
+            const float *vsh = v_scale + (b * Hk + hk) * D;
+            for (int64_t i = 0; i < Lq; ++i) {
+                const int8_t *qi = q + ((b * Hq + h) * Lq + i) * D;
+                const float cq = scale_log2 * q_scale[(b * Hq + h) * q_tiles + i / 16];
+                const int64_t nb = causal ? (i / 64 + 1 < nblk ? i / 64 + 1 : nblk) : nblk;
+                float m = -5000000.0f, d = 1.0f;
+                for (int64_t c = 0; c < D; ++c) O[c] = 0.0f;
+                for (int64_t j = 0; j < nb; ++j) {
+                    const float cj = cq * ksh[j];
+                    float s[64];
+                    float mx = -5000000.0f;
+                    for (int t = 0; t < 64; ++t) {
+                        const int64_t key = j * 64 + t;
+                        if (key >= Lk || (causal && key > i)) {
+                            s[t] = -5000000.0f;
+                        } else {
+                            int32_t acc = 0;
+                            const int8_t *kk = kh + key * D;
+                            for (int64_t c = 0; c < D; ++c) acc += (int32_t)qi[c] * (int32_t)kk[c];
+                            s[t] = (float)acc;
+                        }
+                        mx = fmaxf(mx, s[t]);
+                    }
+                    const float m_new = fmaxf(m, fmaf(mx, cj, -7.9943534f));
+                    const float f = exp2f(m - m_new);
+                    d *= f;
+                    for (int64_t c = 0; c < D; ++c) O[c] *= f;
+                    m = m_new;
+                    int32_t pu[64];
+                    float psum = 0.0f;
+                    for (int t = 0; t < 64; ++t) {
+                        const int64_t key = j * 64 + t;
+                        const int masked = key >= Lk || (causal && key > i);
+                        const float pt = masked ? 0.0f : exp2f(fmaf(s[t], cj, -m));
+                        pu[t] = cvt_rni_sat_u8(pt);
+                        psum += pt;
+                    }
+                    d += psum;
+                    for (int64_t c = 0; c < D; ++c) {
+                        int32_t acc = 0;
+                        const int8_t *vc = vh + c * Lpad + j * 64;
+                        for (int t = 0; t < 64; ++t) acc += pu[t] * (int32_t)vc[t];
+                        O[c] += (float)acc;
+                    }
+                }
+                const float inv = 1.0f / d;
+                float *orow = out + ((b * Hq + h) * Lq + i) * D;
+                for (int64_t c = 0; c < D; ++c) orow[c] = O[c] * inv * vsh[c];
+            }
+        }
+    }
+    free(O);
+}
+
 /* ------------------------------------------------------------ helpers ---- */
 
 void orc_f32_to_bf16(const float *x, int64_t n, uint16_t *out) {

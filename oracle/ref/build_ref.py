@@ -8,7 +8,7 @@ oracle/_ref/ (git-ignored; it travels to the GPU box with the snapshot):
     the CUTLASS 2.x headers vendored in site-packages, plus
     oracle/ref/ref_linear_shim.cu (C entry points);
   * ref_sage*.so — kernel/csrc/turing/sage/{fused,qk_preprocess,
-    qk_int_sv_f16_cuda_sm75}.cu
+    qk_int_sv_f16_cuda_sm75,sol_sparse_cuda_sm75,quant_v_int8_cuda_sm75}.cu
     with the reference's attention flags (adds --use_fast_math,
     kernel/setup.py:483-497), as a torch extension built here with
     torch.utils.cpp_extension (not the reference's own setup.py).
@@ -77,7 +77,8 @@ def build_sage() -> None:
     sage = CSRC / "turing" / "sage"
     load(name="ref_sage",
          sources=[str(HERE / "ref_sage_shim.cpp"), str(sage / "fused.cu"),
-                  str(sage / "qk_preprocess.cu"), str(sage / "qk_int_sv_f16_cuda_sm75.cu")],
+                  str(sage / "qk_preprocess.cu"), str(sage / "qk_int_sv_f16_cuda_sm75.cu"),
+                  str(sage / "sol_sparse_cuda_sm75.cu"), str(sage / "quant_v_int8_cuda_sm75.cu")],
          extra_include_paths=[str(CSRC / "turing"), str(sage)],
          extra_cflags=["-O3", "-DENABLE_BF16=1", "-std=c++17"],
          extra_cuda_cflags=[*ARCH, *COMMON, "--use_fast_math"],

@@ -126,10 +126,67 @@ def qkrope_fixtures(dev, S) -> dict:
     return fx
 
 
+def w8a8_fixtures(dev, S) -> dict:
+    """Dense W8A8-PV path: rotated (anchored) Q/K INT8 (sage/fused.cu:201-639),
+    channel-wise INT8 V (quant_v_int8_cuda_sm75.cu:58-246) and the force_dense
+    attention (sol_sparse_cuda_sm75.cu:709-1394, 2767-2932).  v8 is stored as
+    the reference writes it (16-token permuted)."""
+    fx = {}
+    cases = [  # name, dtype, Hq, Hk, Lq, Lk, D, stabilize_k, causal, K offset
+        ("w8a8_bf16_d128_anchor", torch.bfloat16, 2, 2, 200, 200, 128, True, False, 2.0),
+        ("w8a8_f16_d64_gqa", torch.float16, 4, 2, 130, 190, 64, False, False, 0.0),
+        ("w8a8_bf16_d128_causal", torch.bfloat16, 1, 1, 300, 300, 128, True, True, 1.0),
+    ]
+    for i, (name, dt, hq, hk, lq, lk, d, stab, causal, off) in enumerate(cases):
+        g = torch.Generator().manual_seed(9100 + i)
+        q = (torch.randn((1, hq, lq, d), generator=g) * 1.5).to(dt)
+        k = (torch.randn((1, hk, lk, d), generator=g)
+             + torch.randn((1, hk, 1, d), generator=g) * off).to(dt)
+        v = torch.randn((1, hk, lk, d), generator=g).to(dt)
+        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        q8 = torch.empty(q.shape, dtype=torch.int8, device=dev)
+        k8 = torch.empty(k.shape, dtype=torch.int8, device=dev)
+        qs = torch.empty((1, hq, (lq + 63) // 64 * 4), dtype=torch.float32, device=dev)
+        ks = torch.empty((1, hk, (lk + 63) // 64), dtype=torch.float32, device=dev)
+        rec = {"q": bits(q), "k": bits(k), "v": bits(v)}
+        if stab:
+            anchors = torch.empty((1, hk), dtype=torch.int32, device=dev)
+            S.quant_qk_per_warp_int8_rotated_anchored_cuda(qd, kd, q8, k8, qs, ks, anchors, 64, 16,
+                                                           64, 1)
+        else:
+            S.quant_qk_per_warp_int8_rotated_cuda(qd, kd, q8, k8, qs, ks, 64, 16, 64, 1)
+        lpad = (lk + 63) // 64 * 64
+        v8 = torch.empty((1, hk, d, lpad), dtype=torch.int8, device=dev)
+        vs = torch.empty((1, hk, d), dtype=torch.float32, device=dev)
+        S.quantize_v_int8_sm75(vd, v8, vs)
+        o = torch.empty(q.shape, dtype=dt, device=dev)
+        he = torch.empty((0, 0, 0, 0), dtype=torch.float16, device=dev)
+        fe = torch.empty((0, 0, 0), dtype=torch.float32, device=dev)
+        sq = torch.zeros(((lq + 63) // 64,), dtype=torch.uint8, device=dev)
+        ek = torch.zeros(((lk + 63) // 64,), dtype=torch.uint8, device=dev)
+        S.sol_sparse_online_w8a8_prequantized_attn(q8, k8, v8, vs, o, qs, ks, he, he, he, fe, fe,
+                                                   sq, ek, 0.0, 1, d ** -0.5, 0, 1, 64,
+                                                   int(causal), 1)
+        torch.cuda.synchronize()
+        rec.update({"q8": bits(q8), "qs": bits(qs), "k8": bits(k8), "ks": bits(ks),
+                    "v8_permuted": bits(v8), "vs": bits(vs), "out": bits(o),
+                    "meta": np.array([int(dt == torch.float16), int(stab), int(causal)], np.int32)})
+        if stab:
+            rec["anchors"] = bits(anchors)
+        fx[name] = rec
+    return fx
+
+
 def main(out_dir: Path, only: str = "") -> None:
     out_dir.mkdir(parents=True, exist_ok=True)
     if only == "qkrope":
         fx = qkrope_fixtures(torch.device("cuda:0"), R.sage())
+        for name, rec in fx.items():
+            np.savez_compressed(out_dir / f"{name}.npz", **rec)
+        print(f"wrote {len(fx)} fixtures to {out_dir}")
+        return
+    if only == "w8a8":
+        fx = w8a8_fixtures(torch.device("cuda:0"), R.sage())
         for name, rec in fx.items():
             np.savez_compressed(out_dir / f"{name}.npz", **rec)
         print(f"wrote {len(fx)} fixtures to {out_dir}")
