@@ -134,10 +134,82 @@ def sol_sparse_sageattn_from_prequantized(*args, **kwargs):
     return _impl(*args, **kwargs)
 
 
+def _structured_qkv(heads, lengths, head_dim, dtype, divisor, device):
+    """Deterministic self-test inputs (turing_sage/__init__.py:620-627 form)."""
+    q_values = torch.arange(heads[0] * lengths[0] * head_dim, device=device, dtype=torch.float32)
+    kv_values = torch.arange(heads[1] * lengths[1] * head_dim, device=device, dtype=torch.float32)
+    q = (((q_values % 29) - 14) / divisor).reshape(1, heads[0], lengths[0], head_dim).to(dtype)
+    k = ((((kv_values * 3) % 31) - 15) / divisor).reshape(1, heads[1], lengths[1],
+                                                           head_dim).to(dtype)
+    v = ((((kv_values * 5) % 37) - 18) / divisor).reshape_as(k).to(dtype)
+    return q, k, v
+
+
+def _sm100_device(device: torch.device, what: str) -> None:
+    if device.type != "cuda" or not torch.cuda.is_available():
+        raise RuntimeError(f"{what} requires CUDA, got {device}")
+    if torch.cuda.get_device_capability(device) != (10, 0):
+        raise RuntimeError(f"{what} requires sm100 (B200), got {device}")
+
+
+def preflight(device: torch.device) -> None:
+    """Self-test the Sage kernels on `device` before the plugin routes
+    attention to them (turing_sage/__init__.py:612-663, called by the plugin's
+    preflight_bundled, attention/stable.py:521-528): fp16 / bf16 at head dims
+    64, 96 and 128 against fp32 SDPA.  The varlen half of the reference's test
+    is absent with the varlen kernel."""
+    _sm100_device(device, "Turing Sage")
+    if not available():
+        raise RuntimeError("the bundled Turing Sage extensions are not built")
+    with torch.inference_mode(), torch.cuda.device(device):
+        for dtype in (torch.float16, torch.bfloat16):
+            for head_dim in (64, 96, 128):
+                q, k, v = _structured_qkv((4, 2), (65, 73), head_dim, dtype, 32, device)
+                output = sageattn(q, k, v, tensor_layout="HND", smooth_k=False)
+                reference = torch.nn.functional.scaled_dot_product_attention(
+                    q.float(), k.float(), v.float(), enable_gqa=True)
+                if (output.dtype != dtype or output.shape != q.shape
+                        or not torch.isfinite(output).all()
+                        or not torch.allclose(output.float(), reference, rtol=0.08, atol=0.05)):
+                    raise RuntimeError(f"Turing Sage {dtype} D={head_dim} self-test failed")
+        torch.cuda.synchronize(device)
+
+
+def preflight_w8a8(device: torch.device) -> None:
+    """Self-test of the dense W8A8-PV attention (turing_sage/__init__.py:573-610,
+    called by preflight_bundled_w8a8, attention/stable.py:551-558)."""
+    _sm100_device(device, "W8A8 attention")
+    if not w8a8_available():
+        raise RuntimeError("the W8A8 attention extension is not built")
+    with torch.inference_mode(), torch.cuda.device(device):
+        for head_dim in (64, 128):
+            q, k, v = _structured_qkv((4, 2), (129, 151), head_dim, torch.bfloat16, 16, device)
+            output = w8a8attn(q, k, v)
+            reference = torch.nn.functional.scaled_dot_product_attention(
+                q.float(), k.float(), v.float(), enable_gqa=True)
+            if (output.dtype != torch.bfloat16 or output.shape != q.shape
+                    or not torch.isfinite(output).all()
+                    or not torch.allclose(output.float(), reference, rtol=0.12, atol=0.09)):
+                raise RuntimeError(f"Turing W8A8 attention BF16 D={head_dim} self-test failed")
+        torch.cuda.synchronize(device)
+
+
+def preflight_sparse(device: torch.device) -> None:
+    """The Sol sparse kernels are not part of this package
+    (turing_sage/__init__.py:432-468 raises the same way when unbuilt)."""
+    raise RuntimeError("the Sol sparse attention extension is not built")
+
+
+def preflight_sla(device: torch.device) -> None:
+    """The SLA sparse kernels are not part of this package (:471-510)."""
+    raise RuntimeError("the SLA sparse attention extension is not built")
+
+
 from . import custom_ops  # noqa: E402,F401  (registers the turing_utils:: sage custom ops)
 
 __all__ = ["available", "fused_qk_preprocessing_available", "overlap_accumulate_available",
-           "overlap_blend_available", "per_warp_int8", "per_warp_int8_hadamard",
+           "overlap_blend_available", "per_warp_int8", "per_warp_int8_hadamard", "preflight",
+           "preflight_sla", "preflight_sparse", "preflight_w8a8",
            "prequantize_rms_rope_qk", "prequantize_sageattn", "prequantize_sageattn_from_qk",
            "prequantize_sol_sageattn", "prequantize_sol_sageattn_from_qk",
            "quantize_key_per_block", "rms_rope_per_warp_int8", "quantize_query_per_warp",

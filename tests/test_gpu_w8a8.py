@@ -282,3 +282,14 @@ def test_against_reference_kernels(path):
 
 def test_no_watchdog_errors():
     assert _lib.device_error() == 0
+
+
+def test_preflight_self_tests():
+    """The plugin's preflight_bundled / preflight_bundled_w8a8 entry points
+    (attention/stable.py:521-558) pass on the B200."""
+    dev = torch.device("cuda:0")
+    turing_sage.preflight(dev)
+    turing_sage.preflight_w8a8(dev)
+    with pytest.raises(RuntimeError, match="not built"):
+        turing_sage.preflight_sparse(dev)
+    assert _lib.device_error() == 0

@@ -5,6 +5,7 @@ from __future__ import annotations
 
 from unittest import mock
 
+import pytest
 import torch
 
 import comfyui_turing_utils_kernel as kernel
@@ -147,3 +148,30 @@ def test_fused_qk_wrapper_passes_the_production_contract():
                                      rotate_qk=False, stabilize_k=False, query_rrms=rq,
                                      key_rrms=rk)
     assert native.call_args.args[19] == 2 and native.call_args.args[9] is rq
+
+
+def test_preflight_contract_without_gpu():
+    """preflight / preflight_w8a8 refuse a non-CUDA device with the reference's
+    message form; the unbuilt sparse backends report themselves
+    (turing_sage/__init__.py:432-663)."""
+    from comfyui_turing_utils_kernel import turing_sage
+
+    for fn, what in ((turing_sage.preflight, "Turing Sage"),
+                     (turing_sage.preflight_w8a8, "W8A8 attention")):
+        with pytest.raises(RuntimeError, match=f"{what} requires CUDA"):
+            fn(torch.device("cpu"))
+    for fn in (turing_sage.preflight_sparse, turing_sage.preflight_sla):
+        with pytest.raises(RuntimeError, match="not built"):
+            fn(torch.device("cpu"))
+    assert {"preflight", "preflight_w8a8", "w8a8attn", "w8a8attn_compiled",
+            "prequantize_sol_sageattn"} <= set(turing_sage.__all__)
+
+
+def test_w8a8_attention_op_fake():
+    """turing_utils::w8a8_attention has the reference's schema and fake
+    (custom_ops.py:170-210)."""
+    from comfyui_turing_utils_kernel.turing_sage.custom_ops import w8a8_attention
+
+    q = torch.empty((1, 2, 50, 128), dtype=torch.bfloat16, device="meta")
+    out = w8a8_attention(q, q, q, "HND", False, -1.0, 0, True, True)
+    assert out.shape == q.shape and out.dtype == q.dtype and out.device.type == "meta"
