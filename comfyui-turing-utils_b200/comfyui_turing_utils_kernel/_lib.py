@@ -66,8 +66,13 @@ SIGNATURES: dict[str, list] = {
     "tb_qk_int8_sv_f16_accum_f32_attn": [_p, _p, _p, _int, _p, _int, _p, _p, _p, _i64, _i64,
                                          _i64, _i64, _i64, _i64, _p, _int, _int, _int,
                                          ctypes.c_float, _p],
-    "tb_quant_qk_int8_rotated": [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
-                                 _p, _int, _p],
+    "tb_quant_qk_int8_rotated": [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                 _i64, _p, _int, _int, _int, _p],
+    "tb_qk_rms_rope_apply": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                             _i64, _p, _p, _i64, _i64, _i64, _int, _int, _int, ctypes.c_float,
+                             _p],
+    "tb_qk_anchor_processed": [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i64, _i64,
+                               _i64, _int, _int, _int, ctypes.c_float, _p],
     "tb_quantize_v_int8": [_p, _int, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p],
     "tb_w8a8_attn": [_p, _p, _p, _p, _p, _int, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p,
                      _int, ctypes.c_float, _p],

@@ -108,11 +108,12 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
                                 query_warp_block_size, key_block_size, tensor_layout, norm_scope,
                                 split_half, rotate):
     """Fused RMSNorm + RoPE + Q/K INT8 quantization (qk_preprocess.cu:566-753).
-    The Hadamard-rotated form with K anchors (rotate=True) feeds only the W8A8
-    attention, which this package does not provide."""
-    _check(not rotate and anchor_indices.numel() == 0,
-           "the Hadamard-rotated Q/K preprocessing (rotate=True, K anchors) is not built in "
-           "this package")
+    rotate=True is the W8A8 form: the normalized + rotated values are written
+    once in the input dtype (tb_qk_rms_rope_apply), K's anchor is chosen from
+    nine processed samples when anchor_indices is non-empty
+    (tb_qk_anchor_processed; as in the reference, anchors are ignored without
+    rotate), and the randomized-Hadamard quantizer codes them
+    (tb_quant_qk_int8_rotated, NaN -> -127 as in this prologue)."""
     for t, name in ((query, "query"), (key, "key"), (query_output, "query_output"),
                     (key_output, "key_output"), (query_scale, "query_scale"),
                     (key_scale, "key_scale"), (query_norm, "query_norm"), (key_norm, "key_norm")):
@@ -172,6 +173,11 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
         key_norm = key_norm.clone()
     qo = _geometry(query_output, int(tensor_layout))
     ko = _geometry(key_output, int(tensor_layout))
+    if rotate:
+        _rms_rope_rotated(query, key, query_output, key_output, query_scale, key_scale, query_norm,
+                          key_norm, freqs, query_rrms, key_rrms, anchor_indices, anchor_values,
+                          epsilon, rot_dim, tensor_layout, norm_scope, split_half, fstr, fb, fs)
+        return
     strides = torch.tensor([qsb, qsh, qsl, ksb, ksh, ksl, qo[4], qo[5], qo[6], ko[4], ko[5], ko[6],
                             query_scale.stride(0), query_scale.stride(1), key_scale.stride(0),
                             key_scale.stride(1)], dtype=torch.int64)
@@ -184,6 +190,51 @@ def quant_qk_rms_rope_int8_cuda(query, key, query_output, key_output, query_scal
              strides.data_ptr(), None if fstr is None else fstr.data_ptr(), fb, fs, int(rot_dim),
              int(norm_scope), int(bool(split_half)), dtype_code(query), float(epsilon),
              stream_of(query))
+
+
+def _rms_rope_rotated(query, key, query_output, key_output, query_scale, key_scale, query_norm,
+                      key_norm, freqs, query_rrms, key_rrms, anchor_indices, anchor_values,
+                      epsilon, rot_dim, tensor_layout, norm_scope, split_half, fstr, fb, fs):
+    layout = int(tensor_layout)
+    B, qh, ql, D, qsb, qsh, qsl = _geometry(query, layout)
+    _, kh, kl, _, ksb, ksh, ksl = _geometry(key, layout)
+    stabilize = anchor_indices.numel() != 0
+    if stabilize:
+        _check(anchor_indices.is_cuda and anchor_values.is_cuda
+               and anchor_indices.dtype == torch.int32 and anchor_values.dtype == torch.float32,
+               "K anchor scratch must be int32 / float32 CUDA tensors")
+        _check(tuple(anchor_indices.shape) == (B, kh), "anchor index shape is incompatible")
+        _check(tuple(anchor_values.shape) == (B, kh, D) and anchor_values.is_contiguous()
+               and anchor_indices.is_contiguous(), "anchor value shape is incompatible")
+    # The normalized + rotated Q/K, once, in the input dtype and output layout.
+    q_proc = torch.empty(query_output.shape, dtype=query.dtype, device=query.device)
+    k_proc = torch.empty(key_output.shape, dtype=key.dtype, device=key.device)
+    qp, kp = _geometry(q_proc, layout), _geometry(k_proc, layout)
+    qo, ko = _geometry(query_output, layout), _geometry(key_output, layout)
+    apply_strides = torch.tensor([qsb, qsh, qsl, ksb, ksh, ksl, qp[4], qp[5], qp[6], kp[4], kp[5],
+                                  kp[6]], dtype=torch.int64)
+    quant_strides = (ctypes.c_int64 * 12)(qp[4], qp[5], qp[6], kp[4], kp[5], kp[6], qo[4], qo[5],
+                                          qo[6], ko[4], ko[5], ko[6])
+    fptr = ptr(freqs) if rot_dim > 0 else None
+    fsp = None if fstr is None else fstr.data_ptr()
+    with torch.cuda.device(query.device):
+        stream = stream_of(query)
+        call("tb_qk_rms_rope_apply", ptr(query), ptr(key), ptr(q_proc), ptr(k_proc),
+             ptr(query_norm), ptr(key_norm), fptr, ptr(query_rrms) if norm_scope else None,
+             ptr(key_rrms) if norm_scope else None, B, qh, kh, ql, kl, D,
+             apply_strides.data_ptr(), fsp, fb, fs, int(rot_dim), int(norm_scope),
+             int(bool(split_half)), dtype_code(query), float(epsilon), stream)
+        if stabilize:
+            kst = (ctypes.c_int64 * 3)(ksb, ksh, ksl)
+            call("tb_qk_anchor_processed", ptr(key), ptr(key_norm), fptr,
+                 ptr(key_rrms) if norm_scope else None, ptr(anchor_indices), ptr(anchor_values),
+                 B, kh, kl, D, kst, fsp, fb, fs, int(rot_dim), int(norm_scope),
+                 int(bool(split_half)), dtype_code(query), float(epsilon), stream)
+        call("tb_quant_qk_int8_rotated", ptr(q_proc), ptr(k_proc), ptr(query_output),
+             ptr(key_output), ptr(query_scale), ptr(key_scale),
+             ptr(anchor_indices) if stabilize else None, ptr(anchor_values) if stabilize else None,
+             B, qh, kh, ql, kl, D, quant_strides, 2 if stabilize else 0, -127, dtype_code(query),
+             stream)
 
 
 def row_sum_squares_cuda(input, sums, tensor_layout):
@@ -237,10 +288,14 @@ def _rotated(query, key, query_output, key_output, query_scale, key_scale, ancho
     _, _, _, _, qob, qoh, qol = _geometry(query_output, layout)
     _, _, _, _, kob, koh, kol = _geometry(key_output, layout)
     strides = (ctypes.c_int64 * 12)(qb, qh, ql, kb, kh, kl, qob, qoh, qol, kob, koh, kol)
+    values = None
+    if anchor_indices is not None:
+        values = torch.empty((B, Hk, D), dtype=torch.float32, device=key.device)
     with torch.cuda.device(query.device):
         call("tb_quant_qk_int8_rotated", ptr(query), ptr(key), ptr(query_output), ptr(key_output),
-             ptr(query_scale), ptr(key_scale), ptr(anchor_indices), B, Hq, Hk, Lq, Lk, D,
-             strides, dtype_code(query), stream_of(query))
+             ptr(query_scale), ptr(key_scale), ptr(anchor_indices), ptr(values), B, Hq, Hk, Lq,
+             Lk, D, strides, 1 if anchor_indices is not None else 0, 0, dtype_code(query),
+             stream_of(query))
 
 
 def quant_qk_per_warp_int8_rotated_cuda(query, key, query_output, key_output, query_scale,

@@ -176,10 +176,10 @@ def prequantize_rms_rope_qk(q, k, q_norm, k_norm, freqs, *, epsilon: float, rot_
                             tensor_layout: str = "HND", norm_scope: str = "head",
                             split_half: bool = False, rotate_qk: bool = False,
                             stabilize_k: bool = False) -> PrequantizedQK:
-    """Normalize, rotate (RoPE) and quantize Q/K in one pass without
-    materializing the 16-bit intermediates (core.py:222-285).  The
-    Hadamard-rotated variant (rotate_qk) feeds only the W8A8 attention, which
-    is not part of this package, and is rejected."""
+    """Normalize, rotate (RoPE) and quantize Q/K (core.py:222-285).  Without
+    rotate_qk the 16-bit intermediates are never materialized; the
+    Hadamard-rotated form (rotate_qk, optionally stabilize_k) that feeds the
+    W8A8 attention writes them once and codes them in a second pass."""
     if not q.is_cuda or not k.is_cuda:
         raise ValueError("Q/K inputs must be on CUDA")
     if q.device != k.device:
@@ -193,9 +193,6 @@ def prequantize_rms_rope_qk(q, k, q_norm, k_norm, freqs, *, epsilon: float, rot_
     head_dim = int(q.shape[-1])
     if head_dim not in (64, 128):
         raise ValueError("fused Q/K preprocessing requires head_dim 64 or 128")
-    if rotate_qk:
-        raise ValueError("the Hadamard-rotated Q/K preprocessing (rotate_qk) is not built in "
-                         "this package")
     q_norm = q_norm.to(device=q.device, dtype=q.dtype).contiguous()
     k_norm = k_norm.to(device=q.device, dtype=q.dtype).contiguous()
     if freqs is None:
@@ -207,9 +204,9 @@ def prequantize_rms_rope_qk(q, k, q_norm, k_norm, freqs, *, epsilon: float, rot_
     q_int8, q_scale, k_int8, k_scale = qk_rms_rope_int8(
         q, k, q_norm, k_norm, freqs, epsilon=float(epsilon), rot_dim=int(rot_dim),
         tensor_layout=tensor_layout, norm_scope=norm_scope, split_half=bool(split_half),
-        rotate_qk=False, stabilize_k=bool(stabilize_k))
+        rotate_qk=bool(rotate_qk), stabilize_k=bool(stabilize_k))
     return PrequantizedQK(q_int8, q_scale, k_int8, k_scale, tensor_layout, q.dtype, head_dim,
-                          False)
+                          bool(rotate_qk))
 
 
 def prequantize_sageattn_from_qk(qk: PrequantizedQK, value: torch.Tensor, *,

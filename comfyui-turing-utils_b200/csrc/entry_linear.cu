@@ -271,16 +271,35 @@ extern "C" int tb_qk_int8_sv_f16_accum_f32_attn(
 
 extern "C" int tb_quant_qk_int8_rotated(const void* query, const void* key, int8_t* query_out,
                                         int8_t* key_out, float* query_scale, float* key_scale,
-                                        int32_t* anchors, int64_t batch, int64_t query_heads,
-                                        int64_t key_heads, int64_t query_length,
-                                        int64_t key_length, int64_t head_dim,
-                                        const int64_t* strides, int dtype, tb_stream_t stream) {
+                                        int32_t* anchors, float* anchor_values, int64_t batch,
+                                        int64_t query_heads, int64_t key_heads,
+                                        int64_t query_length, int64_t key_length,
+                                        int64_t head_dim, const int64_t* strides, int anchor_mode,
+                                        int nan_code, int dtype, tb_stream_t stream) {
   return guarded([&] {
     TB_REQUIRE(query && key && strides, "query and key must be CUDA tensors");
     tb::require_sm100();
-    tb::rot_quant_launch(query, key, query_out, key_out, query_scale, key_scale, anchors, batch,
-                         query_heads, key_heads, query_length, key_length, head_dim, strides,
-                         dtype, static_cast<cudaStream_t>(stream));
+    tb::rot_quant_launch(query, key, query_out, key_out, query_scale, key_scale, anchors,
+                         anchor_values, batch, query_heads, key_heads, query_length, key_length,
+                         head_dim, strides, anchor_mode, nan_code, dtype,
+                         static_cast<cudaStream_t>(stream));
+  });
+}
+
+extern "C" int tb_qk_anchor_processed(const void* key, const void* key_norm, const void* freqs,
+                                      const float* key_rrms, int32_t* anchors,
+                                      float* anchor_values, int64_t batch, int64_t key_heads,
+                                      int64_t key_length, int64_t head_dim,
+                                      const int64_t* key_strides, const int64_t* freq_strides,
+                                      int64_t freq_batches, int64_t freq_sequence,
+                                      int64_t rot_dim, int norm_scope, int split_half, int dtype,
+                                      float epsilon, tb_stream_t stream) {
+  return guarded([&] {
+    tb::require_sm100();
+    tb::qk_anchor_launch(key, key_norm, freqs, key_rrms, anchors, anchor_values, batch, key_heads,
+                         key_length, head_dim, key_strides, freq_strides, freq_batches,
+                         freq_sequence, rot_dim, norm_scope, split_half, dtype, epsilon,
+                         static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -3,8 +3,10 @@
 // the per-tile INT8 quantization of the Sage contract (Q per 16-token warp
 // tile, K per 64-token block).  Reference: kernel/csrc/turing/sage/
 // qk_preprocess.cu:151-201 (per-element processing), :203-251 (row RMS),
-// :417-563 (tile quantizer), :566-753 (launcher), without the Hadamard /
-// anchor variant that only feeds the W8A8 attention.
+// :417-563 (tile quantizer), :566-753 (launcher).  For the Hadamard /
+// anchor variant that feeds the W8A8 attention the kernel writes the
+// normalized + rotated values instead of codes (tb_qk_rms_rope_apply); the
+// anchor and the rotated quantization run in w8a8_quant.cu.
 //
 // Per element of token t, channel c of a head (T = the input dtype):
 //   n(c)  = T(x[c] * rrms * w[c])            rrms = rsqrt(sum_c x^2 / D + eps)
@@ -140,6 +142,8 @@ struct QkRopeArgs {
   int row_scope;
   int rrms_given;           // row scope with the RRMS supplied by the caller
   int sum_only;             // row pass: write the sum of squares, not the RRMS
+  void* proc[2];            // processed mode: T outputs (strides o_*), no codes
+  int processed;
 };
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
@@ -170,7 +174,8 @@ struct QkGeom {
 // [h0, h1): the tokens' rotations and row RRMS are loaded once, and each
 // thread streams its own 16-byte packs of the next heads into a private
 // cp.async ring while it works on the current head.
-template <typename T, int D, bool SPLIT>
+// PROC: write the normalized + rotated values (a.proc) instead of codes.
+template <typename T, int D, bool SPLIT, bool PROC>
 __device__ __forceinline__ void qk_block(const QkRopeArgs& a, int which, int blk, int h0, int h1,
                                          int batch, uint8_t* ring) {
   using G = QkGeom<D>;
@@ -336,51 +341,64 @@ __device__ __forceinline__ void qk_block(const QkRopeArgs& a, int which, int blk
       }
     }
 
-    // Max |v| per iteration and warp, then per Q warp tile (16 tokens) or the K block.
+    if constexpr (PROC) {
+      // The normalized + rotated values themselves (already rounded to T).
+      T* dst = static_cast<T*>(a.proc[which]) + static_cast<int64_t>(batch) * a.o_b[which] +
+               static_cast<int64_t>(head) * a.o_h[which] + p * 8;
 #pragma unroll
-    for (int it = 0; it < kIters; ++it) {
-      const uint32_t m2 = absmax2<T>(absmax2<T>(v[it][0], v[it][1]), absmax2<T>(v[it][2], v[it][3]));
-      float m = fmaxf(1e-7f, fmaxf(lo<T>(m2), hi<T>(m2)));
+      for (int it = 0; it < kIters; ++it) {
+        const int tok = tok0 + it * kTokPerIter + tin;
+        if (tok < L)
+          *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(tok) * a.o_l[which]) =
+              make_uint4(v[it][0], v[it][1], v[it][2], v[it][3]);
+      }
+    } else {
+      // Max |v| per iteration and warp, then per Q warp tile (16 tokens) or the K block.
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if ((tid & 31) == 0) red[rb][warp][it] = m;
-    }
-    __syncthreads();
-    const int n_tiles = which == 0 ? 4 : 1;
-    if (tid < n_tiles) {
-      // Warp w of iteration it covers tokens it*kTokPerIter + w*(32/P) .. + 32/P - 1.
-      float m = 1e-7f;
+      for (int it = 0; it < kIters; ++it) {
+        const uint32_t m2 = absmax2<T>(absmax2<T>(v[it][0], v[it][1]), absmax2<T>(v[it][2], v[it][3]));
+        float m = fmaxf(1e-7f, fmaxf(lo<T>(m2), hi<T>(m2)));
 #pragma unroll
-      for (int it = 0; it < kIters; ++it)
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if ((tid & 31) == 0) red[rb][warp][it] = m;
+      }
+      __syncthreads();
+      const int n_tiles = which == 0 ? 4 : 1;
+      if (tid < n_tiles) {
+        // Warp w of iteration it covers tokens it*kTokPerIter + w*(32/P) .. + 32/P - 1.
+        float m = 1e-7f;
 #pragma unroll
-        for (int wp = 0; wp < kWarps; ++wp) {
-          const int t16 = (it * kTokPerIter + wp * (32 / P)) / 16;
-          if (which == 1 || t16 == tid) m = fmaxf(m, red[rb][wp][it]);
-        }
-      a.scale[which][static_cast<int64_t>(batch) * a.sc_b[which] +
-                     static_cast<int64_t>(head) * a.sc_h[which] + blk * n_tiles + tid] =
-          __fdiv_rn(m, 127.0f);
-      inv_sm[rb][tid] = __fdiv_rn(127.0f, m);
-    }
-    __syncthreads();
-    float inv[kIters];
+        for (int it = 0; it < kIters; ++it)
 #pragma unroll
-    for (int it = 0; it < kIters; ++it) inv[it] = inv_sm[rb][which == 0 ? (it * kTokPerIter + tin) / 16 : 0];
-    // red / inv_sm alternate between two buffers: the next head writes the
-    // other one, and the head after it passes two barriers first.
+          for (int wp = 0; wp < kWarps; ++wp) {
+            const int t16 = (it * kTokPerIter + wp * (32 / P)) / 16;
+            if (which == 1 || t16 == tid) m = fmaxf(m, red[rb][wp][it]);
+          }
+        a.scale[which][static_cast<int64_t>(batch) * a.sc_b[which] +
+                       static_cast<int64_t>(head) * a.sc_h[which] + blk * n_tiles + tid] =
+            __fdiv_rn(m, 127.0f);
+        inv_sm[rb][tid] = __fdiv_rn(127.0f, m);
+      }
+      __syncthreads();
+      float inv[kIters];
+#pragma unroll
+      for (int it = 0; it < kIters; ++it) inv[it] = inv_sm[rb][which == 0 ? (it * kTokPerIter + tin) / 16 : 0];
+      // red / inv_sm alternate between two buffers: the next head writes the
+      // other one, and the head after it passes two barriers first.
 
-    int8_t* out = a.out[which] + static_cast<int64_t>(batch) * a.o_b[which] +
-                  static_cast<int64_t>(head) * a.o_h[which] + p * 8;
+      int8_t* out = a.out[which] + static_cast<int64_t>(batch) * a.o_b[which] +
+                    static_cast<int64_t>(head) * a.o_h[which] + p * 8;
 #pragma unroll
-    for (int it = 0; it < kIters; ++it) {
-      const int tok = tok0 + it * kTokPerIter + tin;
-      if (tok >= L) continue;
-      uint32_t cb[8];
+      for (int it = 0; it < kIters; ++it) {
+        const int tok = tok0 + it * kTokPerIter + tin;
+        if (tok >= L) continue;
+        uint32_t cb[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        cb[c] = code_bits((c & 1) ? hi<T>(v[it][c >> 1]) : lo<T>(v[it][c >> 1]), inv[it]);
-      const uint32_t wq[2] = {pack_codes(cb[0], cb[1], cb[2], cb[3]), pack_codes(cb[4], cb[5], cb[6], cb[7])};
-      *reinterpret_cast<uint2*>(out + static_cast<int64_t>(tok) * a.o_l[which]) = make_uint2(wq[0], wq[1]);
+        for (int c = 0; c < 8; ++c)
+          cb[c] = code_bits((c & 1) ? hi<T>(v[it][c >> 1]) : lo<T>(v[it][c >> 1]), inv[it]);
+        const uint32_t wq[2] = {pack_codes(cb[0], cb[1], cb[2], cb[3]), pack_codes(cb[4], cb[5], cb[6], cb[7])};
+        *reinterpret_cast<uint2*>(out + static_cast<int64_t>(tok) * a.o_l[which]) = make_uint2(wq[0], wq[1]);
+      }
     }
   }
   cp_async_wait<0>();
@@ -388,7 +406,7 @@ __device__ __forceinline__ void qk_block(const QkRopeArgs& a, int which, int blk
 
 // grid (Q tasks + K tasks, batch); a task is one 64-token block and one group
 // of head_group consecutive heads.
-template <typename T, int D, bool SPLIT>
+template <typename T, int D, bool SPLIT, bool PROC>
 __global__ void __launch_bounds__(kQkThreads, 3) qk_rms_rope_kernel(const QkRopeArgs a, int head_group) {
   extern __shared__ __align__(16) uint8_t ring[];
   const int task = blockIdx.x;
@@ -402,7 +420,7 @@ __global__ void __launch_bounds__(kQkThreads, 3) qk_rms_rope_kernel(const QkRope
   const int blk = local / groups, grp = local - blk * groups;
   const int h0 = grp * head_group;
   const int h1 = min(a.heads[which], h0 + head_group);
-  qk_block<T, D, SPLIT>(a, which, blk, h0, h1, batch, ring);
+  qk_block<T, D, SPLIT, PROC>(a, which, blk, h0, h1, batch, ring);
 }
 
 // Row scope: RRMS of every token over all heads (qk_preprocess.cu:203-251).
@@ -510,16 +528,21 @@ void qk_rms_rope_launch(QkRopeArgs& a, int batch, int head_dim, int split_half, 
   const int tasks = ((a.heads[0] + head_group - 1) / head_group) * a.blocks[0] +
                     ((a.heads[1] + head_group - 1) / head_group) * a.blocks[1];
   const dim3 grid(static_cast<unsigned>(tasks), static_cast<unsigned>(batch));
-#define TB_QK_LAUNCH(T, D, S)                                                                     \
+#define TB_QK_LAUNCH1(T, D, S, PR)                                                                \
   do {                                                                                            \
     static bool attr_set = false;                                                                 \
     if (!attr_set) {                                                                              \
-      TB_CUDA_CHECK(cudaFuncSetAttribute(qk_rms_rope_kernel<T, D, S>,                             \
+      TB_CUDA_CHECK(cudaFuncSetAttribute(qk_rms_rope_kernel<T, D, S, PR>,                         \
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,             \
                                          QkGeom<D>::kSmemBytes));                                 \
       attr_set = true;                                                                            \
     }                                                                                             \
-    qk_rms_rope_kernel<T, D, S><<<grid, kQkThreads, QkGeom<D>::kSmemBytes, stream>>>(a, head_group); \
+    qk_rms_rope_kernel<T, D, S, PR><<<grid, kQkThreads, QkGeom<D>::kSmemBytes, stream>>>(a, head_group); \
+  } while (0)
+#define TB_QK_LAUNCH(T, D, S)                          \
+  do {                                                 \
+    if (a.processed) TB_QK_LAUNCH1(T, D, S, true);     \
+    else TB_QK_LAUNCH1(T, D, S, false);                \
   } while (0)
   if (dtype == TB_DTYPE_BF16) {
     using T = __nv_bfloat16;
@@ -531,12 +554,112 @@ void qk_rms_rope_launch(QkRopeArgs& a, int batch, int head_dim, int split_half, 
     else { if (split_half) TB_QK_LAUNCH(T, 64, true); else TB_QK_LAUNCH(T, 64, false); }
   }
 #undef TB_QK_LAUNCH
+#undef TB_QK_LAUNCH1
   TB_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace tb
 
 using tb::guarded;
+
+namespace {
+
+// Checks and kernel arguments shared by the quantizing and the processed-value
+// entries (outputs: INT8 codes + scales, or 16-bit values).
+tb::QkRopeArgs prologue_args(const void* query, const void* key, void* query_out, void* key_out,
+                             float* query_scale, float* key_scale, const void* query_norm,
+                             const void* key_norm, const void* freqs, float* query_rrms,
+                             float* key_rrms, int64_t batch, int64_t query_heads,
+                             int64_t key_heads, int64_t query_length, int64_t key_length,
+                             int64_t head_dim, const int64_t* strides, const int64_t* freq_strides,
+                             int64_t freq_batches, int64_t freq_sequence, int64_t rot_dim,
+                             int norm_scope, int split_half, int dtype, float epsilon,
+                             bool processed) {
+  TB_REQUIRE(query && key && query_out && key_out && query_norm && key_norm && strides,
+             "Q/K, outputs and norm weights must be CUDA tensors");
+  TB_REQUIRE(processed || (query_scale && key_scale), "scales must be CUDA tensors");
+  TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16, "Q/K must be float16 or bfloat16");
+  TB_REQUIRE(head_dim == 64 || head_dim == 128,
+             "fused Q/K preprocessing requires head_dim 64 or 128");
+  TB_REQUIRE(norm_scope >= 0 && norm_scope <= 2,
+             "norm_scope must be 0 (per head), 1 (whole row) or 2 (whole row, RRMS given)");
+  TB_REQUIRE(rot_dim >= 0 && rot_dim <= head_dim && rot_dim % 2 == 0,
+             "rot_dim must be even and within head_dim");
+  TB_REQUIRE(rot_dim == 0 || (freqs && freq_strides),
+             "RoPE frequencies are required when rot_dim > 0");
+  TB_REQUIRE(norm_scope == 0 || (query_rrms && key_rrms), "row RRMS scratch must be provided");
+  TB_REQUIRE(batch > 0 && query_heads > 0 && key_heads > 0 && query_length > 0 && key_length > 0,
+             "Q/K dimensions must be positive");
+  TB_REQUIRE(batch <= 65535 && query_heads <= INT32_MAX && query_length <= INT32_MAX &&
+                 key_length <= INT32_MAX,
+             "Q/K dimensions exceed the CUDA kernel range");
+  for (int i = 0; i < 12; ++i)
+    TB_REQUIRE(strides[i] % 8 == 0,
+               "Q/K and output strides must be multiples of 8 elements (16-byte packs)");
+  TB_REQUIRE((reinterpret_cast<uintptr_t>(query) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(key) & 15u) == 0,
+             "Q/K must be 16-byte aligned");
+  const uintptr_t out_align = processed ? 15u : 7u;
+  TB_REQUIRE((reinterpret_cast<uintptr_t>(query_out) & out_align) == 0 &&
+                 (reinterpret_cast<uintptr_t>(key_out) & out_align) == 0,
+             processed ? "the processed Q/K outputs must be 16-byte aligned"
+                       : "the INT8 Q/K outputs must be 8-byte aligned");
+  TB_REQUIRE((reinterpret_cast<uintptr_t>(query_norm) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(key_norm) & 15u) == 0,
+             "Q/K norm weights must be 16-byte aligned");
+  tb::QkRopeArgs a{};
+  a.in[0] = query; a.in[1] = key;
+  a.processed = processed ? 1 : 0;
+  if (processed) {
+    a.proc[0] = query_out; a.proc[1] = key_out;
+  } else {
+    a.out[0] = static_cast<int8_t*>(query_out); a.out[1] = static_cast<int8_t*>(key_out);
+    a.scale[0] = query_scale; a.scale[1] = key_scale;
+  }
+  a.norm[0] = query_norm; a.norm[1] = key_norm;
+  a.freqs = freqs;
+  a.heads[0] = static_cast<int>(query_heads); a.heads[1] = static_cast<int>(key_heads);
+  a.length[0] = static_cast<int>(query_length); a.length[1] = static_cast<int>(key_length);
+  a.blocks[0] = static_cast<int>((query_length + 63) / 64);
+  a.blocks[1] = static_cast<int>((key_length + 63) / 64);
+  // strides: q (b, h, l), k (b, h, l), q_out (b, h, l), k_out (b, h, l) and,
+  // quantizing, q_scale (b, h), k_scale (b, h).
+  for (int w = 0; w < 2; ++w) {
+    a.s_b[w] = strides[3 * w + 0]; a.s_h[w] = strides[3 * w + 1]; a.s_l[w] = strides[3 * w + 2];
+    a.o_b[w] = strides[6 + 3 * w + 0]; a.o_h[w] = strides[6 + 3 * w + 1]; a.o_l[w] = strides[6 + 3 * w + 2];
+    if (!processed) {
+      a.sc_b[w] = strides[12 + 2 * w + 0]; a.sc_h[w] = strides[12 + 2 * w + 1];
+    }
+  }
+  if (rot_dim > 0) {
+    a.f_b = freq_strides[0]; a.f_s = freq_strides[1]; a.f_p = freq_strides[2];
+    a.f_r = freq_strides[3]; a.f_c = freq_strides[4];
+    a.f_batches = static_cast<int>(freq_batches);
+    a.f_seq = static_cast<int>(freq_sequence);
+    a.fast_freqs = !split_half && a.f_p == 4 && a.f_r == 2 && a.f_c == 1 && a.f_s % 8 == 0 &&
+                   a.f_b % 8 == 0 && (reinterpret_cast<uintptr_t>(freqs) & 15u) == 0;
+  } else {
+    a.f_batches = a.f_seq = 1;
+  }
+  a.rot_dim = static_cast<int>(rot_dim);
+  a.eps = epsilon;
+  a.row_scope = norm_scope ? 1 : 0;
+  a.rrms_given = norm_scope == 2;
+  // Loads that the kernel skips at run time (no RoPE, head-scope norm) must
+  // still name readable memory: the compiler may issue a guarded load ahead
+  // of its guard (for example when hoisting it out of the per-head loop), so
+  // the unused pointers name the inputs themselves, with zero strides for
+  // the rotations.
+  a.rrms[0] = norm_scope ? query_rrms : static_cast<float*>(const_cast<void*>(query));
+  a.rrms[1] = norm_scope ? key_rrms : static_cast<float*>(const_cast<void*>(key));
+  if (rot_dim == 0) {
+    a.freqs = query;
+    a.f_b = a.f_s = a.f_p = a.f_r = a.f_c = 0;
+  }
+  return a;
+}
+
+}  // namespace
 
 extern "C" int tb_quant_qk_rms_rope_int8(
     const void* query, const void* key, int8_t* query_out, int8_t* key_out, float* query_scale,
@@ -546,78 +669,31 @@ extern "C" int tb_quant_qk_rms_rope_int8(
     const int64_t* freq_strides, int64_t freq_batches, int64_t freq_sequence, int64_t rot_dim,
     int norm_scope, int split_half, int dtype, float epsilon, tb_stream_t stream) {
   return guarded([&] {
-    TB_REQUIRE(query && key && query_out && key_out && query_scale && key_scale && query_norm &&
-                   key_norm && strides,
-               "Q/K, outputs, scales and norm weights must be CUDA tensors");
-    TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16, "Q/K must be float16 or bfloat16");
-    TB_REQUIRE(head_dim == 64 || head_dim == 128,
-               "fused Q/K preprocessing requires head_dim 64 or 128");
-    TB_REQUIRE(norm_scope >= 0 && norm_scope <= 2,
-               "norm_scope must be 0 (per head), 1 (whole row) or 2 (whole row, RRMS given)");
-    TB_REQUIRE(rot_dim >= 0 && rot_dim <= head_dim && rot_dim % 2 == 0,
-               "rot_dim must be even and within head_dim");
-    TB_REQUIRE(rot_dim == 0 || (freqs && freq_strides),
-               "RoPE frequencies are required when rot_dim > 0");
-    TB_REQUIRE(norm_scope == 0 || (query_rrms && key_rrms), "row RRMS scratch must be provided");
-    TB_REQUIRE(batch > 0 && query_heads > 0 && key_heads > 0 && query_length > 0 && key_length > 0,
-               "Q/K dimensions must be positive");
-    TB_REQUIRE(batch <= 65535 && query_heads <= INT32_MAX && query_length <= INT32_MAX &&
-                   key_length <= INT32_MAX,
-               "Q/K dimensions exceed the CUDA kernel range");
-    for (int i = 0; i < 12; ++i)
-      TB_REQUIRE(strides[i] % 8 == 0,
-                 "Q/K and output strides must be multiples of 8 elements (16-byte packs)");
-    TB_REQUIRE((reinterpret_cast<uintptr_t>(query) & 15u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(key) & 15u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(query_out) & 7u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(key_out) & 7u) == 0,
-               "Q/K must be 16-byte aligned and their INT8 outputs 8-byte aligned");
-    TB_REQUIRE((reinterpret_cast<uintptr_t>(query_norm) & 15u) == 0 &&
-                   (reinterpret_cast<uintptr_t>(key_norm) & 15u) == 0,
-               "Q/K norm weights must be 16-byte aligned");
+    tb::QkRopeArgs a = prologue_args(query, key, query_out, key_out, query_scale, key_scale,
+                                     query_norm, key_norm, freqs, query_rrms, key_rrms, batch,
+                                     query_heads, key_heads, query_length, key_length, head_dim,
+                                     strides, freq_strides, freq_batches, freq_sequence, rot_dim,
+                                     norm_scope, split_half, dtype, epsilon, false);
     tb::require_sm100();
-    tb::QkRopeArgs a{};
-    a.in[0] = query; a.in[1] = key;
-    a.out[0] = query_out; a.out[1] = key_out;
-    a.scale[0] = query_scale; a.scale[1] = key_scale;
-    a.norm[0] = query_norm; a.norm[1] = key_norm;
-    a.freqs = freqs;
-    a.heads[0] = static_cast<int>(query_heads); a.heads[1] = static_cast<int>(key_heads);
-    a.length[0] = static_cast<int>(query_length); a.length[1] = static_cast<int>(key_length);
-    a.blocks[0] = static_cast<int>((query_length + 63) / 64);
-    a.blocks[1] = static_cast<int>((key_length + 63) / 64);
-    // strides: q (b, h, l), k (b, h, l), q_out (b, h, l), k_out (b, h, l),
-    // q_scale (b, h), k_scale (b, h) -> 16 values.
-    for (int w = 0; w < 2; ++w) {
-      a.s_b[w] = strides[3 * w + 0]; a.s_h[w] = strides[3 * w + 1]; a.s_l[w] = strides[3 * w + 2];
-      a.o_b[w] = strides[6 + 3 * w + 0]; a.o_h[w] = strides[6 + 3 * w + 1]; a.o_l[w] = strides[6 + 3 * w + 2];
-      a.sc_b[w] = strides[12 + 2 * w + 0]; a.sc_h[w] = strides[12 + 2 * w + 1];
-    }
-    if (rot_dim > 0) {
-      a.f_b = freq_strides[0]; a.f_s = freq_strides[1]; a.f_p = freq_strides[2];
-      a.f_r = freq_strides[3]; a.f_c = freq_strides[4];
-      a.f_batches = static_cast<int>(freq_batches);
-      a.f_seq = static_cast<int>(freq_sequence);
-      a.fast_freqs = !split_half && a.f_p == 4 && a.f_r == 2 && a.f_c == 1 && a.f_s % 8 == 0 &&
-                     a.f_b % 8 == 0 && (reinterpret_cast<uintptr_t>(freqs) & 15u) == 0;
-    } else {
-      a.f_batches = a.f_seq = 1;
-    }
-    a.rot_dim = static_cast<int>(rot_dim);
-    a.eps = epsilon;
-    a.row_scope = norm_scope ? 1 : 0;
-    a.rrms_given = norm_scope == 2;
-    // Loads that the kernel skips at run time (no RoPE, head-scope norm) must
-    // still name readable memory: the compiler may issue a guarded load ahead
-    // of its guard (for example when hoisting it out of the per-head loop), so
-    // the unused pointers name the inputs themselves, with zero strides for
-    // the rotations.
-    a.rrms[0] = norm_scope ? query_rrms : static_cast<float*>(const_cast<void*>(query));
-    a.rrms[1] = norm_scope ? key_rrms : static_cast<float*>(const_cast<void*>(key));
-    if (rot_dim == 0) {
-      a.freqs = query;
-      a.f_b = a.f_s = a.f_p = a.f_r = a.f_c = 0;
-    }
+    tb::qk_rms_rope_launch(a, static_cast<int>(batch), static_cast<int>(head_dim), split_half,
+                           dtype, static_cast<cudaStream_t>(stream));
+  });
+}
+
+extern "C" int tb_qk_rms_rope_apply(
+    const void* query, const void* key, void* query_out, void* key_out, const void* query_norm,
+    const void* key_norm, const void* freqs, float* query_rrms, float* key_rrms, int64_t batch,
+    int64_t query_heads, int64_t key_heads, int64_t query_length, int64_t key_length,
+    int64_t head_dim, const int64_t* strides, const int64_t* freq_strides, int64_t freq_batches,
+    int64_t freq_sequence, int64_t rot_dim, int norm_scope, int split_half, int dtype,
+    float epsilon, tb_stream_t stream) {
+  return guarded([&] {
+    tb::QkRopeArgs a = prologue_args(query, key, query_out, key_out, nullptr, nullptr, query_norm,
+                                     key_norm, freqs, query_rrms, key_rrms, batch, query_heads,
+                                     key_heads, query_length, key_length, head_dim, strides,
+                                     freq_strides, freq_batches, freq_sequence, rot_dim,
+                                     norm_scope, split_half, dtype, epsilon, true);
+    tb::require_sm100();
     tb::qk_rms_rope_launch(a, static_cast<int>(batch), static_cast<int>(head_dim), split_half,
                            dtype, static_cast<cudaStream_t>(stream));
   });

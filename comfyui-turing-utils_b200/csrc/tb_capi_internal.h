@@ -94,8 +94,15 @@ struct AttnArgs {
 // Kernels implemented in the other translation units.
 void sage_attn_launch(const AttnArgs& a, cudaStream_t stream);
 void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out, float* q_scale,
-                      float* k_scale, int32_t* anchors, int64_t B, int64_t Hq, int64_t Hk,
-                      int64_t Lq, int64_t Lk, int64_t D, const int64_t* strides, int dtype,
+                      float* k_scale, int32_t* anchors, float* anchor_values, int64_t B,
+                      int64_t Hq, int64_t Hk, int64_t Lq, int64_t Lk, int64_t D,
+                      const int64_t* strides, int anchor_mode, int nan_code, int dtype,
+                      cudaStream_t stream);
+void qk_anchor_launch(const void* key, const void* key_norm, const void* freqs,
+                      const float* key_rrms, int32_t* anchors, float* anchor_values, int64_t B,
+                      int64_t Hk, int64_t Lk, int64_t D, const int64_t* k_strides,
+                      const int64_t* freq_strides, int64_t freq_batches, int64_t freq_sequence,
+                      int64_t rot_dim, int norm_scope, int split_half, int dtype, float eps,
                       cudaStream_t stream);
 void v_quant_launch(const void* v, int dtype, uint16_t* codes_f16, int8_t* codes_cm, float* scale,
                     int64_t B, int64_t H, int64_t L, int64_t D, int64_t Lpad, int64_t sb,

@@ -4,12 +4,16 @@
 //   K anchor   per (batch, kv head): nine keys at rows s * (L - 1) / 8; the one
 //              nearest their mean becomes the anchor when subtracting it
 //              lowers the samples' energy and grows their range by at most
-//              12.5 %; otherwise -1 (no subtraction).
+//              12.5 %; otherwise -1 (no subtraction).  The fused prologue's
+//              variant (qk_preprocess.cu:252-415) samples the normalized +
+//              rotated keys instead (qk_anchor_kernel).
 //   rotation   x -> H_D diag(sign) x / sqrt(D) over the D = 64 / 128 channels
 //              of a token (Sylvester Walsh-Hadamard, the sign vector of the
 //              reference), K minus its anchor row first.
 //   codes      per tile (Q: 16 tokens, K: 64 tokens) amax = max(1e-7, |x|),
-//              scale = amax / 127, q = rni_sat(x * (127 / amax)).
+//              scale = amax / 127, q = rni_sat(x * (127 / amax)); a NaN codes
+//              as 0 (fused.cu's cvt.rni.sat.s8) or -127 (the prologue's clamp
+//              of nearbyintf, qk_preprocess.cu:43-47).
 // V (quant_v_int8_cuda_sm75.cu:58-164): per (batch, head, channel) over all
 //   tokens, scale = max(amax / 127, 1e-12), q = rni_sat(v * (1 / scale)).
 //
@@ -54,11 +58,11 @@ __device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
   }
 }
 
-// Low byte = rni_sat_s8(v) for |v| <= 127 * (1 + 2^-23) or NaN (-> 0): adding
-// 1.5 * 2^23 rounds to the nearest integer, ties to even, and leaves it
-// two's-complement in the low byte.
-__device__ __forceinline__ uint32_t code_bits(float v) {
-  return __float_as_uint(__fadd_rn(v == v ? v : 0.0f, 12582912.0f));
+// Low byte = rni_sat_s8(v) for |v| <= 127 * (1 + 2^-23), or nan_code for a
+// NaN: adding 1.5 * 2^23 rounds to the nearest integer, ties to even, and
+// leaves it two's-complement in the low byte.
+__device__ __forceinline__ uint32_t code_bits(float v, float nan_code) {
+  return __float_as_uint(__fadd_rn(v == v ? v : nan_code, 12582912.0f));
 }
 __device__ __forceinline__ uint32_t pack_codes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -73,6 +77,7 @@ __device__ constexpr uint32_t kRotSigns[4] = {0x1035997bu, 0x8087f5eeu, 0xee2e4e
 struct AnchorParams {
   const void* k;
   int32_t* anchors;  // [B, Hk]
+  float* values;     // [B, Hk, D]: the anchor rows, zeros for -1
   int H, L;
   int64_t sb, sh, sl;
 };
@@ -90,24 +95,16 @@ __device__ __forceinline__ float tree_max(float v) {
   return v;
 }
 
-// grid (Hk, B), 128 threads: thread t owns channel t.
-template <typename T, int D>
-__global__ void __launch_bounds__(128) k_anchor_kernel(AnchorParams p) {
-  __shared__ float samp[kAnchorSamples][D];
+// The anchor choice over samp[9][D] (filled by the caller, synced), run by the
+// 128 threads of the CTA (thread t owns channel t); writes the row index (or
+// -1) and the anchor's values (zeros for -1).
+template <int D>
+__device__ __forceinline__ void anchor_select(const float (*samp)[D], int L, int32_t* anchor,
+                                              float* values) {
   __shared__ float w_oe[4], w_om[4], w_be[4], w_bm[4];
   __shared__ float w_cd[kAnchorSamples][4];
   __shared__ int best_sh;
-  const int h = blockIdx.x, b = blockIdx.y;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const T* kh = static_cast<const T*>(p.k) + b * p.sb + h * p.sh;
-  for (int i = t; i < kAnchorSamples * D; i += 128) {
-    const int s = i / D, c = i - s * D;
-    const int64_t row = static_cast<int64_t>(s) * (p.L - 1) / (kAnchorSamples - 1);
-    const T v = kh[row * p.sl + c];
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) samp[s][c] = __bfloat162float(v);
-    else samp[s][c] = __half2float(v);
-  }
-  __syncthreads();
   float oe = 0.0f, om = 0.0f;
   float cd[kAnchorSamples];
 #pragma unroll
@@ -179,10 +176,109 @@ __global__ void __launch_bounds__(128) k_anchor_kernel(AnchorParams p) {
       tbm = fmaxf(tbm, w_bm[w]);
     }
     const bool keep = tbe < toe && tbm <= tom * 1.125f;
-    p.anchors[b * p.H + h] =
-        keep ? static_cast<int32_t>(static_cast<int64_t>(best) * (p.L - 1) / (kAnchorSamples - 1))
-             : -1;
+    *anchor = keep ? static_cast<int32_t>(static_cast<int64_t>(best) * (L - 1) / (kAnchorSamples - 1))
+                   : -1;
+    best_sh = keep ? best : -1;
   }
+  __syncthreads();
+  if (t < D) values[t] = best_sh >= 0 ? samp[best_sh][t] : 0.0f;
+}
+
+// Anchor of the raw keys.  grid (Hk, B), 128 threads.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) k_anchor_kernel(AnchorParams p) {
+  __shared__ float samp[kAnchorSamples][D];
+  const int h = blockIdx.x, b = blockIdx.y;
+  const T* kh = static_cast<const T*>(p.k) + b * p.sb + h * p.sh;
+  for (int i = threadIdx.x; i < kAnchorSamples * D; i += 128) {
+    const int s = i / D, c = i - s * D;
+    const int64_t row = static_cast<int64_t>(s) * (p.L - 1) / (kAnchorSamples - 1);
+    const T v = kh[row * p.sl + c];
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) samp[s][c] = __bfloat162float(v);
+    else samp[s][c] = __half2float(v);
+  }
+  __syncthreads();
+  anchor_select<D>(samp, p.L, p.anchors + b * p.H + h,
+                   p.values + (static_cast<int64_t>(b) * p.H + h) * D);
+}
+
+// Anchor of the fused prologue's normalized + rotated keys
+// (detect_anchor_kernel, qk_preprocess.cu:252-415).  Each sampled token gets
+// its own RRMS (row scope: the row RRMS; head scope: one FMA chain over the
+// channels in order, then the correctly rounded 1/sqrt), then
+// n = T(x * rrms * w) and, on the first rot_dim channels,
+// v = T(fma(f[row][1], n(second), f[row][0] * n(first))).  grid (Hk, B), 128 threads.
+struct ProcAnchorParams {
+  const void* k;
+  const void* norm;      // [D] (head scope) or [Hk * D] (row scope)
+  const void* freqs;     // valid memory even when rot_dim == 0
+  const float* rrms;     // row scope: [B, L]; else unused (valid memory)
+  int32_t* anchors;      // [B, Hk]
+  float* values;         // [B, Hk, D]
+  int H, L, rot_dim, split_half, row_scope, f_batches, f_seq;
+  int64_t sb, sh, sl;
+  int64_t f_b, f_s, f_p, f_r, f_c;
+  float eps;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(v);
+  else return __half2float(v);
+}
+template <typename T>
+__device__ __forceinline__ float round_to(float v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
+  else return __half2float(__float2half_rn(v));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) qk_anchor_kernel(ProcAnchorParams p) {
+  __shared__ float samp[kAnchorSamples][D];
+  __shared__ float rr[kAnchorSamples];
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  const T* kh = static_cast<const T*>(p.k) + b * p.sb + h * p.sh;
+  const T* w = static_cast<const T*>(p.norm) + (p.row_scope ? h * D : 0);
+  if (t < kAnchorSamples) {
+    const int tok = static_cast<int>(static_cast<int64_t>(t) * (p.L - 1) / (kAnchorSamples - 1));
+    if (p.row_scope) {
+      rr[t] = p.rrms[static_cast<int64_t>(b) * p.L + tok];
+    } else {
+      float sum = 0.0f;
+      for (int c = 0; c < D; ++c) {
+        const float v = to_f(kh[static_cast<int64_t>(tok) * p.sl + c]);
+        sum = fmaf(v, v, sum);
+      }
+      rr[t] = __frsqrt_rn(__fdiv_rn(sum, static_cast<float>(D)) + p.eps);
+    }
+  }
+  __syncthreads();
+  if (t < D) {
+    const int half = p.rot_dim / 2;
+    const T* fr = static_cast<const T*>(p.freqs);
+    for (int s = 0; s < kAnchorSamples; ++s) {
+      const int tok = static_cast<int>(static_cast<int64_t>(s) * (p.L - 1) / (kAnchorSamples - 1));
+      const T* row = kh + static_cast<int64_t>(tok) * p.sl;
+      const float rs = rr[s];
+      float v = round_to<T>(to_f(row[t]) * rs * to_f(w[t]));
+      if (t < p.rot_dim) {
+        const int pair = p.split_half ? (t < half ? t : t - half) : t / 2;
+        const int first = p.split_half ? pair : 2 * pair;
+        const int second = p.split_half ? pair + half : first + 1;
+        const int comp = p.split_half ? (t >= half) : (t & 1);
+        const float x0 = round_to<T>(to_f(row[first]) * rs * to_f(w[first]));
+        const float x1 = round_to<T>(to_f(row[second]) * rs * to_f(w[second]));
+        const int64_t fbase = static_cast<int64_t>(p.f_batches == 1 ? 0 : b) * p.f_b +
+                              static_cast<int64_t>(p.f_seq == 1 ? 0 : tok) * p.f_s +
+                              static_cast<int64_t>(pair) * p.f_p + comp * p.f_r;
+        v = round_to<T>(fmaf(to_f(fr[fbase + p.f_c]), x1, to_f(fr[fbase]) * x0));
+      }
+      samp[s][t] = v;
+    }
+  }
+  __syncthreads();
+  anchor_select<D>(samp, p.L, p.anchors + b * p.H + h,
+                   p.values + (static_cast<int64_t>(b) * p.H + h) * D);
 }
 
 // --------------------------------------------------- rotated Q/K codes ----
@@ -191,7 +287,8 @@ struct RotParams {
   const void* in[2];      // Q, K
   int8_t* out[2];
   float* scale[2];        // Q: [B, Hq, blocks*4]; K: [B, Hk, blocks]
-  const int32_t* anchors; // [B, Hk] or null
+  const float* anchor_values;  // [B, Hk, D] subtracted from K (zeros: none) or null
+  float nan_code;              // code of a NaN: 0 or -127
   int heads[2], length[2], blocks[2];
   int64_t s_b[2], s_h[2], s_l[2];   // input strides (elements)
   int64_t o_b[2], o_h[2], o_l[2];   // output strides
@@ -221,12 +318,17 @@ __global__ void __launch_bounds__(128) rot_quant_kernel(const RotParams a) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = lane & 3;
   const T* in = static_cast<const T*>(a.in[which]) + b * a.s_b[which] + h * a.s_h[which];
-  int anchor = -1;
-  if (which == 1 && a.anchors != nullptr) anchor = __ldg(a.anchors + b * a.heads[1] + h);
+  const bool anchored = which == 1 && a.anchor_values != nullptr;
   float anc[NP][8];
-  if (anchor >= 0) {
+  if (anchored) {
+    const float* av = a.anchor_values + (static_cast<int64_t>(b) * a.heads[1] + h) * D;
 #pragma unroll
-    for (int k = 0; k < NP; ++k) load8(in + static_cast<int64_t>(anchor) * a.s_l[which] + 8 * (r + 4 * k), anc[k]);
+    for (int k = 0; k < NP; ++k) {
+      const float4 lo4 = __ldg(reinterpret_cast<const float4*>(av + 8 * (r + 4 * k)));
+      const float4 hi4 = __ldg(reinterpret_cast<const float4*>(av + 8 * (r + 4 * k) + 4));
+      anc[k][0] = lo4.x; anc[k][1] = lo4.y; anc[k][2] = lo4.z; anc[k][3] = lo4.w;
+      anc[k][4] = hi4.x; anc[k][5] = hi4.y; anc[k][6] = hi4.z; anc[k][7] = hi4.w;
+    }
   }
   float v[2][NP][8];
   float amax = 0.0000001f;
@@ -237,7 +339,7 @@ __global__ void __launch_bounds__(128) rot_quant_kernel(const RotParams a) {
 #pragma unroll
       for (int k = 0; k < NP; ++k) {
         load8(in + static_cast<int64_t>(tok) * a.s_l[which] + 8 * (r + 4 * k), v[ps][k]);
-        if (anchor >= 0) {
+        if (anchored) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[ps][k][e] = __fsub_rn(v[ps][k][e], anc[k][e]);
         }
@@ -318,7 +420,7 @@ __global__ void __launch_bounds__(128) rot_quant_kernel(const RotParams a) {
     for (int k = 0; k < NP; ++k) {
       uint32_t cb[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) cb[e] = code_bits(__fmul_rn(v[ps][k][e], inv));
+      for (int e = 0; e < 8; ++e) cb[e] = code_bits(__fmul_rn(v[ps][k][e], inv), a.nan_code);
       *reinterpret_cast<uint2*>(out + static_cast<int64_t>(tok) * a.o_l[which] + 8 * (r + 4 * k)) =
           make_uint2(pack_codes(cb[0], cb[1], cb[2], cb[3]), pack_codes(cb[4], cb[5], cb[6], cb[7]));
     }
@@ -389,7 +491,7 @@ __global__ void __launch_bounds__(256) v_codes_kernel(VParams p) {
       float x[8];
       load8(vh + static_cast<int64_t>(tok) * p.sl + c8, x);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) cb[e] = code_bits(__fmul_rn(x[e], inv_sh[c8 + e])) & 0xffu;
+      for (int e = 0; e < 8; ++e) cb[e] = code_bits(__fmul_rn(x[e], inv_sh[c8 + e]), 0.0f) & 0xffu;
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) cb[e] = 0;
@@ -441,8 +543,9 @@ void check_rows(const void* p, int64_t sb, int64_t sh, int64_t sl, const char* m
 }  // namespace
 
 void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out, float* q_scale,
-                      float* k_scale, int32_t* anchors, int64_t B, int64_t Hq, int64_t Hk,
-                      int64_t Lq, int64_t Lk, int64_t D, const int64_t* s, int dtype,
+                      float* k_scale, int32_t* anchors, float* anchor_values, int64_t B,
+                      int64_t Hq, int64_t Hk, int64_t Lq, int64_t Lk, int64_t D,
+                      const int64_t* s, int anchor_mode, int nan_code, int dtype,
                       cudaStream_t stream) {
   TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16,
              "Turing W8A8 Q/K must be float16 or bfloat16");
@@ -456,6 +559,13 @@ void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out
                  s[8] % 8 == 0 && s[9] % 8 == 0 && s[10] % 8 == 0 && s[11] % 8 == 0,
              "INT8 Q/K outputs must start on 8-byte boundaries with strides of 8 elements");
   TB_REQUIRE(q_scale && k_scale, "scales must be CUDA tensors");
+  TB_REQUIRE(anchor_mode >= 0 && anchor_mode <= 2,
+             "anchor_mode must be 0 (none), 1 (detect from K) or 2 (values given)");
+  TB_REQUIRE(anchor_mode == 0 || ((reinterpret_cast<uintptr_t>(anchor_values) & 15u) == 0 &&
+                                  anchor_values != nullptr),
+             "K anchor values must be a 16-byte aligned float32 [B, Hk, D] CUDA tensor");
+  TB_REQUIRE(anchor_mode != 1 || anchors != nullptr, "K anchor scratch must be a CUDA tensor");
+  TB_REQUIRE(nan_code == 0 || nan_code == -127, "nan_code must be 0 or -127");
   RotParams a{};
   a.in[0] = q;
   a.in[1] = k;
@@ -463,7 +573,8 @@ void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out
   a.out[1] = k_out;
   a.scale[0] = q_scale;
   a.scale[1] = k_scale;
-  a.anchors = anchors;
+  a.anchor_values = anchor_mode ? anchor_values : nullptr;
+  a.nan_code = static_cast<float>(nan_code);
   a.heads[0] = static_cast<int>(Hq);
   a.heads[1] = static_cast<int>(Hk);
   a.length[0] = static_cast<int>(Lq);
@@ -481,8 +592,9 @@ void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out
   const int64_t tasks = Hq * a.blocks[0] + Hk * a.blocks[1];
   TB_REQUIRE(tasks <= INT32_MAX, "Q/K dimensions exceed the kernel range");
   const dim3 grid(static_cast<unsigned>(tasks), static_cast<unsigned>(B));
-  if (anchors != nullptr) {
-    AnchorParams ap{k, anchors, static_cast<int>(Hk), static_cast<int>(Lk), s[3], s[4], s[5]};
+  if (anchor_mode == 1) {
+    AnchorParams ap{k, anchors, anchor_values, static_cast<int>(Hk), static_cast<int>(Lk),
+                    s[3], s[4], s[5]};
     const dim3 ag(static_cast<unsigned>(Hk), static_cast<unsigned>(B));
     TB_REQUIRE(Hk <= 65535, "K head count exceeds the grid range");
     if (dtype == TB_DTYPE_BF16) {
@@ -500,6 +612,60 @@ void rot_quant_launch(const void* q, const void* k, int8_t* q_out, int8_t* k_out
   } else {
     if (D == 128) rot_quant_kernel<__half, 128><<<grid, 128, 0, stream>>>(a);
     else rot_quant_kernel<__half, 64><<<grid, 128, 0, stream>>>(a);
+  }
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+void qk_anchor_launch(const void* key, const void* key_norm, const void* freqs,
+                      const float* key_rrms, int32_t* anchors, float* anchor_values, int64_t B,
+                      int64_t Hk, int64_t Lk, int64_t D, const int64_t* k_strides,
+                      const int64_t* freq_strides, int64_t freq_batches, int64_t freq_sequence,
+                      int64_t rot_dim, int norm_scope, int split_half, int dtype, float eps,
+                      cudaStream_t stream) {
+  TB_REQUIRE(key && key_norm && anchors && anchor_values && k_strides,
+             "K, its norm weight and the anchor outputs must be CUDA tensors");
+  TB_REQUIRE(dtype == TB_DTYPE_BF16 || dtype == TB_DTYPE_F16, "K must be float16 or bfloat16");
+  TB_REQUIRE(D == 64 || D == 128, "fused Q/K preprocessing requires head_dim 64 or 128");
+  TB_REQUIRE(B > 0 && Hk > 0 && Lk > 0 && B <= 65535 && Hk <= 65535 && Lk <= INT32_MAX,
+             "K dimensions must be positive and within the CUDA grid range");
+  TB_REQUIRE(norm_scope >= 0 && norm_scope <= 2, "norm_scope must be 0, 1 or 2");
+  TB_REQUIRE(norm_scope == 0 || key_rrms != nullptr, "row RRMS of K must be provided");
+  TB_REQUIRE(rot_dim >= 0 && rot_dim <= D && rot_dim % 2 == 0,
+             "rot_dim must be even and within head_dim");
+  TB_REQUIRE(rot_dim == 0 || (freqs && freq_strides),
+             "RoPE frequencies are required when rot_dim > 0");
+  ProcAnchorParams p{};
+  p.k = key;
+  p.norm = key_norm;
+  // Pointers the kernel does not use at run time still name readable memory.
+  p.freqs = rot_dim > 0 ? freqs : key;
+  p.rrms = norm_scope ? key_rrms : static_cast<const float*>(key);
+  p.anchors = anchors;
+  p.values = anchor_values;
+  p.H = static_cast<int>(Hk);
+  p.L = static_cast<int>(Lk);
+  p.rot_dim = static_cast<int>(rot_dim);
+  p.split_half = split_half;
+  p.row_scope = norm_scope ? 1 : 0;
+  p.sb = k_strides[0];
+  p.sh = k_strides[1];
+  p.sl = k_strides[2];
+  if (rot_dim > 0) {
+    p.f_b = freq_strides[0]; p.f_s = freq_strides[1]; p.f_p = freq_strides[2];
+    p.f_r = freq_strides[3]; p.f_c = freq_strides[4];
+    p.f_batches = static_cast<int>(freq_batches);
+    p.f_seq = static_cast<int>(freq_sequence);
+  } else {
+    p.f_batches = p.f_seq = 1;
+  }
+  p.eps = eps;
+  const dim3 grid(static_cast<unsigned>(Hk), static_cast<unsigned>(B));
+  if (dtype == TB_DTYPE_BF16) {
+    if (D == 128) qk_anchor_kernel<__nv_bfloat16, 128><<<grid, 128, 0, stream>>>(p);
+    else qk_anchor_kernel<__nv_bfloat16, 64><<<grid, 128, 0, stream>>>(p);
+  } else {
+    if (D == 128) qk_anchor_kernel<__half, 128><<<grid, 128, 0, stream>>>(p);
+    else qk_anchor_kernel<__half, 64><<<grid, 128, 0, stream>>>(p);
   }
   TB_CUDA_CHECK(cudaGetLastError());
 }

@@ -312,21 +312,56 @@ TB_API int tb_qk_int8_sv_f16_accum_f32_attn(const int8_t *q, const int8_t *k, co
  * vector and butterfly order), then Q is quantized per 16-token tile into
  * query_scale [B, Hq, ceil(Lq/64)*4] and K per 64-token block into key_scale
  * [B, Hk, ceil(Lk/64)], amax floor 1e-7, scale = amax / 127, codes
- * rni(x * 127 / amax).  anchors: int32 [B, Hk] scratch, or NULL; when given,
- * each (batch, kv head) first picks its K anchor row (or -1) from nine sampled
- * keys and that row is subtracted from every key before the rotation.
- * strides (elements, 12 values): q (b, h, l), k (b, h, l), q_out (b, h, l),
- * k_out (b, h, l); last dimension contiguous, Q/K rows 16-byte aligned, the
- * INT8 outputs 8-byte aligned.  dtype BF16 / F16.  Replaces
- * quant_qk_per_warp_int8_rotated_anchored_cuda (anchors given) and
- * quant_qk_per_warp_int8_rotated_cuda (NULL) (kernel/csrc/turing/sage/
- * fused.h:55-78, fused.cu:1252-1287 with the kernels at :201-639). */
+ * rni(x * 127 / amax), a NaN coded nan_code (0 or -127).  anchor_mode 0: no
+ * K anchor; 1: each (batch, kv head) picks its anchor row from nine sampled
+ * keys, writes it to anchors int32 [B, Hk] (or -1) and its values to
+ * anchor_values fp32 [B, Hk, D] (zeros for -1), and K minus those values is
+ * rotated; 2: anchor_values are given (tb_qk_anchor_processed) and
+ * subtracted.  strides (elements, 12 values): q (b, h, l), k (b, h, l),
+ * q_out (b, h, l), k_out (b, h, l); last dimension contiguous, Q/K rows
+ * 16-byte aligned, the INT8 outputs 8-byte aligned.  dtype BF16 / F16.
+ * Replaces quant_qk_per_warp_int8_rotated_anchored_cuda (mode 1) and
+ * quant_qk_per_warp_int8_rotated_cuda (mode 0) (kernel/csrc/turing/sage/
+ * fused.h:55-78, fused.cu:1252-1287 with the kernels at :201-639), and with
+ * mode 2 / nan_code -127 the quantizing half of the fused prologue's rotated
+ * form (qk_preprocess.cu:417-563). */
 TB_API int tb_quant_qk_int8_rotated(const void *query, const void *key, int8_t *query_out,
                                     int8_t *key_out, float *query_scale, float *key_scale,
-                                    int32_t *anchors, int64_t batch, int64_t query_heads,
-                                    int64_t key_heads, int64_t query_length, int64_t key_length,
-                                    int64_t head_dim, const int64_t *strides, int dtype,
-                                    tb_stream_t stream);
+                                    int32_t *anchors, float *anchor_values, int64_t batch,
+                                    int64_t query_heads, int64_t key_heads, int64_t query_length,
+                                    int64_t key_length, int64_t head_dim, const int64_t *strides,
+                                    int anchor_mode, int nan_code, int dtype, tb_stream_t stream);
+
+/* The normalizing half of tb_quant_qk_rms_rope_int8 for its Hadamard-rotated
+ * form: the same RMSNorm + RoPE (same arguments and checks), but each token's
+ * values are written, rounded to the input dtype, to query_out / key_out (16-bit,
+ * 16-byte aligned, strides in strides[6..11]) instead of being quantized.
+ * Replaces the value computation of quantize_tile<..., Rotate>
+ * (kernel/csrc/turing/sage/qk_preprocess.cu:417-537). */
+TB_API int tb_qk_rms_rope_apply(const void *query, const void *key, void *query_out,
+                                void *key_out, const void *query_norm, const void *key_norm,
+                                const void *freqs, float *query_rrms, float *key_rrms,
+                                int64_t batch, int64_t query_heads, int64_t key_heads,
+                                int64_t query_length, int64_t key_length, int64_t head_dim,
+                                const int64_t *strides, const int64_t *freq_strides,
+                                int64_t freq_batches, int64_t freq_sequence, int64_t rot_dim,
+                                int norm_scope, int split_half, int dtype, float epsilon,
+                                tb_stream_t stream);
+
+/* K anchor of the fused prologue's rotated form: nine sampled tokens of each
+ * (batch, kv head) normalized and rotated as tb_qk_rms_rope_apply does, with
+ * their own RRMS (norm_scope 0: one FMA chain over the channels; 1/2: key_rrms
+ * [B, Lk] as written by the row pass), then the anchor rule of
+ * tb_quant_qk_int8_rotated; anchors int32 [B, Hk] (row or -1), anchor_values
+ * fp32 [B, Hk, D].  key_strides (b, h, l) in elements.  Replaces
+ * detect_anchor_kernel (kernel/csrc/turing/sage/qk_preprocess.cu:252-415). */
+TB_API int tb_qk_anchor_processed(const void *key, const void *key_norm, const void *freqs,
+                                  const float *key_rrms, int32_t *anchors, float *anchor_values,
+                                  int64_t batch, int64_t key_heads, int64_t key_length,
+                                  int64_t head_dim, const int64_t *key_strides,
+                                  const int64_t *freq_strides, int64_t freq_batches,
+                                  int64_t freq_sequence, int64_t rot_dim, int norm_scope,
+                                  int split_half, int dtype, float epsilon, tb_stream_t stream);
 
 /* Channel-wise INT8 V: per (batch, head, channel) scale = max(amax over the
  * tokens / 127, 1e-12) into scale [B, H, D] fp32 (also the kernels' amax

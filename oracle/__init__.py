@@ -67,9 +67,14 @@ def lib() -> ctypes.CDLL:
         L.orc_qk_rms_rope.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64,
                                       _i64, _i64, _int, _int, _int, _int, ctypes.c_float, _ptr,
                                       _ptr]
-        L.orc_k_anchor.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _ptr]
+        L.orc_k_anchor.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr]
         L.orc_rot_quant.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _ptr,
-                                    _ptr, _ptr]
+                                    _int, _ptr, _ptr]
+        L.orc_qk_processed.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64, _i64,
+                                       _int, _int, _int, _int, ctypes.c_float, _ptr]
+        L.orc_qk_anchor_processed.argtypes = [_ptr, _ptr, _ptr, _i64, _i64, _i64, _i64, _i64,
+                                              _i64, _int, _int, _int, _int, ctypes.c_float, _ptr,
+                                              _ptr]
         L.orc_quant_v.argtypes = [_ptr, _int, _i64, _i64, _i64, _i64, _i64, _i64, _ptr, _ptr]
         L.orc_w8a8_attn.argtypes = [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _int, _ptr]
@@ -310,23 +315,29 @@ def _hnd(x_bits, layout):
     return x
 
 
-def k_anchor(k_bits: np.ndarray, *, layout: str = "HND", fp16: bool = False) -> np.ndarray:
+def k_anchor(k_bits: np.ndarray, *, layout: str = "HND", fp16: bool = False,
+             with_values: bool = False):
     """K stabilization anchor row per (batch, kv head), or -1
-    (DetectKAnchorKernel, sage/fused.cu:406-556).  Returns int32 [B, Hk]."""
+    (DetectKAnchorKernel, sage/fused.cu:406-556).  Returns int32 [B, Hk]
+    (and, with_values, the anchor rows as fp32 [B, Hk, D], zeros for -1)."""
     k = _hnd(k_bits, layout)
     B, H, L, D = k.shape
     out = np.empty((B, H), np.int32)
-    lib().orc_k_anchor(_p(k), int(fp16), B * H, L, D, L * D, D, _p(out))
-    return out
+    vals = np.empty((B, H, D), np.float32)
+    lib().orc_k_anchor(_p(k), int(fp16), B * H, L, D, L * D, D, _p(out), _p(vals))
+    return (out, vals) if with_values else out
 
 
 def rot_quant(x_bits: np.ndarray, tile_tokens: int, *, layout: str = "HND", fp16: bool = False,
-              anchor: np.ndarray | None = None, block: int | None = None):
+              anchor_values: np.ndarray | None = None, block: int | None = None,
+              nan_code: int = 0):
     """Randomized-Hadamard per-tile INT8 (quant_int8_tile, sage/fused.cu:260-398)
     of a [B, H, L, D] (HND) / [B, L, H, D] (NHD) tensor with D = 64 or 128.
-    tile_tokens 16 (Q, per-warp layout: pass block=64) or 64 (K).  anchor:
-    optional int32 [B, H] rows subtracted first (K).  Returns (codes int8 in the
-    input layout, scale fp32 [B, H, tiles])."""
+    tile_tokens 16 (Q, per-warp layout: pass block=64) or 64 (K).
+    anchor_values: optional fp32 [B, H, D] subtracted first (K; zeros = no
+    anchor).  nan_code: code of a NaN (0 as fused.cu, -127 as the fused
+    prologue).  Returns (codes int8 in the input layout, scale fp32
+    [B, H, tiles])."""
     x = _hnd(x_bits, layout)
     B, H, L, D = x.shape
     if D not in (64, 128):
@@ -336,9 +347,9 @@ def rot_quant(x_bits: np.ndarray, tile_tokens: int, *, layout: str = "HND", fp16
         tiles = (L + block - 1) // block * (block // tile_tokens)
     out = np.empty(x.shape, np.int8)
     scale = np.empty((B, H, tiles), np.float32)
-    a = None if anchor is None else _c(anchor, np.int32).reshape(B * H)
+    a = None if anchor_values is None else _c(anchor_values, np.float32).reshape(B * H, D)
     lib().orc_rot_quant(_p(x), int(fp16), B * H, L, D, L * D, D, tile_tokens, tiles,
-                        None if a is None else _p(a), _p(out), _p(scale))
+                        None if a is None else _p(a), int(nan_code), _p(out), _p(scale))
     if layout == "NHD":
         out = np.ascontiguousarray(out.transpose(0, 2, 1, 3))
     return out, scale
@@ -349,9 +360,70 @@ def per_warp_int8_hadamard(q_bits, k_bits, *, layout: str = "HND", fp16: bool = 
     """Q per 16 rows and K per 64 rows, both rotated, K anchored when
     stabilize_k (turing_sage/quant.py:182-243).  Returns (q8, q_scale, k8,
     k_scale, anchors or None)."""
-    anchors = k_anchor(k_bits, layout=layout, fp16=fp16) if stabilize_k else None
+    anchors, values = (k_anchor(k_bits, layout=layout, fp16=fp16, with_values=True)
+                       if stabilize_k else (None, None))
     q8, qs = rot_quant(q_bits, 16, layout=layout, fp16=fp16, block=64)
-    k8, ks = rot_quant(k_bits, 64, layout=layout, fp16=fp16, anchor=anchors)
+    k8, ks = rot_quant(k_bits, 64, layout=layout, fp16=fp16, anchor_values=values)
+    return q8, qs, k8, ks, anchors
+
+
+def _prologue_args(x_bits, norm_bits, freqs_bits, rot_dim, layout):
+    x = _hnd(x_bits, layout)
+    f = None
+    fb = fs = 1
+    if rot_dim > 0:
+        f = _c(freqs_bits, np.uint16)
+        fb, fs = f.shape[0], f.shape[1]
+        f = np.ascontiguousarray(f.reshape(fb, fs, rot_dim // 2, 2, 2))
+    return x, _c(norm_bits, np.uint16).reshape(-1), f, fb, fs
+
+
+def qk_processed(x_bits, norm_bits, freqs_bits, *, eps: float, rot_dim: int,
+                 layout: str = "HND", norm_scope: str = "head", split_half: bool = False,
+                 fp16: bool = False) -> np.ndarray:
+    """RMSNorm + RoPE of every token as the fused prologue computes it before
+    quantizing (qk_preprocess.cu:151-201): bits of the input dtype, input layout."""
+    x, n, f, fb, fs = _prologue_args(x_bits, norm_bits, freqs_bits, rot_dim, layout)
+    B, H, L, D = x.shape
+    out = np.empty(x.shape, np.uint16)
+    lib().orc_qk_processed(_p(x), _p(n), None if f is None else _p(f), B, H, L, D, fb, fs,
+                           int(rot_dim), int(bool(split_half)), int(norm_scope == "row"),
+                           int(fp16), float(eps), _p(out))
+    if layout == "NHD":
+        out = np.ascontiguousarray(out.transpose(0, 2, 1, 3))
+    return out
+
+
+def qk_anchor_processed(k_bits, norm_bits, freqs_bits, *, eps: float, rot_dim: int,
+                        layout: str = "HND", norm_scope: str = "head", split_half: bool = False,
+                        fp16: bool = False):
+    """The fused prologue's K anchor (detect_anchor_kernel, qk_preprocess.cu:252-415).
+    Returns (int32 [B, H] row or -1, fp32 [B, H, D] anchor values)."""
+    k, n, f, fb, fs = _prologue_args(k_bits, norm_bits, freqs_bits, rot_dim, layout)
+    B, H, L, D = k.shape
+    idx = np.empty((B, H), np.int32)
+    vals = np.empty((B, H, D), np.float32)
+    lib().orc_qk_anchor_processed(_p(k), _p(n), None if f is None else _p(f), B, H, L, D, fb, fs,
+                                  int(rot_dim), int(bool(split_half)), int(norm_scope == "row"),
+                                  int(fp16), float(eps), _p(idx), _p(vals))
+    return idx, vals
+
+
+def qk_rms_rope_rotated_int8(q_bits, k_bits, q_norm, k_norm, freqs_bits, *, eps: float,
+                             rot_dim: int, layout: str = "HND", norm_scope: str = "head",
+                             split_half: bool = False, fp16: bool = False,
+                             stabilize_k: bool = True):
+    """The fused prologue with rotate_qk (qk_preprocess.cu:417-753): processed
+    Q/K, K minus its processed anchor, randomized Hadamard, per-tile INT8 with
+    NaN -> -127.  Returns (q8, q_scale, k8, k_scale, anchors or None)."""
+    kw = dict(eps=eps, rot_dim=rot_dim, layout=layout, norm_scope=norm_scope,
+              split_half=split_half, fp16=fp16)
+    qp = qk_processed(q_bits, q_norm, freqs_bits, **kw)
+    kp = qk_processed(k_bits, k_norm, freqs_bits, **kw)
+    anchors, values = (qk_anchor_processed(k_bits, k_norm, freqs_bits, **kw)
+                       if stabilize_k else (None, None))
+    q8, qs = rot_quant(qp, 16, layout=layout, fp16=fp16, block=64, nan_code=-127)
+    k8, ks = rot_quant(kp, 64, layout=layout, fp16=fp16, anchor_values=values, nan_code=-127)
     return q8, qs, k8, ks, anchors
 
 

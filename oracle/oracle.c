@@ -492,11 +492,57 @@ static float head_rrms(const uint16_t *row, int64_t D, int fp16, float eps) {
  * split-half, (p, p + rot_dim/2): v = T(fma(f[row][1], n1, f[row][0] * n0));
  * per tile amax = max(1e-7, max|v|), scale = amax / 127,
  * q = clamp(rint(v * (127 / amax)), -127, 127), IEEE divides. */
+/* The processed row of token tok of head h (qk_preprocess.cu:151-201):
+ * n = T(x * rrms * w) per channel, then RoPE on the first rot_dim channels,
+ * v = T(fma(f[row][1], n(second), f[row][0] * n(first))).  nrm: D scratch. */
+static void process_row(const uint16_t *row, const uint16_t *w, const uint16_t *freqs, int64_t b,
+                        int64_t tok, int64_t D, int64_t fb, int64_t fs, int rot_dim,
+                        int split_half, int fp16, float rrms, float *nrm, float *v) {
+    const int half = rot_dim / 2;
+    for (int64_t c = 0; c < D; ++c)
+        nrm[c] = round_elem(elem(row, c, fp16) * rrms * elem(w, c, fp16), fp16);
+    for (int64_t c = 0; c < D; ++c) {
+        v[c] = nrm[c];
+        if (c < rot_dim) {
+            const int64_t pair = split_half ? (c < half ? c : c - half) : c / 2;
+            const int64_t first = split_half ? pair : 2 * pair;
+            const int64_t second = split_half ? pair + half : first + 1;
+            const int64_t comp = split_half ? (c >= half) : (c & 1);
+            const int64_t fbase =
+                (((fb == 1 ? 0 : b) * fs + (fs == 1 ? 0 : tok)) * half + pair) * 4 + comp * 2;
+            const float f0 = elem(freqs, fbase, fp16);
+            const float f1 = elem(freqs, fbase + 1, fp16);
+            v[c] = round_elem(fmaf(f1, nrm[second], f0 * nrm[first]), fp16);
+        }
+    }
+}
+
+/* The normalized + rotated values of every token (the first half of the
+ * fused prologue), written as T bits in the input's [B, H, L, D] layout. */
+void orc_qk_processed(const uint16_t *x, const uint16_t *norm, const uint16_t *freqs, int64_t B,
+                      int64_t H, int64_t L, int64_t D, int64_t fb, int64_t fs, int rot_dim,
+                      int split_half, int row_scope, int fp16, float eps, uint16_t *out) {
+    float *nrm = (float *)malloc(sizeof(float) * (size_t)D);
+    float *v = (float *)malloc(sizeof(float) * (size_t)D);
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t tok = 0; tok < L; ++tok) {
+                const uint16_t *row = x + ((b * H + h) * L + tok) * D;
+                const float rrms = row_scope ? row_rrms(x, H, L, D, b, tok, fp16, eps)
+                                             : head_rrms(row, D, fp16, eps);
+                process_row(row, norm + (row_scope ? h * D : 0), freqs, b, tok, D, fb, fs,
+                            rot_dim, split_half, fp16, rrms, nrm, v);
+                uint16_t *o = out + ((b * H + h) * L + tok) * D;
+                for (int64_t c = 0; c < D; ++c) o[c] = fp16 ? f32_to_f16_rn(v[c]) : f32_to_bf16_rn(v[c]);
+            }
+    free(nrm);
+    free(v);
+}
+
 void orc_qk_rms_rope(const uint16_t *x, const uint16_t *norm, const uint16_t *freqs, int64_t B,
                      int64_t H, int64_t L, int64_t D, int64_t T, int64_t tiles, int64_t fb,
                      int64_t fs, int rot_dim, int split_half, int row_scope, int fp16, float eps,
                      int8_t *out, float *scale) {
-    const int half = rot_dim / 2;
     float *vals = (float *)malloc(sizeof(float) * (size_t)(T * D));
     float *nrm = (float *)malloc(sizeof(float) * (size_t)D);
     for (int64_t b = 0; b < B; ++b) {
@@ -510,24 +556,9 @@ void orc_qk_rms_rope(const uint16_t *x, const uint16_t *norm, const uint16_t *fr
                     const uint16_t *row = x + ((b * H + h) * L + tok) * D;
                     const float rrms = row_scope ? row_rrms(x, H, L, D, b, tok, fp16, eps)
                                                  : head_rrms(row, D, fp16, eps);
-                    for (int64_t c = 0; c < D; ++c)
-                        nrm[c] = round_elem(elem(row, c, fp16) * rrms * elem(w, c, fp16), fp16);
-                    for (int64_t c = 0; c < D; ++c) {
-                        float v = nrm[c];
-                        if (c < rot_dim) {
-                            const int64_t pair = split_half ? (c < half ? c : c - half) : c / 2;
-                            const int64_t first = split_half ? pair : 2 * pair;
-                            const int64_t second = split_half ? pair + half : first + 1;
-                            const int64_t comp = split_half ? (c >= half) : (c & 1);
-                            const int64_t fbase = (((fb == 1 ? 0 : b) * fs + (fs == 1 ? 0 : tok)) *
-                                                       half + pair) * 4 + comp * 2;
-                            const float f0 = elem(freqs, fbase, fp16);
-                            const float f1 = elem(freqs, fbase + 1, fp16);
-                            v = round_elem(fmaf(f1, nrm[second], f0 * nrm[first]), fp16);
-                        }
-                        vals[i * D + c] = v;
-                        amax = fmaxf(amax, fabsf(v));
-                    }
+                    process_row(row, w, freqs, b, tok, D, fb, fs, rot_dim, split_half, fp16, rrms,
+                                nrm, vals + i * D);
+                    for (int64_t c = 0; c < D; ++c) amax = fmaxf(amax, fabsf(vals[i * D + c]));
                 }
                 scale[(b * H + h) * tiles + t] = amax / 127.0f;
                 const float inv = 127.0f / amax;
@@ -593,92 +624,141 @@ static float warp_tree(const float *lane_vals, int is_max) {
     return a[0];
 }
 
-/* K stabilization anchor of each (batch, kv head) (DetectKAnchorKernel,
- * fused.cu:406-556): nine keys at rows s * (L - 1) / 8, the sample nearest
- * their mean (squared distance of 9 * sample - sum), kept only when centring
- * on it lowers the energy of the samples and grows their range by at most
- * 12.5 %.  128 threads, one channel each, warp trees, then the four warps in
- * order.  anchor[o] = row index or -1. */
-void orc_k_anchor(const uint16_t *k, int fp16, int64_t outer, int64_t L, int64_t D,
-                  int64_t s_outer, int64_t s_tok, int32_t *anchor) {
+/* Anchor choice over nine sampled key rows samp[9][128] of one (batch, kv head)
+ * (DetectKAnchorKernel, fused.cu:406-556; detect_anchor_kernel,
+ * qk_preprocess.cu:252-415, the same statistics): the sample nearest the
+ * samples' mean (squared distance of 9 * sample - sum) is kept when centring on
+ * it lowers their energy and grows their range by at most 12.5 %.  128
+ * threads, one channel each, warp trees, then the four warps in order.
+ * Returns the chosen sample (0..8) or -1. */
+static int anchor_select(float samp[9][128], int64_t D) {
     enum { NS = 9, NT = 128 };
-    for (int64_t o = 0; o < outer; ++o) {
-        float samp[NS][128];
+    float oe[NT], om[NT], cd[NS][NT];
+    for (int t = 0; t < NT; ++t) {
+        oe[t] = om[t] = 0.0f;
+        for (int c = 0; c < NS; ++c) cd[c][t] = 0.0f;
+        if (t >= D) continue;
+        float sum = 0.0f;
         for (int s = 0; s < NS; ++s) {
-            const int64_t row = (int64_t)s * (L - 1) / (NS - 1);
+            const float v = samp[s][t];
+            oe[t] = fmaf(v, v, oe[t]);
+            om[t] = fmaxf(om[t], fabsf(v));
+            sum += v;
+        }
+        for (int c = 0; c < NS; ++c) {
+            const float dist = fmaf(9.0f, samp[c][t], -sum);  /* 9 * x is exact */
+            cd[c][t] = fmaf(dist, dist, cd[c][t]);
+        }
+    }
+    float w_oe[4], w_om[4], w_cd[NS][4];
+    for (int w = 0; w < 4; ++w) {
+        w_oe[w] = warp_tree(oe + 32 * w, 0);
+        w_om[w] = warp_tree(om + 32 * w, 1);
+        for (int c = 0; c < NS; ++c) w_cd[c][w] = warp_tree(cd[c] + 32 * w, 0);
+    }
+    int best = 0;
+    float best_d = 3.402823466e+38F;
+    for (int c = 0; c < NS; ++c) {
+        float d = 0.0f;
+        for (int w = 0; w < 4; ++w) d += w_cd[c][w];
+        if (d < best_d) {
+            best = c;
+            best_d = d;
+        }
+    }
+    float be[NT], bm[NT];
+    for (int t = 0; t < NT; ++t) {
+        be[t] = bm[t] = 0.0f;
+        if (t >= D) continue;
+        for (int s = 0; s < NS; ++s) {
+            const float r = samp[s][t] - samp[best][t];
+            be[t] = fmaf(r, r, be[t]);
+            bm[t] = fmaxf(bm[t], fabsf(r));
+        }
+    }
+    float toe = 0.0f, tom = 0.0f, tbe = 0.0f, tbm = 0.0f;
+    for (int w = 0; w < 4; ++w) {
+        toe += w_oe[w];
+        tom = fmaxf(tom, w_om[w]);
+        tbe += warp_tree(be + 32 * w, 0);
+        tbm = fmaxf(tbm, warp_tree(bm + 32 * w, 1));
+    }
+    return tbe < toe && tbm <= tom * 1.125f ? best : -1;
+}
+
+/* Anchor of the raw keys (DetectKAnchorKernel): nine rows s * (L - 1) / 8 of
+ * K; anchor[o] = row index or -1, values[o, :] = that row as float or zeros
+ * (values may be NULL). */
+void orc_k_anchor(const uint16_t *k, int fp16, int64_t outer, int64_t L, int64_t D,
+                  int64_t s_outer, int64_t s_tok, int32_t *anchor, float *values) {
+    for (int64_t o = 0; o < outer; ++o) {
+        float samp[9][128];
+        for (int s = 0; s < 9; ++s) {
+            const int64_t row = (int64_t)s * (L - 1) / 8;
             for (int c = 0; c < 128; ++c)
                 samp[s][c] = c < D ? elem(k, o * s_outer + row * s_tok + c, fp16) : 0.0f;
         }
-        float oe[NT], om[NT], cd[NS][NT];
-        for (int t = 0; t < NT; ++t) {
-            oe[t] = om[t] = 0.0f;
-            for (int c = 0; c < NS; ++c) cd[c][t] = 0.0f;
-            if (t >= D) continue;
-            float sum = 0.0f;
-            for (int s = 0; s < NS; ++s) {
-                const float v = samp[s][t];
-                oe[t] = fmaf(v, v, oe[t]);
-                om[t] = fmaxf(om[t], fabsf(v));
-                sum += v;
-            }
-            for (int c = 0; c < NS; ++c) {
-                const float dist = fmaf(9.0f, samp[c][t], -sum);  /* 9 * x is exact */
-                cd[c][t] = fmaf(dist, dist, cd[c][t]);
-            }
-        }
-        float w_oe[4], w_om[4], w_cd[NS][4];
-        for (int w = 0; w < 4; ++w) {
-            w_oe[w] = warp_tree(oe + 32 * w, 0);
-            w_om[w] = warp_tree(om + 32 * w, 1);
-            for (int c = 0; c < NS; ++c) w_cd[c][w] = warp_tree(cd[c] + 32 * w, 0);
-        }
-        int best = 0;
-        float best_d = 3.402823466e+38F;
-        for (int c = 0; c < NS; ++c) {
-            float d = 0.0f;
-            for (int w = 0; w < 4; ++w) d += w_cd[c][w];
-            if (d < best_d) {
-                best = c;
-                best_d = d;
-            }
-        }
-        float be[NT], bm[NT];
-        for (int t = 0; t < NT; ++t) {
-            be[t] = bm[t] = 0.0f;
-            if (t >= D) continue;
-            for (int s = 0; s < NS; ++s) {
-                const float r = samp[s][t] - samp[best][t];
-                be[t] = fmaf(r, r, be[t]);
-                bm[t] = fmaxf(bm[t], fabsf(r));
-            }
-        }
-        float toe = 0.0f, tom = 0.0f, tbe = 0.0f, tbm = 0.0f;
-        for (int w = 0; w < 4; ++w) {
-            toe += w_oe[w];
-            tom = fmaxf(tom, w_om[w]);
-            tbe += warp_tree(be + 32 * w, 0);
-            tbm = fmaxf(tbm, warp_tree(bm + 32 * w, 1));
-        }
-        const int keep = tbe < toe && tbm <= tom * 1.125f;
-        anchor[o] = keep ? (int32_t)((int64_t)best * (L - 1) / (NS - 1)) : -1;
+        const int sel = anchor_select(samp, D);
+        anchor[o] = sel >= 0 ? (int32_t)((int64_t)sel * (L - 1) / 8) : -1;
+        if (values)
+            for (int64_t c = 0; c < D; ++c) values[o * D + c] = sel >= 0 ? samp[sel][c] : 0.0f;
     }
 }
 
-/* Randomized-Hadamard per-tile INT8 quantizer (quant_int8_tile, fused.cu:260-398):
- * per tile of T tokens (16: Q per warp; 64: K per block) the rows, minus the
- * anchor row when anchor[o] >= 0 (K only), are rotated (rot_row), amax starts
- * at 1e-7, scale = amax / 127, codes = rni_sat(x * (127 / amax)).  IEEE
- * divides (the reference's extension uses --use_fast_math).  x and out share
- * strides; scale is [outer, tiles]. */
+/* Anchor of the normalized + rotated keys of the fused prologue
+ * (detect_anchor_kernel, qk_preprocess.cu:252-415): the nine sampled tokens
+ * are processed as in process_row with their own RRMS (row scope: the row
+ * RRMS; head scope: one FMA chain over channels 0..D-1, then the correctly
+ * rounded 1/sqrt); the anchor's values are those processed floats.
+ * k [B, H, L, D] contiguous bits; anchor [B, H]; values [B, H, D]. */
+void orc_qk_anchor_processed(const uint16_t *k, const uint16_t *norm, const uint16_t *freqs,
+                             int64_t B, int64_t H, int64_t L, int64_t D, int64_t fb, int64_t fs,
+                             int rot_dim, int split_half, int row_scope, int fp16, float eps,
+                             int32_t *anchor, float *values) {
+    float nrm[128];
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h) {
+            float samp[9][128];
+            for (int s = 0; s < 9; ++s) {
+                const int64_t tok = (int64_t)s * (L - 1) / 8;
+                const uint16_t *row = k + ((b * H + h) * L + tok) * D;
+                float rrms;
+                if (row_scope) {
+                    rrms = row_rrms(k, H, L, D, b, tok, fp16, eps);
+                } else {
+                    float sum = 0.0f;
+                    for (int64_t c = 0; c < D; ++c) {
+                        const float v = elem(row, c, fp16);
+                        sum = fmaf(v, v, sum);
+                    }
+                    rrms = rsqrt_rn(sum / (float)D + eps);
+                }
+                for (int c = 0; c < 128; ++c) samp[s][c] = 0.0f;
+                process_row(row, norm + (row_scope ? h * D : 0), freqs, b, tok, D, fb, fs,
+                            rot_dim, split_half, fp16, rrms, nrm, samp[s]);
+            }
+            const int64_t o = b * H + h;
+            const int sel = anchor_select(samp, D);
+            anchor[o] = sel >= 0 ? (int32_t)((int64_t)sel * (L - 1) / 8) : -1;
+            for (int64_t c = 0; c < D; ++c) values[o * D + c] = sel >= 0 ? samp[sel][c] : 0.0f;
+        }
+}
+
+/* Randomized-Hadamard per-tile INT8 quantizer (quant_int8_tile, fused.cu:260-398;
+ * quantize_tile, qk_preprocess.cu:417-563): per tile of T tokens (16: Q per
+ * warp; 64: K per block) the rows, minus the anchor values [outer, D] when
+ * given (K only; zeros = no anchor), are rotated (rot_row), amax starts at
+ * 1e-7, scale = amax / 127, codes = rni(x * (127 / amax)) saturated, NaN ->
+ * nan_code (0: cvt.rni.sat.s8 of fused.cu; -127: the prologue's
+ * clamp(nearbyintf), qk_preprocess.cu:43-47).  IEEE divides (the reference's
+ * extension uses --use_fast_math).  x and out share strides; scale is
+ * [outer, tiles]. */
 void orc_rot_quant(const uint16_t *x, int fp16, int64_t outer, int64_t L, int64_t D,
                    int64_t s_outer, int64_t s_tok, int64_t T, int64_t tiles,
-                   const int32_t *anchor, int8_t *out, float *scale) {
+                   const float *anchor_values, int nan_code, int8_t *out, float *scale) {
     float *buf = (float *)malloc(sizeof(float) * (size_t)(T * D));
-    float anc[128];
     for (int64_t o = 0; o < outer; ++o) {
-        const int32_t a = anchor ? anchor[o] : -1;
-        if (a >= 0)
-            for (int64_t c = 0; c < D; ++c) anc[c] = elem(x, o * s_outer + (int64_t)a * s_tok + c, fp16);
+        const float *anc = anchor_values ? anchor_values + o * D : NULL;
         for (int64_t t = 0; t < tiles; ++t) {
             float amax = 0.0000001f;
             for (int64_t i = 0; i < T; ++i) {
@@ -687,7 +767,7 @@ void orc_rot_quant(const uint16_t *x, int fp16, int64_t outer, int64_t L, int64_
                 if (tok >= L) continue;
                 for (int64_t c = 0; c < D; ++c) {
                     v[c] = elem(x, o * s_outer + tok * s_tok + c, fp16);
-                    if (a >= 0) v[c] -= anc[c];
+                    if (anc) v[c] -= anc[c];
                 }
                 rot_row(v, (int)D);
                 for (int64_t c = 0; c < D; ++c) amax = fmaxf(amax, fabsf(v[c]));
@@ -697,8 +777,10 @@ void orc_rot_quant(const uint16_t *x, int fp16, int64_t outer, int64_t L, int64_
             for (int64_t i = 0; i < T; ++i) {
                 const int64_t tok = t * T + i;
                 if (tok >= L) continue;
-                for (int64_t c = 0; c < D; ++c)
-                    out[o * s_outer + tok * s_tok + c] = cvt_rni_sat_s8(buf[i * D + c] * inv);
+                for (int64_t c = 0; c < D; ++c) {
+                    const float y = buf[i * D + c] * inv;
+                    out[o * s_outer + tok * s_tok + c] = isnan(y) ? (int8_t)nan_code : cvt_rni_sat_s8(y);
+                }
             }
         }
     }

@@ -2,7 +2,7 @@
 own CUDA kernels (built from its sources by oracle/ref/build_ref.py into
 oracle/_ref) on seeded CPU-generated inputs, on a B200.
 
-    python tests/golden/make_golden.py [out_dir] [--only norm|qkrope]
+    python tests/golden/make_golden.py [out_dir] [--only norm|qkrope|qkrot|w8a8]
 
 Each fixture is a compressed .npz holding the inputs (as raw bits) and the
 reference's outputs.  tests/test_oracle_golden.py checks the CPU oracle
@@ -126,6 +126,56 @@ def qkrope_fixtures(dev, S) -> dict:
     return fx
 
 
+QKROT_CASES = [
+    # name, dtype, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs, stabilize, K offset
+    ("bf16_hnd_d128_row_anchor", torch.bfloat16, "HND", 1, 2, 2, 150, 150, 128, "row", False,
+     128, 1, 150, True, 2.0),
+    ("f16_nhd_d64_head_split", torch.float16, "NHD", 2, 3, 1, 70, 90, 64, "head", True, 48, 1,
+     1, True, 1.5),
+    ("bf16_hnd_d128_head_plain", torch.bfloat16, "HND", 1, 2, 2, 100, 100, 128, "head", False,
+     0, 1, 1, False, 0.0),
+]
+
+
+def qkrot_fixtures(dev, S) -> dict:
+    """The fused prologue's Hadamard-rotated form with the K anchor
+    (sage/qk_preprocess.cu:252-415, 417-753, rotate=True)."""
+    fx = {}
+    for i, (name, dt, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs, stab, off) in \
+            enumerate(QKROT_CASES):
+        g = torch.Generator().manual_seed(700 + i)
+        qshape = (B, hq, lq, D) if layout == "HND" else (B, lq, hq, D)
+        kshape = (B, hk, lk, D) if layout == "HND" else (B, lk, hk, D)
+        oshape = (1, hk, 1, D) if layout == "HND" else (1, 1, hk, D)
+        q = (torch.randn(qshape, generator=g) * 1.5 + 0.2).to(dt)
+        k = (torch.randn(kshape, generator=g) + torch.randn(oshape, generator=g) * off).to(dt)
+        nq, nk = (D if scope == "head" else hq * D), (D if scope == "head" else hk * D)
+        qn = (torch.rand((nq,), generator=g) + 0.5).to(dt)
+        kn = (torch.rand((nk,), generator=g) + 0.5).to(dt)
+        fr = rope_freqs(fb, fs, rot // 2, 800 + i, dt) if rot else torch.empty(0, dtype=dt)
+        qd, kd, qnd, knd, frd = (t.to(dev) for t in (q, k, qn, kn, fr))
+        q8 = torch.empty(qshape, dtype=torch.int8, device=dev)
+        k8 = torch.empty(kshape, dtype=torch.int8, device=dev)
+        qs = torch.empty((B, hq, (lq + 63) // 64 * 4), dtype=torch.float32, device=dev)
+        ks = torch.empty((B, hk, (lk + 63) // 64), dtype=torch.float32, device=dev)
+        qr = torch.empty((B, lq) if scope == "row" else (0,), dtype=torch.float32, device=dev)
+        kr = torch.empty((B, lk) if scope == "row" else (0,), dtype=torch.float32, device=dev)
+        ai = torch.empty((B, hk) if stab else (0,), dtype=torch.int32, device=dev)
+        av = torch.empty((B, hk, D) if stab else (0,), dtype=torch.float32, device=dev)
+        S.quant_qk_rms_rope_int8_cuda(qd, kd, q8, k8, qs, ks, qnd, knd, frd, qr, kr, ai, av,
+                                      1e-6, rot, 64, 16, 64, 1 if layout == "HND" else 0,
+                                      1 if scope == "row" else 0, split, True)
+        torch.cuda.synchronize()
+        rec = {"q": bits(q), "k": bits(k), "qn": bits(qn), "kn": bits(kn), "freqs": bits(fr),
+               "params": np.array([rot, int(split), int(scope == "row"), int(dt == torch.float16),
+                                   int(layout == "NHD"), int(stab)], np.int64),
+               "q8": bits(q8), "qs": bits(qs), "k8": bits(k8), "ks": bits(ks)}
+        if stab:
+            rec["anchors"], rec["anchor_values"] = bits(ai), bits(av)
+        fx[f"qkrot_{name}"] = rec
+    return fx
+
+
 def w8a8_fixtures(dev, S) -> dict:
     """Dense W8A8-PV path: rotated (anchored) Q/K INT8 (sage/fused.cu:201-639),
     channel-wise INT8 V (quant_v_int8_cuda_sm75.cu:58-246) and the force_dense
@@ -181,6 +231,12 @@ def main(out_dir: Path, only: str = "") -> None:
     out_dir.mkdir(parents=True, exist_ok=True)
     if only == "qkrope":
         fx = qkrope_fixtures(torch.device("cuda:0"), R.sage())
+        for name, rec in fx.items():
+            np.savez_compressed(out_dir / f"{name}.npz", **rec)
+        print(f"wrote {len(fx)} fixtures to {out_dir}")
+        return
+    if only == "qkrot":
+        fx = qkrot_fixtures(torch.device("cuda:0"), R.sage())
         for name, rec in fx.items():
             np.savez_compressed(out_dir / f"{name}.npz", **rec)
         print(f"wrote {len(fx)} fixtures to {out_dir}")

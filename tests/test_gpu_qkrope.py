@@ -178,9 +178,6 @@ def test_custom_op_and_prequantized_attention(oracle):
 def test_rejections():
     q = torch.randn((1, 1, 64, 128), device="cuda", dtype=torch.bfloat16)
     w = torch.ones(128, device="cuda", dtype=torch.bfloat16)
-    with pytest.raises(ValueError, match="rotate_qk"):
-        turing_sage.prequantize_rms_rope_qk(q, q, w, w, None, epsilon=1e-6, rot_dim=0,
-                                            rotate_qk=True)
     with pytest.raises(ValueError, match="head_dim 64 or 128"):
         turing_sage.prequantize_rms_rope_qk(q[..., :96], q[..., :96], w[:96], w[:96], None,
                                             epsilon=1e-6, rot_dim=0)
@@ -224,3 +221,87 @@ def test_row_sum_squares_and_given_rrms_match_row_scope(layout, D):
                                          **kw)
     for a, b in zip(own, given):
         assert torch.equal(a, b)
+
+
+ROT_CASES = [
+    # dt, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs, stabilize, K offset
+    (torch.bfloat16, "HND", 1, 2, 2, 150, 150, 128, "row", False, 128, 1, 150, True, 2.0),
+    (torch.float16, "NHD", 2, 3, 1, 70, 90, 64, "head", True, 48, 1, 1, True, 1.5),
+    (torch.bfloat16, "HND", 1, 2, 2, 100, 100, 128, "head", False, 0, 1, 1, True, 3.0),
+    (torch.bfloat16, "NHD", 1, 4, 2, 33, 129, 128, "row", True, 128, 1, 1, False, 0.0),
+    (torch.float16, "HND", 2, 1, 1, 1, 1, 64, "head", False, 64, 2, 1, True, 0.0),
+]
+
+
+def _rot_inputs(case, seed):
+    dt, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs, stab, off = case
+    g = torch.Generator().manual_seed(seed)
+    qs_ = (B, hq, lq, D) if layout == "HND" else (B, lq, hq, D)
+    ks_ = (B, hk, lk, D) if layout == "HND" else (B, lk, hk, D)
+    os_ = (1, hk, 1, D) if layout == "HND" else (1, 1, hk, D)
+    q = (torch.randn(qs_, generator=g) * 1.5 + 0.2).to(dt)
+    k = (torch.randn(ks_, generator=g) + torch.randn(os_, generator=g) * off).to(dt)
+    qn = (torch.rand((D if scope == "head" else hq * D,), generator=g) + 0.5).to(dt)
+    kn = (torch.rand((D if scope == "head" else hk * D,), generator=g) + 0.5).to(dt)
+    fr = _freqs(fb, fs, rot // 2, seed + 1, dt) if rot else None
+    return q, k, qn, kn, fr
+
+
+@pytest.mark.parametrize("case", ROT_CASES, ids=lambda c: "-".join(map(str, c[1:])))
+def test_rotated_prologue_bit_exact_against_oracle(oracle, case):
+    """rotate_qk (+ stabilize_k): normalized + rotated values written once,
+    the K anchor from nine processed samples, then the randomized-Hadamard
+    quantizer — codes and scales equal the oracle's (qk_preprocess.cu:252-753)."""
+    dt, layout, B, hq, hk, lq, lk, D, scope, split, rot, fb, fs, stab, off = case
+    q, k, qn, kn, fr = _rot_inputs(case, seed=lq * 5 + hk + D)
+    got = quant.rms_rope_per_warp_int8(q.cuda(), k.cuda(), qn.cuda(), kn.cuda(),
+                                       None if fr is None else fr.cuda(), epsilon=1e-6,
+                                       rot_dim=rot, tensor_layout=layout, norm_scope=scope,
+                                       split_half=split, rotate_qk=True, stabilize_k=stab)
+    want = oracle.qk_rms_rope_rotated_int8(
+        bf16_bits(q), bf16_bits(k), bf16_bits(qn), bf16_bits(kn),
+        None if fr is None else bf16_bits(fr), eps=1e-6, rot_dim=rot, layout=layout,
+        norm_scope=scope, split_half=split, fp16=dt == torch.float16, stabilize_k=stab)
+    _exact(got, want[:4])
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("qkrot_*.npz")), ids=lambda p: p.stem)
+def test_rotated_prologue_matches_reference_kernel(oracle, path):
+    f = np.load(path)
+    rot, split, row, fp16, nhd, stab = (int(v) for v in f["params"])
+    dt = torch.float16 if fp16 else torch.bfloat16
+    q, k, qn, kn = (from_bits(f[n], dt).cuda() for n in ("q", "k", "qn", "kn"))
+    fr = from_bits(f["freqs"], dt).cuda() if rot else None
+    got = quant.rms_rope_per_warp_int8(q, k, qn, kn, fr, epsilon=1e-6, rot_dim=rot,
+                                       tensor_layout="NHD" if nhd else "HND",
+                                       norm_scope="row" if row else "head",
+                                       split_half=bool(split), rotate_qk=True,
+                                       stabilize_k=bool(stab))
+    for g, w in ((got[0], f["q8"]), (got[2], f["k8"])):
+        d = np.abs(g.cpu().numpy().astype(np.int16) - w.astype(np.int16))
+        assert d.max() <= 1 and (d > 0).mean() <= 2e-3, (d.max(), (d > 0).mean())
+
+
+def test_rotated_prologue_feeds_w8a8(oracle):
+    """prequantize_rms_rope_qk(rotate_qk, stabilize_k) ->
+    prequantize_sol_sageattn_from_qk(use_w8a8, force_dense) ->
+    sol_sparse_sageattn_from_prequantized, the plugin's W8A8 route with the
+    fused prologue (attention/stable.py:388-460, 501-518): the output equals the
+    oracle's W8A8 attention on the oracle's codes."""
+    case = (torch.bfloat16, "HND", 1, 2, 2, 200, 200, 128, "row", False, 128, 1, 200, True, 2.0)
+    q, k, qn, kn, fr = _rot_inputs(case, seed=77)
+    v = torch.randn((1, 2, 200, 128), generator=torch.Generator().manual_seed(78)).to(torch.bfloat16)
+    qk = turing_sage.prequantize_rms_rope_qk(q.cuda(), k.cuda(), qn.cuda(), kn.cuda(), fr.cuda(),
+                                            epsilon=1e-6, rot_dim=128, norm_scope="row",
+                                            rotate_qk=True, stabilize_k=True)
+    assert qk.route_original_basis
+    pre = turing_sage.prequantize_sol_sageattn_from_qk(qk, v.cuda(), use_w8a8=True,
+                                                       force_dense=True)
+    out = turing_sage.sol_sparse_sageattn_from_prequantized(pre)
+    q8, qs, k8, ks, _ = oracle.qk_rms_rope_rotated_int8(
+        bf16_bits(q), bf16_bits(k), bf16_bits(qn), bf16_bits(kn), bf16_bits(fr), eps=1e-6,
+        rot_dim=128, norm_scope="row", stabilize_k=True)
+    v8, vs = oracle.quant_v(bf16_bits(v))
+    want = oracle.w8a8_attn(q8, k8, v8, vs, qs, ks, sm_scale=128 ** -0.5)
+    m = oracle.metrics(out.float().cpu().numpy(), want)
+    assert m["cosine"] >= 0.99999 and m["rel_l2"] <= 5e-3, m
