@@ -45,13 +45,26 @@ def w8a8_available() -> bool:
     return hasattr(module, "quantize_v_int8_sm75")
 
 
+def split_prequantization_available() -> bool:
+    """True when the split prequantize / execute path is present
+    (turing_sage/__init__.py:82-95 of the reference): the plugin then installs
+    its dense container function (attention/patches.py:494-497), which calls
+    prequantize_sageattn / prequantize_sol_sageattn(use_w8a8, force_dense) and
+    the *_from_prequantized executors, all built here.  The Sol summary entry
+    the reference's probe also looks for serves only the sparse routes, whose
+    own probes answer False."""
+    if not w8a8_available():
+        return False
+    module = importlib.import_module("comfyui_turing_utils_kernel._sage_qattn_sm75")
+    return hasattr(module, "sol_sparse_online_w8a8_prequantized_attn")
+
+
 # The plugin probes these before choosing a backend (turing_sage/__init__.py:25-145 of the
 # reference).  The sparse (Sol/SLA), varlen and VAE overlap kernels are not part of this
 # package, so each of these probes answers False.
 sparse_available = _not_built
 sla_available = _not_built
 w8a8_varlen_available = _not_built
-split_prequantization_available = _not_built
 overlap_blend_available = _not_built
 overlap_accumulate_available = _not_built
 

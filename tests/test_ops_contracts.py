@@ -175,3 +175,18 @@ def test_w8a8_attention_op_fake():
     q = torch.empty((1, 2, 50, 128), dtype=torch.bfloat16, device="meta")
     out = w8a8_attention(q, q, q, "HND", False, -1.0, 0, True, True)
     assert out.shape == q.shape and out.dtype == q.dtype and out.device.type == "meta"
+
+
+def test_backend_probes():
+    """The probes the plugin reads (turing_sage/__init__.py:16-107 of the
+    reference): dense Sage, W8A8, split prequantization and the fused Q/K
+    prologue are built; the sparse and varlen backends are not."""
+    from comfyui_turing_utils_kernel import turing_sage
+
+    assert turing_sage.available() and turing_sage.w8a8_available()
+    assert turing_sage.split_prequantization_available()
+    assert turing_sage.fused_qk_preprocessing_available()
+    for probe in (turing_sage.sparse_available, turing_sage.sla_available,
+                  turing_sage.w8a8_varlen_available, turing_sage.overlap_blend_available,
+                  turing_sage.overlap_accumulate_available):
+        assert probe() is False
