@@ -152,6 +152,13 @@ class ClockSampler:
 
 # --------------------------------------------------------------- workloads --
 
+def _host(t: torch.Tensor) -> torch.Tensor:
+    """A host copy of t, pinned when CUDA is present (the CPU-only reference
+    arm has no pinned memory)."""
+    t = t.cpu()
+    return t.pin_memory() if torch.cuda.is_available() else t
+
+
 class LinearWorkload:
     name = "linear"
     config = {"workload": "convrot_w8a8_linear (BASELINE configs[0])", "m": 4096, "k": 5120,
@@ -461,8 +468,8 @@ class AttentionWorkload:
         self.k = k.to(torch.bfloat16)
         del k
         self.v = torch.randn((B, H, L, D), generator=g, device=device).to(torch.bfloat16)
-        self.host = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
-        self.out_host = torch.empty_like(self.host[0]).pin_memory()
+        self.host = [_host(t) for t in (self.q, self.k, self.v)]
+        self.out_host = _host(torch.empty_like(self.host[0]))
         self.launches_per_step = 4  # Q quant, K token mean, K quant, attention
         self.dominant = "sage_attn"
         self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
@@ -537,7 +544,7 @@ class AttentionRopeWorkload(AttentionWorkload):
         c, s_ = torch.cos(ang), torch.sin(ang)
         self.freqs = torch.cat([torch.cat([c, -s_], -1), torch.cat([s_, c], -1)], -2).to(
             torch.bfloat16)
-        self.host += [t.cpu().pin_memory() for t in (self.qn, self.kn, self.freqs)]
+        self.host += [_host(t) for t in (self.qn, self.kn, self.freqs)]
         self.h2d_bytes = sum(t.numel() * t.element_size() for t in self.host)
         self.launches_per_step = 3  # row RRMS, fused Q/K prologue, attention
         # Algorithmic bytes of the prologue: Q and K read once, INT8 codes and
