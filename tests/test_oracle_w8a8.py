@@ -160,3 +160,20 @@ def test_oracle_matches_reference_kernels(oracle, path):
     ref = to_f(f["out"])
     m = oracle.metrics(o, ref)
     assert m["cosine"] > 0.99999 and m["rel_l2"] < 5e-3, m
+
+
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_reference_self_test_inputs(oracle, head_dim):
+    """The reference's W8A8 self-test (turing_sage/__init__.py:573-610): integer
+    ramps Q [1,4,129,D], K/V [1,2,151,D] in bf16 (GQA 2:1) stay within
+    rtol 0.12 / atol 0.09 of fp32 SDPA through the W8A8 arithmetic."""
+    qv = torch.arange(4 * 129 * head_dim, dtype=torch.float32)
+    kv = torch.arange(2 * 151 * head_dim, dtype=torch.float32)
+    q = (((qv % 29) - 14) / 16).reshape(1, 4, 129, head_dim).to(torch.bfloat16)
+    k = ((((kv * 3) % 31) - 15) / 16).reshape(1, 2, 151, head_dim).to(torch.bfloat16)
+    v = ((((kv * 5) % 37) - 18) / 16).reshape_as(k).to(torch.bfloat16)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    out = oracle.bf16_to_f32(oracle.w8a8attn(bits(q), bits(k), bits(v)))
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(),
+                                                           enable_gqa=True)
+    assert torch.allclose(torch.from_numpy(out), ref, rtol=0.12, atol=0.09)
