@@ -218,6 +218,37 @@ def preflight_sla(device: torch.device) -> None:
     raise RuntimeError("the SLA sparse attention extension is not built")
 
 
+def _unbuilt(name: str, what: str):
+    def entry(*args, **kwargs):
+        raise RuntimeError(f"the {what} extension is not built")
+
+    entry.__name__ = name
+    entry.__doc__ = (f"{name} of the reference's turing_sage: the {what} kernels are not part "
+                     "of this package (their availability probe answers False).")
+    return entry
+
+
+# Entry points of the reference's sparse (Sol / SLA), varlen and VAE-overlap
+# backends (turing_sage/__init__.py:122-369): named here so callers that reach
+# them past a False probe get the reference's "not built" error.
+sol_sparse_sageattn = _unbuilt("sol_sparse_sageattn", "Sol sparse attention")
+sol_sparse_sageattn_compiled = _unbuilt("sol_sparse_sageattn_compiled", "Sol sparse attention")
+sla_sparse_sageattn = _unbuilt("sla_sparse_sageattn", "SLA sparse attention")
+sla_sparse_sageattn_compiled = _unbuilt("sla_sparse_sageattn_compiled", "SLA sparse attention")
+sla_sparse_sageattn_from_prequantized = _unbuilt("sla_sparse_sageattn_from_prequantized",
+                                                 "SLA sparse attention")
+prequantize_sla_sageattn = _unbuilt("prequantize_sla_sageattn", "SLA sparse attention")
+prequantize_sla_sageattn_from_qk = _unbuilt("prequantize_sla_sageattn_from_qk",
+                                            "SLA sparse attention")
+sageattn_varlen = _unbuilt("sageattn_varlen", "Turing Sage varlen")
+sageattn_varlen_compiled = _unbuilt("sageattn_varlen_compiled", "Turing Sage varlen")
+w8a8attn_varlen = _unbuilt("w8a8attn_varlen", "W8A8 varlen attention")
+w8a8attn_varlen_compiled = _unbuilt("w8a8attn_varlen_compiled", "W8A8 varlen attention")
+overlap_blend_compiled = _unbuilt("overlap_blend_compiled", "VAE overlap blend")
+overlap_accumulate_compiled = _unbuilt("overlap_accumulate_compiled", "VAE overlap accumulate")
+run_attention_correctness_gate = _unbuilt("run_attention_correctness_gate", "Sol sparse attention")
+
+
 from . import custom_ops  # noqa: E402,F401  (registers the turing_utils:: sage custom ops)
 
 __all__ = ["available", "fused_qk_preprocessing_available", "overlap_accumulate_available",

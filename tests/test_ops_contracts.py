@@ -190,3 +190,14 @@ def test_backend_probes():
                   turing_sage.w8a8_varlen_available, turing_sage.overlap_blend_available,
                   turing_sage.overlap_accumulate_available):
         assert probe() is False
+
+
+def test_unbuilt_backends_raise():
+    """Entry points of the sparse / varlen / overlap backends exist and raise the
+    reference's "not built" error."""
+    from comfyui_turing_utils_kernel import turing_sage
+
+    for name in ("sol_sparse_sageattn", "sla_sparse_sageattn", "sageattn_varlen",
+                 "w8a8attn_varlen", "overlap_blend_compiled", "prequantize_sla_sageattn"):
+        with pytest.raises(RuntimeError, match="not built"):
+            getattr(turing_sage, name)(None, None, None)
