@@ -201,3 +201,75 @@ def test_unbuilt_backends_raise():
                  "w8a8attn_varlen", "overlap_blend_compiled", "prequantize_sla_sageattn"):
         with pytest.raises(RuntimeError, match="not built"):
             getattr(turing_sage, name)(None, None, None)
+
+
+def test_rotated_fused_qk_wrapper_contract():
+    """rotate_qk with stabilize_k hands the native entry the reference's K
+    anchor scratch (int32 [B, Hk], fp32 [B, Hk, D]) and rotate=True
+    (turing_sage/quant.py:59-92); without stabilize_k the scratch is empty."""
+    q = torch.empty((1, 3, 70, 64), dtype=torch.float16)
+    k = torch.empty((1, 1, 90, 64), dtype=torch.float16)
+    w = torch.empty((64,), dtype=torch.float16)
+    with mock.patch.object(quant._fused, "quant_qk_rms_rope_int8_cuda") as native:
+        quant.rms_rope_per_warp_int8(q, k, w, w, None, epsilon=1e-6, rot_dim=0,
+                                     tensor_layout="HND", norm_scope="head", split_half=False,
+                                     rotate_qk=True, stabilize_k=True)
+    args = native.call_args.args
+    assert args[11].dtype == torch.int32 and args[11].shape == (1, 1)
+    assert args[12].dtype == torch.float32 and args[12].shape == (1, 1, 64)
+    assert args[21] is True
+    with mock.patch.object(quant._fused, "quant_qk_rms_rope_int8_cuda") as native:
+        quant.rms_rope_per_warp_int8(q, k, w, w, None, epsilon=1e-6, rot_dim=0,
+                                     tensor_layout="HND", norm_scope="head", split_half=False,
+                                     rotate_qk=True, stabilize_k=False)
+    assert native.call_args.args[11].numel() == 0 and native.call_args.args[12].numel() == 0
+
+
+def test_w8a8_facade_rejections():
+    """w8a8attn / prequantize_sol_sageattn / the prequantized entry raise the
+    reference's errors before any device work (core.py:656-914,
+    sol_sparse_cuda_sm75.cu:2824-2833)."""
+    from comfyui_turing_utils_kernel import _sage_qattn_sm75 as qattn
+    from comfyui_turing_utils_kernel.turing_sage import core
+
+    q = torch.zeros((1, 2, 64, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="Unsupported tensor_layout"):
+        core.w8a8attn.__wrapped__(q, q, q, tensor_layout="BHLD")
+    with pytest.raises(TypeError, match="float16 or bfloat16"):
+        core.w8a8attn.__wrapped__(q.float(), q.float(), q.float())
+    wide = torch.zeros((1, 2, 64, 160), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match=r"head_dim in \[1, 128\]"):
+        core.w8a8attn.__wrapped__(wide, wide, wide)
+    with pytest.raises(ValueError, match="must be on CUDA"):
+        core.w8a8attn.__wrapped__(q, q, q)
+    with pytest.raises(ValueError, match="must be on CUDA"):   # checked before the layout
+        core.prequantize_sol_sageattn.__wrapped__(q, q, q, tensor_layout="NHD")
+    qk = core.PrequantizedQK(q.to(torch.int8), torch.zeros((1, 2, 4)), q.to(torch.int8),
+                             torch.zeros((1, 2, 1)), "HND", torch.bfloat16, 128, True)
+    with pytest.raises(ValueError, match="dense W8A8"):
+        core.prequantize_sol_sageattn_from_qk(qk, q, use_w8a8=False)
+    with pytest.raises(ValueError, match="causal masking is supported only by dense W8A8"):
+        core.prequantize_sol_sageattn_from_qk(qk, q, use_w8a8=True, is_causal=True)
+    with pytest.raises(ValueError, match="key_tile_tokens"):
+        core.prequantize_sol_sageattn_from_qk(qk, q, use_w8a8=True, force_dense=True,
+                                              key_tile_tokens=32)
+    with pytest.raises(RuntimeError, match="force_dense"):
+        qattn.sol_sparse_online_w8a8_prequantized_attn(
+            q, q, q, q, q, q, q, None, None, None, None, None, None, None, 1.0, 1, 0.1, 0, 0, 64,
+            0, 1)
+    with pytest.raises(RuntimeError, match="key_tile_tokens must be 64 or 128"):
+        qattn.sol_sparse_online_w8a8_prequantized_attn(
+            q, q, q, q, q, q, q, None, None, None, None, None, None, None, 1.0, 1, 0.1, 0, 1, 96,
+            0, 1)
+
+
+def test_w8a8_attention_is_a_fullgraph_leaf():
+    from comfyui_turing_utils_kernel.turing_sage.custom_ops import w8a8_attention
+
+    q = torch.empty((1, 8, 300, 128), dtype=torch.bfloat16, device="meta")
+    k = torch.empty((1, 2, 300, 128), dtype=torch.bfloat16, device="meta")
+    compiled = torch.compile(
+        lambda a, b, c: w8a8_attention(a, b, c, "HND", True, -1.0, 0, True, True),
+        backend="eager", fullgraph=True)
+    out = compiled(q, k, k)
+    assert out.shape == q.shape and out.dtype == q.dtype
