@@ -9,7 +9,8 @@
 //              rotated keys instead (qk_anchor_kernel).
 //   rotation   x -> H_D diag(sign) x / sqrt(D) over the D = 64 / 128 channels
 //              of a token (Sylvester Walsh-Hadamard, the sign vector of the
-//              reference), K minus its anchor row first.
+//              reference), K minus its anchor's values first (the raw anchor
+//              row, or the prologue's processed sample).
 //   codes      per tile (Q: 16 tokens, K: 64 tokens) amax = max(1e-7, |x|),
 //              scale = amax / 127, q = rni_sat(x * (127 / amax)); a NaN codes
 //              as 0 (fused.cu's cvt.rni.sat.s8) or -127 (the prologue's clamp
