@@ -1,0 +1,72 @@
+"""The float identities the sm_100a kernels rely on for bit-exact results,
+checked exhaustively (or on dense grids) in numpy float32 on the CPU.
+
+* Scores: an INT32 score s with |s| < 2^22 becomes the float 1.5 * 2^23 + s by
+  an integer add to the bits of 1.5 * 2^23 (sage_attn.cu magic_pair), and
+  subtracting 1.5 * 2^23 back gives float(s) exactly, so the W8A8 softmax's
+  fma(s, c, -m) is the reference's fmaf of the exact score.
+* Rounding: v + 1.5 * 2^23 rounds v to the nearest integer, ties to even, for
+  |v| < 2^22 (w8a8_quant.cu / convrot.cu code_bits, the W8A8 u8 codes of P),
+  i.e. it equals cvt.rni.
+* INT8 code -> fp16: the bits 0x6400 | (c ^ 0x80) are the fp16 1024 + (c + 128);
+  minus 1152 gives c exactly (w8a8_quant.cu v_codes_kernel).
+* u8 saturation: min(p + 1.5 * 2^23, 1.5 * 2^23 + 255) - 1.5 * 2^23 is
+  rni_sat_u8(p) for p in [0, 2^22) (sage_attn.cu u8_code_pair).
+* PV on the fp16 tensor path: every u8 x s8 product and every sum of 16 of
+  them is an integer below 2^24, exact in fp32 and in fp16 operands.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+MAGIC = np.float32(12582912.0)          # 1.5 * 2^23
+MAGIC_BITS = np.uint32(0x4B400000)
+
+
+def test_score_to_float_through_the_magic_constant():
+    s = np.arange(-(1 << 21), 1 << 21, 7, dtype=np.int64)
+    s = np.concatenate([s, [-(1 << 22) + 1, (1 << 22) - 1, -127 * 127 * 128, 127 * 127 * 128]])
+    bits = (s.astype(np.int64) + int(MAGIC_BITS)).astype(np.uint32)
+    t = bits.view(np.float32)
+    np.testing.assert_array_equal(t - MAGIC, s.astype(np.float32))
+
+
+def test_magic_add_is_round_half_even():
+    v = np.concatenate([np.arange(-300.0, 300.0, 0.125, dtype=np.float32),
+                        np.float32([0.5, 1.5, 2.5, -0.5, -1.5, 126.5, 127.5, 254.5, 255.49998])])
+    got = (v + MAGIC) - MAGIC
+    np.testing.assert_array_equal(got, np.rint(v).astype(np.float32))
+    # The low byte of the sum is the two's-complement INT8 code.
+    codes = (v[np.abs(v) <= 127] + MAGIC).view(np.uint32) & 0xFF
+    want = np.rint(v[np.abs(v) <= 127]).astype(np.int64) & 0xFF
+    np.testing.assert_array_equal(codes.astype(np.int64), want)
+
+
+def test_int8_code_to_fp16_exactly():
+    c = np.arange(-128, 128, dtype=np.int64)
+    biased = (0x6400 | ((c & 0xFF) ^ 0x80)).astype(np.uint16).view(np.float16)
+    got = biased - np.float16(1152.0)
+    np.testing.assert_array_equal(got.astype(np.float64), c.astype(np.float64))
+
+
+def test_u8_saturating_code():
+    p = np.concatenate([np.linspace(0.0, 300.0, 240001, dtype=np.float32),
+                        np.float32([255.49998, 255.5, 255.50002, 1e6])])
+    r = np.minimum(p + MAGIC, np.float32(12583167.0)) - MAGIC
+    want = np.clip(np.rint(p), 0, 255).astype(np.float32)
+    np.testing.assert_array_equal(r, want)
+
+
+def test_pv_partial_sums_are_exact():
+    # The largest |u8 x s8| product and the largest 16-term and 64-term sums.
+    assert 255 * 128 * 16 < 2 ** 24 and 255 * 128 * 64 < 2 ** 24
+    rng = np.random.default_rng(0)
+    p = rng.integers(0, 256, size=(1000, 16)).astype(np.float32)
+    v = rng.integers(-128, 128, size=(1000, 16)).astype(np.float32)
+    exact = (p.astype(np.int64) * v.astype(np.int64)).sum(axis=1)
+    acc = np.zeros(1000, np.float32)
+    for j in range(16):                 # any order of fp32 adds gives the integer
+        acc = acc + p[:, j] * v[:, j]
+    np.testing.assert_array_equal(acc.astype(np.int64), exact)
+    # Every code is exact in fp16 (an fp16 integer needs <= 11 significant bits).
+    assert (np.arange(-128, 256).astype(np.float16).astype(np.int64) == np.arange(-128, 256)).all()
