@@ -808,7 +808,7 @@ class DiTBlockWorkload:
         self-attention of those query rows against all L keys and the
         cross-attention against the 512 text keys (LayerNorm, GELU and the
         per-block text K/V projection are under 0.1 % of the work)."""
-        rows = min(rows, 32)
+        rows = min(rows, self.cpu_rows_cap)
         d, H, D = self.cfg.dim, self.cfg.heads, self.cfg.head_dim
         x = torch.randn((rows, d))
         wqkv, wo, wcq, wco, wup, wdown = self.cpu_w
@@ -822,6 +822,8 @@ class DiTBlockWorkload:
         x = x + torch.nn.functional.gelu(x @ wup.t(), approximate="tanh") @ wdown.t()
         return x, float(rows)  # tokens
 
+    # Each sampled token attends to all 75600 keys: 32 tokens are ~0.1 s of CPU work.
+    cpu_rows_cap = 32
     cpu_sample_desc = ("tokens through the fp32 block path (all linears; self-attention "
                        "against all 75600 keys; cross-attention against 512 text keys)")
 
@@ -989,7 +991,7 @@ def cpu_baseline(wl, args) -> dict:
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     wl.prepare_cpu()
-    rows = args.cpu_rows
+    rows = min(args.cpu_rows, getattr(wl, "cpu_rows_cap", args.cpu_rows))
     wl.cpu_reference_step(min(rows, 16))  # warm-up
     # About 10 s of CPU work: repeat the row sample until the budget is used.
     t0 = time.perf_counter()
@@ -1014,7 +1016,7 @@ def run_reference(args, world, rank, local):
     wl.prepare_cpu()
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    rows = args.cpu_rows
+    rows = min(args.cpu_rows, getattr(wl, "cpu_rows_cap", args.cpu_rows))
     for _ in range(args.warmup):
         wl.cpu_reference_step(min(rows, 16))
     times, total_ops = [], 0.0

@@ -517,6 +517,22 @@ void launch_staged_t(const void* input, int rows, int k, void* rotated, float* p
 
 }  // namespace
 
+// The kernels move 16 bytes per load/store (input, codes, rotated scratch)
+// and 4 bytes per scale or partial absmax; a sub-allocated pointer off those
+// boundaries would be a misaligned access on the device, so it is rejected
+// here, before anything is launched.
+void convrot_check_pointers(const void* input, const void* out, const float* scales, int staged,
+                            const void* rotated, const float* partial) {
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(input) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(out) % 16 == 0,
+             "ConvRot input and output must be 16-byte aligned");
+  TB_REQUIRE(reinterpret_cast<uintptr_t>(scales) % 4 == 0,
+             "ConvRot scales must be 4-byte aligned");
+  TB_REQUIRE(!staged || (reinterpret_cast<uintptr_t>(rotated) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(partial) % 4 == 0),
+             "staged ConvRot scratch must be 16-byte (rotated) and 4-byte (partial) aligned");
+}
+
 // Shared dispatcher for both forms.  dtype: TB_DTYPE_BF16 or TB_DTYPE_F16
 // (fp16 only for the staged form, as in the reference).
 void convrot_quantize_impl(const void* input, int dtype, int64_t rows64, int64_t k64, int act,
@@ -534,6 +550,7 @@ void convrot_quantize_impl(const void* input, int dtype, int64_t rows64, int64_t
   const int rows = static_cast<int>(rows64), k = static_cast<int>(k64);
   TB_REQUIRE(!staged || (rotated != nullptr && partial != nullptr),
              "staged ConvRot requires rotated and partial_absmax scratch");
+  convrot_check_pointers(input, out, scales, staged, rotated, partial);
   TB_REQUIRE(static_cast<size_t>(k) * 2 + 32 * kTbufStride * 4 + 64 <= 227 * 1024 || staged,
              "ConvRot row does not fit in shared memory; use the staged form");
 
@@ -581,22 +598,63 @@ constexpr size_t kNoAllocScratchBytes = 16u << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[64] = {};  // device address of the array, per device
+// Device address of the array per device ordinal, with the id of the context
+// it was looked up in.  A cudaDeviceReset (or any new primary context) loads
+// the module again, possibly at another address, and gets a new context id,
+// so a changed id triggers a fresh lookup.
+struct NoAllocSlot {
+  unsigned long long ctx_id;
+  void* addr;
+};
+NoAllocSlot g_noalloc_slot[64] = {};
 
-// Looks up the device address of the scratch array for the current device
-// (once per device).  The array's name is only a host-side stand-in; kernels
-// must be given this address.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Id of the calling thread's current context (0 when none is current yet).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  static CtxGetIdFn get_id = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<CtxGetIdFn>(p);
+  }();
+  if (get_current == nullptr || get_id == nullptr)
+    throw Error(TB_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Looks up the device address of the scratch array for the current device,
+// once per device and context.  The array's name is only a host-side
+// stand-in; kernels must be given this address.
 void* noalloc_scratch_for_current_device() {
   int dev = 0;
   TB_CUDA_CHECK(cudaGetDevice(&dev));
   TB_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range for the scratch table");
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_addr[dev] == nullptr) {
+  NoAllocSlot& slot = g_noalloc_slot[dev];
+  const unsigned long long id = current_context_id();
+  if (slot.addr == nullptr || id == 0 || id != slot.ctx_id) {
     void* ptr = nullptr;
-    TB_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
-    g_noalloc_addr[dev] = ptr;
+    TB_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));  // makes the context current
+    slot.addr = ptr;
+    slot.ctx_id = current_context_id();
   }
-  return g_noalloc_addr[dev];
+  return slot.addr;
 }
 
 }  // namespace
@@ -624,6 +682,7 @@ extern "C" int tb_swiglu_int8_convrot_quantize_noalloc(const void* input, int dt
                "problem too large for the allocation-free quantizer: rows * hidden * 2 + "
                "rows * hidden / 64 bytes must fit in its 16 MiB scratch; split the rows or use "
                "tb_swiglu_int8_convrot_quantize with caller-owned scratch");
+    tb::convrot_check_pointers(input, output, scales, 0, nullptr, nullptr);
     tb::require_sm100();
     unsigned char* scratch = static_cast<unsigned char*>(tb::noalloc_scratch_for_current_device());
     // Nothing in the scratch has to start at zero: the first pass writes every

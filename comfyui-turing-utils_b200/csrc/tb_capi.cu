@@ -170,6 +170,7 @@ int tb_bf16_int8_convrot_quantize(const void* input, int64_t rows, int64_t hidde
                    forced_threads == 1024,
                "forced_threads must be 0, 512, 768, or 1024");
     check_rowbuffer_args(input, rows, hidden);
+    tb::convrot_check_pointers(input, output, scales, 0, nullptr, nullptr);
     tb::require_sm100();
     tb::convrot_quantize_impl(input, TB_DTYPE_BF16, rows, hidden, swiglu ? 1 : 0, 0, 0, nullptr,
                               nullptr, output, scales, static_cast<cudaStream_t>(stream));
@@ -180,6 +181,7 @@ int tb_bf16_int4_convrot_quantize(const void* input, int64_t rows, int64_t hidde
                                   int8_t* output, float* scales, tb_stream_t stream) {
   return guarded([&] {
     check_rowbuffer_args(input, rows, hidden);
+    tb::convrot_check_pointers(input, output, scales, 0, nullptr, nullptr);
     tb::require_sm100();
     tb::convrot_quantize_impl(input, TB_DTYPE_BF16, rows, hidden, swiglu ? 1 : 0, 1, 0, nullptr,
                               nullptr, output, scales, static_cast<cudaStream_t>(stream));
@@ -190,6 +192,7 @@ int tb_bf16_gelu_int8_convrot_quantize(const void* input, int64_t rows, int64_t 
                                        int8_t* output, float* scales, tb_stream_t stream) {
   return guarded([&] {
     check_rowbuffer_args(input, rows, hidden);
+    tb::convrot_check_pointers(input, output, scales, 0, nullptr, nullptr);
     tb::require_sm100();
     tb::convrot_quantize_impl(input, TB_DTYPE_BF16, rows, hidden, 2, 0, 0, nullptr, nullptr,
                               output, scales, static_cast<cudaStream_t>(stream));
@@ -200,6 +203,7 @@ int tb_bf16_gelu_int4_convrot_quantize(const void* input, int64_t rows, int64_t 
                                        int8_t* output, float* scales, tb_stream_t stream) {
   return guarded([&] {
     check_rowbuffer_args(input, rows, hidden);
+    tb::convrot_check_pointers(input, output, scales, 0, nullptr, nullptr);
     tb::require_sm100();
     tb::convrot_quantize_impl(input, TB_DTYPE_BF16, rows, hidden, 2, 1, 0, nullptr, nullptr,
                               output, scales, static_cast<cudaStream_t>(stream));
@@ -218,6 +222,9 @@ static int staged_entry(const void* input, int dtype, int64_t rows, int64_t hidd
                "activated width must be positive and divisible by 256");
     TB_REQUIRE(rows <= INT32_MAX && hidden <= INT32_MAX,
                "staged ConvRot dimensions exceed the CUDA kernel range");
+    TB_REQUIRE(rotated != nullptr && partial != nullptr,
+               "staged ConvRot requires rotated and partial_absmax scratch");
+    tb::convrot_check_pointers(input, output, scales, 1, rotated, partial);
     tb::require_sm100();
     tb::convrot_quantize_impl(input, dtype, rows, hidden, act, int4, 1, rotated, partial, output,
                               scales, static_cast<cudaStream_t>(stream));

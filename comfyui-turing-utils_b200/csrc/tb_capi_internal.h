@@ -107,6 +107,8 @@ void qk_anchor_launch(const void* key, const void* key_norm, const void* freqs,
 void v_quant_launch(const void* v, int dtype, uint16_t* codes_f16, int8_t* codes_cm, float* scale,
                     int64_t B, int64_t H, int64_t L, int64_t D, int64_t Lpad, int64_t sb,
                     int64_t sh, int64_t sl, cudaStream_t stream);
+void convrot_check_pointers(const void* input, const void* out, const float* scales, int staged,
+                            const void* rotated, const float* partial);
 void convrot_quantize_impl(const void* input, int dtype, int64_t rows, int64_t k, int act,
                            int int4, int staged, void* rotated, float* partial, int8_t* out,
                            float* scales, cudaStream_t stream);

@@ -65,6 +65,12 @@ TB_API int tb_device_error(int *code_out);
 
 /* ------------------------------------------------ ConvRot quantizers ---- */
 
+/* Alignment (every ConvRot entry below, the allocation-free one included):
+ * input, output and the staged form's rotated scratch must be 16-byte
+ * aligned, scales and partial_absmax 4-byte aligned (the kernels move 16
+ * bytes per access).  Other pointers are rejected with TB_ERR_INVALID before
+ * anything is launched. */
+
 /* BF16 row-buffer ConvRot INT8 quantizer: input bf16 [rows, swiglu ? 2*hidden :
  * hidden], output int8 [rows, hidden], scales fp32 [rows].  forced_threads is
  * validated (0/512/768/1024) for signature parity; the kernel sizes its own
@@ -113,8 +119,10 @@ TB_API int tb_gelu_int4_convrot_quantize(const void *input, int dtype, int64_t r
  * exits.  Limit: rows * hidden * 2 (rounded up to 256) + rows * hidden / 64
  * bytes <= 16 MiB; larger problems are rejected with TB_ERR_INVALID.  The first
  * call on each device looks up the array's device address; make that first
- * call before any stream capture.  All calls share the one array, so calls
- * that overlap on the GPU (different streams without ordering) race on it.
+ * call before any stream capture (a new context on the device, e.g. after
+ * cudaDeviceReset, repeats the lookup).  All calls share the one array, so
+ * calls that overlap on the GPU (different streams without ordering) race on
+ * it.  Alignment as for the other ConvRot entries.
  * No counterpart in the reference. */
 TB_API int tb_swiglu_int8_convrot_quantize_noalloc(const void *input, int dtype, int64_t rows,
                                                    int64_t hidden, int8_t *output, float *scales,

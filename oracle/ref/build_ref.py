@@ -23,7 +23,9 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE.parent / "_ref"
-REF = Path(os.environ.get("TB_REFERENCE_ROOT", "/root/reference"))
+# The reference checkout: TB_REFERENCE_ROOT, else a `reference` directory
+# beside this repository.
+REF = Path(os.environ.get("TB_REFERENCE_ROOT", Path(__file__).resolve().parents[3] / "reference"))
 CSRC = REF / "kernel" / "csrc"
 
 COMMON = ["-DENABLE_BF16=1", "-std=c++17", "-O3", "--expt-relaxed-constexpr",

@@ -17,6 +17,7 @@ import base64
 import importlib.util
 import json
 import struct
+import os
 import sys
 import tempfile
 import types
@@ -224,4 +225,7 @@ def main(root: Path) -> None:
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference"))
+    # The reference checkout: argv[1], else TB_REFERENCE_ROOT, else a
+    # `reference` directory beside this repository.
+    default = os.environ.get("TB_REFERENCE_ROOT", Path(__file__).resolve().parents[3] / "reference")
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else Path(default))

@@ -83,6 +83,33 @@ def test_invalid_arguments_are_rejected_with_messages():
     assert L.last_error() == "output_columns must be positive and no larger than the accumulator width"
 
 
+def test_convrot_entries_reject_misaligned_pointers():
+    """A C host that sub-allocates its own VRAM may pass pointers off the
+    16-byte boundary the ConvRot kernels' vector loads and stores need; every
+    ConvRot entry rejects them before launching anything."""
+    L = _lib()
+    lib = L.load()
+    good = ctypes.c_void_p(4096)   # never dereferenced: validation fails first
+    odd = ctypes.c_void_p(4096 + 8)
+    st = lib.tb_bf16_int8_convrot_quantize(odd, 4, 256, 0, 0, good, good, None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "ConvRot input and output must be 16-byte aligned"
+    st = lib.tb_bf16_gelu_int4_convrot_quantize(good, 4, 256, odd, good, None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "ConvRot input and output must be 16-byte aligned"
+    st = lib.tb_bf16_int4_convrot_quantize(good, 4, 256, 0, good, ctypes.c_void_p(4098), None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "ConvRot scales must be 4-byte aligned"
+    st = lib.tb_swiglu_int8_convrot_quantize(good, L.TB_DTYPE_BF16, 4, 256, odd, good, good,
+                                             good, None)
+    assert st == L.TB_ERR_INVALID
+    assert "scratch must be 16-byte" in L.last_error()
+    st = lib.tb_swiglu_int8_convrot_quantize_noalloc(odd, L.TB_DTYPE_F16, 4, 256, good, good,
+                                                     None)
+    assert st == L.TB_ERR_INVALID
+    assert L.last_error() == "ConvRot input and output must be 16-byte aligned"
+
+
 def test_python_binding_raises_runtime_error():
     import torch
 

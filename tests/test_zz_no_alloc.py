@@ -54,9 +54,40 @@ def test_noalloc_matches_allocating_entry_point_twice(dtype):
     assert _lib.device_error() == 0
 
 
+# The largest problem at hidden 5120 that fits the 16 MiB scratch:
+# rows * 5120 * 2 rotated bytes (already a multiple of 256) + rows * 80 bytes
+# of partial absmax = 10320 * rows <= 16 * 2**20, so 1625 rows (16,770,000
+# bytes); 1626 rows need 16,780,320 bytes.
+FULL_ROWS = 1625
+
+
+@pytest.mark.gpu
+def test_noalloc_fills_its_scratch_exactly():
+    """At the size limit the partial absmax ends within 7 KB of the array's
+    end: an off-by-one in where it starts would overflow the array or
+    overlap the rotated rows, and the codes would differ."""
+    hidden = 5120
+    assert FULL_ROWS * hidden * 2 + FULL_ROWS * hidden // 64 <= 16 << 20
+    assert (FULL_ROWS + 1) * hidden * 2 + (FULL_ROWS + 1) * hidden // 64 > 16 << 20
+    for seed in (21, 22):
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn((FULL_ROWS, 2 * hidden), generator=g).to(torch.bfloat16).cuda()
+        got_q, got_s = _noalloc(x, hidden)
+        want_q, want_s = _allocating(x, hidden)
+        torch.cuda.synchronize()
+        assert torch.equal(got_q, want_q)
+        assert torch.equal(got_s, want_s)
+    assert _lib.device_error() == 0
+
+
 def test_noalloc_rejects_problems_larger_than_its_scratch():
     fake = ctypes.c_void_p(16)  # never dereferenced: the size check fails first
     status = _lib.load().tb_swiglu_int8_convrot_quantize_noalloc(
         fake, _lib.TB_DTYPE_BF16, 4096, 5120, fake, fake, None)
+    assert status == _lib.TB_ERR_INVALID
+    assert "16 MiB" in _lib.last_error()
+    # One row more than the largest problem that fits.
+    status = _lib.load().tb_swiglu_int8_convrot_quantize_noalloc(
+        fake, _lib.TB_DTYPE_BF16, FULL_ROWS + 1, 5120, fake, fake, None)
     assert status == _lib.TB_ERR_INVALID
     assert "16 MiB" in _lib.last_error()
