@@ -252,7 +252,12 @@ class CodebookWorkload:
     config = {"workload": "codebook_w4a8_linear (BASELINE configs[2])", "m": 8192, "k": 5120,
               "n": 5120, "group_size": 128, "rotation": 256,
               "activation": "per-token int8 (ConvRot)",
-              "weight": "4-bit codebook indices, e4m3 group scales, fp32 channel scales"}
+              "weight": "4-bit codebook indices, e4m3 group scales, fp32 channel scales",
+              "zero_points": "not built; parity unpinned: the config's asymmetric per-group "
+                             "zero points need a correction term, which the reference's Turing "
+                             "fast path rejects (dispatch.py:690-702, correction is None) and "
+                             "hands to comfy-kitchen (absent); measured on the symmetric "
+                             "codebook layout the reference's kernel takes"}
 
     def __init__(self, device, seed):
         import comfyui_turing_utils_kernel as kernel
@@ -339,7 +344,12 @@ class W4A4FFNWorkload:
     config = {"workload": "w4a4_convrot_ffn (BASELINE configs[3])", "m": 32760, "dim": 5120,
               "ffn": 13824, "rotation": 256, "activation": "per-token int4 (ConvRot)",
               "weight": "int4 per-channel", "between": "GELU-tanh fused into the down "
-              "projection's INT4 quantizer"}
+              "projection's INT4 quantizer",
+              "group_scales": "not built; parity unpinned: the config's group-64 fp16 scales "
+                              "are only validated by the reference's route (dispatch.py:746-806 "
+                              "requires quant_group_size == 64, then uses per-token activation "
+                              "and per-channel weight scales); measured on that layout, with the "
+                              "W4A4 GEMM pinned to the restated formula (comfy-kitchen absent)"}
 
     def __init__(self, device, seed):
         import comfyui_turing_utils_kernel as kernel
@@ -666,14 +676,23 @@ class DiTBlockWorkload:
     dominant = "sage_attn"
 
     def __init__(self, device, world=1, rank=0, tokens=None, cpu_only=False, use_graph=True,
-                 max_chunks=4):
+                 max_chunks=4, parallel="a2a"):
         from comfyui_turing_utils_kernel import dit_block as db
 
         self.db = db
         self.cfg = db.BlockConfig()
         self.L, self.Lc = tokens or 75600, 512
         self.world, self.rank = world, rank
-        self.plan = db.shard_plan(self.cfg, world, rank)
+        # "a2a": token shards for the linears, head shards for self-attention,
+        # two all-to-alls per block (full weights on every rank); "tp":
+        # Megatron tensor + sequence parallel.  One rank: the same block.
+        self.parallel = parallel if world > 1 else "a2a"
+        a2a = self.parallel == "a2a"
+        self.plan = db.shard_plan(self.cfg, 1 if a2a else world, 0 if a2a else rank)
+        self.nattn = self.cfg.heads // world if a2a else self.plan.nattn
+        # The committed traffic figure is for all 40 heads at L = 75600; a
+        # launch's bytes are proportional to its heads.
+        self.traffic_scale = self.nattn / self.cfg.heads if self.L == 75600 else None
         self.ops = db.block_ops(self.cfg, self.L, self.Lc)  # whole block, all ranks
         self.work = float(self.L)                             # tokens per step
         self.config = {"workload": "Wan2.1-14B DiT block (BASELINE configs[4])",
@@ -687,19 +706,26 @@ class DiTBlockWorkload:
         import torch.distributed as tdist
 
         self.weights = db.make_weights(self.cfg, self.plan, seed=0, device=device)
-        g = torch.Generator(device=device).manual_seed(1)
-        x = torch.randn((self.L, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
-        # Sequence parallel: each rank holds (and is timed on) its own tokens.
-        rows = db.local_rows(self.L, world, rank, db.token_chunks(self.L, world))
-        self.x = x[rows.to(device)].contiguous()
+        x = self.full_x(device)
+        # Each rank holds (and is timed on) its own tokens.
+        self.seq = None
+        if a2a:
+            if world > 1:
+                self.seq = db.SeqShards.make(self.L, world, rank, tdist.group.WORLD)
+            t0, t1 = self.seq.bounds[rank] if self.seq else (0, self.L)
+            self.rows = torch.arange(t0, t1)
+        else:
+            self.rows = db.local_rows(self.L, world, rank, db.token_chunks(self.L, world))
+        self.x = x[self.rows.to(device)].contiguous()
         del x
+        g = torch.Generator(device=device).manual_seed(3)
         self.ctx = torch.randn((self.Lc, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
         self.freqs = db.rope_freqs(self.L, self.cfg.head_dim, seed=2, device=device)
         self.kops = db.KernelOps()
         self.block = db.DiTBlock(self.cfg, self.weights, self.plan, self.kops,
-                                 group=tdist.group.WORLD if world > 1 else None,
-                                 max_chunks=max_chunks)
-        self.config["token_chunks"] = db.token_chunks(self.L, world, max_chunks)
+                                 group=tdist.group.WORLD if world > 1 and not a2a else None,
+                                 max_chunks=max_chunks, seq=self.seq)
+        self.config["token_chunks"] = 1 if a2a else db.token_chunks(self.L, world, max_chunks)
         self.host = [t.cpu().pin_memory() for t in (self.x, self.ctx)]
         self.out_host = torch.empty_like(self.host[0]).pin_memory()
         self.h2d_bytes = sum(t.numel() * 2 for t in self.host)
@@ -710,6 +736,53 @@ class DiTBlockWorkload:
         self.graph = None
         if use_graph:
             self._capture()
+
+    def full_x(self, device):
+        """All L tokens of the block input (seeded; every rank makes the same)."""
+        g = torch.Generator(device=device).manual_seed(1)
+        return torch.randn((self.L, self.cfg.dim), generator=g, device=device).to(torch.bfloat16)
+
+    def parity(self, out, samples=256):
+        """Multi-GPU numerics on a seeded sample of output tokens: each rank
+        contributes the sampled rows it owns, rank 0 compares them (as the
+        residual branches' sum, out - x) with the fp32 reference block at
+        one rank (dit_block.reference_rows: dequantized weights, unquantized
+        activations) and, when it holds the full weights (the all-to-all
+        layout), with its own one-GPU kernel block, bit for bit."""
+        import torch.distributed as tdist
+
+        db, dev = self.db, self.x.device
+        idx = torch.randperm(self.L, generator=torch.Generator().manual_seed(7))[:samples]
+        idx = idx.sort().values
+        pos = torch.full((self.L,), -1, dtype=torch.long)
+        pos[self.rows] = torch.arange(self.rows.numel())
+        mine = pos[idx] >= 0
+        rows = torch.zeros((idx.numel(), self.cfg.dim), dtype=torch.float32, device=dev)
+        rows[mine.to(dev)] = out[pos[idx][mine].to(dev)].float()
+        if self.world > 1:
+            tdist.all_reduce(rows)   # each sampled row is owned by exactly one rank
+        if self.rank != 0:
+            return None
+        x = self.full_x(dev)
+        full_w = self.weights if self.plan.world == 1 else db.make_weights(
+            self.cfg, db.shard_plan(self.cfg, 1, 0), seed=0, device=dev)
+        ref = db.reference_rows(self.cfg, full_w, x, self.ctx, self.freqs, idx.to(dev))
+        xi = x[idx.to(dev)].float()
+        d_out, d_ref = rows - xi, ref - xi
+        res = {"sample_tokens": int(idx.numel()),
+               "vs_fp32_reference": {
+                   "rel_l2": round(float((d_out - d_ref).norm() / d_ref.norm()), 6),
+                   "cos": round(float(torch.nn.functional.cosine_similarity(
+                       d_out.flatten(), d_ref.flatten(), dim=0)), 6),
+                   "on": "out - x (the three residual branches)",
+                   "bound": "rel_l2 <= 3e-2, cos >= 0.999 (tests/test_gpu_dit_block.py)"}}
+        if self.world > 1 and self.plan.world == 1:
+            one = db.DiTBlock(self.cfg, self.weights, self.plan, db.KernelOps()).forward(
+                x, self.ctx, self.freqs)[idx.to(dev)].float()
+            res["vs_one_gpu_kernel_block"] = {
+                "identical_tokens": int((one == rows).all(dim=1).sum()),
+                "max_abs_diff": float((one - rows).abs().max())}
+        return res
 
     def _capture(self):
         """Capture one block forward (kernels and NCCL collectives) in a CUDA
@@ -744,6 +817,13 @@ class DiTBlockWorkload:
         return self._dom
 
     def parallelism(self, world):
+        if world > 1 and self.parallel == "a2a":
+            return (f"all-to-all sequence parallel x{world}: token shards "
+                    f"{self.seq.sizes} (whole 64-token quantizer blocks) through every norm, "
+                    f"linear and the cross-attention with full weights on each rank; "
+                    f"{self.nattn} heads per rank for self-attention over all tokens; NCCL "
+                    "all-to-all of the INT8 Q/K codes, scales and bf16 V to the head owners "
+                    "and of the attention output back")
         return (f"tensor + sequence parallel x{world}: heads {list(self.plan.heads)}, FFN "
                 f"columns {list(self.plan.ffn)}; each rank owns {self.x.size(0)} tokens; NCCL "
                 "all-gather of the INT8 activations before Q/K/V, cross-Q and FFN-up, "
@@ -785,9 +865,9 @@ class DiTBlockWorkload:
         # The timed launch is the last self-attention launch of this rank's heads.
         a0, a1 = self.db.attention_launches(self.L)[-1]
         rows = a1 - a0
-        ops = 4.0 * self.plan.nattn * rows * self.L * self.cfg.head_dim
+        ops = 4.0 * self.nattn * rows * self.L * self.cfg.head_dim
         achieved = ops / (dom_ms * 1e-3) / 1e12
-        return {"kernel": f"sage_attn ({self.plan.nattn} heads x {rows} query rows x {self.L} keys)",
+        return {"kernel": f"sage_attn ({self.nattn} heads x {rows} query rows x {self.L} keys)",
                 "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": round(int8_peak, 1), "unit": "TOPS",
                 "frac": round(achieved / int8_peak, 4),
@@ -839,7 +919,8 @@ def make_workload(args, device, seed, world=1, rank=0):
         return WORKLOADS[args.workload](device, seed, heads=args.heads)
     if args.workload == "dit_block":
         return DiTBlockWorkload(device, world, rank, tokens=args.tokens,
-                                use_graph=not args.no_graph, max_chunks=args.chunks)
+                                use_graph=not args.no_graph, max_chunks=args.chunks,
+                                parallel=args.parallel)
     return WORKLOADS[args.workload](device, seed)
 
 
@@ -943,11 +1024,21 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    parity = None
+    if hasattr(wl, "parity") and not args.no_parity:
+        out = wl.step()
+        torch.cuda.synchronize()
+        parity = wl.parity(out)
+        barrier(world)
     dev_err = _lib.device_error()
 
     peaks = load_peaks()
     roof = wl.roofline(dom_avg, peaks)
     roof["traffic"] = ncu_traffic(wl.dominant, wl.name)
+    if getattr(wl, "traffic_scale", 1) is None:
+        roof["traffic"] = None
+    elif roof["traffic"] is not None and hasattr(wl, "traffic_scale"):
+        roof["traffic"] = round(roof["traffic"] * wl.traffic_scale)
     if hasattr(wl, "aux_roofline"):
         pro = [ev[0].elapsed_time(ev[1]) for ev in events]
         roof.update(wl.aux_roofline(sum(pro) / len(pro), peaks))
@@ -981,6 +1072,7 @@ def run_ours(args, world, rank, local):
         **({"block_tops": round(wl.ops / (ms * 1e-3) / 1e12, 1)} if wl.name == "dit_block" else {}),
         "clocks": dict(sampler.summary(), region="timed+soak" if soak else "timed"),
         "device_error": dev_err,
+        **({"parity": parity} if parity is not None else {}),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(wl, args)
@@ -1059,6 +1151,11 @@ def main():
                     help="dit_block: launch the block eagerly instead of replaying a CUDA graph")
     ap.add_argument("--tokens", type=int, default=None,
                     help="dit_block video tokens (default: the config's 75600)")
+    ap.add_argument("--parallel", default="a2a", choices=["a2a", "tp"],
+                    help="dit_block on several GPUs: all-to-all sequence parallel (token "
+                         "shards, head-sharded self-attention) or Megatron tensor parallel")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="dit_block: skip the sampled-token check against the fp32 reference")
     ap.add_argument("--heads", type=int, default=None,
                     help="attention heads (default: the config's 40); smaller cases for profiling")
     args = ap.parse_args()

@@ -44,6 +44,8 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from .profiling import CUDA_PHASE_PROFILER as PROFILER
+
 GROUP = 256  # ConvRot rotation block
 
 
@@ -448,6 +450,44 @@ def local_rows(L: int, world: int, rank: int, chunks: int) -> torch.Tensor:
                                    c * (L // chunks) + (rank + 1) * piece) for c in range(chunks)])
 
 
+def token_shards(L: int, world: int, block: int = 64) -> list[tuple[int, int]]:
+    """Contiguous token ranges of the all-to-all layout, in rank order: whole
+    64-token blocks (the K quantizer's tile and four Q warp tiles, so every
+    rank's Q/K codes and scales are the one-rank ones) dealt as evenly as
+    possible, larger shares first; the last range ends at L.  L = 75600 on 8
+    ranks: 6 x 9472, 9408, 9360 tokens."""
+    blocks = (L + block - 1) // block
+    if blocks < world:
+        raise ValueError(f"{L} tokens give fewer 64-token blocks than {world} ranks")
+    bounds, t = [], 0
+    for share in split_units(blocks, world):
+        bounds.append((t, min(t + share * block, L)))
+        t = bounds[-1][1]
+    return bounds
+
+
+@dataclasses.dataclass(frozen=True)
+class SeqShards:
+    """All-to-all sequence parallelism: rank `rank` of `world` owns tokens
+    bounds[rank] for every norm, linear and the cross-attention (full
+    weights on every rank), and heads [rank * H / world, (rank + 1) * H /
+    world) of the self-attention over all tokens; two all-to-alls per block
+    move the INT8 Q/K codes, their scales and V to the head owners and the
+    attention output back to the token owners."""
+    world: int
+    rank: int
+    bounds: tuple[tuple[int, int], ...]
+    group: object = None
+
+    @staticmethod
+    def make(L: int, world: int, rank: int, group=None) -> "SeqShards":
+        return SeqShards(world, rank, tuple(token_shards(L, world)), group)
+
+    @property
+    def sizes(self) -> list[int]:
+        return [b - a for a, b in self.bounds]
+
+
 class DiTBlock:
     """One Wan2.1-style block on one tensor-parallel rank.
 
@@ -468,12 +508,25 @@ class DiTBlock:
     attention and the FFN are independent per token and run per chunk.
     `group` is the process group (None: one rank); `attn_split` overrides the
     query row at which self-attention splits (tests).
+
+    With `seq` (SeqShards; `plan` is then the one-rank plan and `weights`
+    the full weights) the block runs all-to-all sequence parallel instead:
+    this rank's tokens go through every norm, linear and the cross-attention
+    as on one GPU, and the self-attention of its heads over all tokens sits
+    between two all-to-alls (`_heads_exchange`, `_tokens_exchange`).  Every
+    output row is then the one-rank block's row bit for bit.
     """
 
     def __init__(self, cfg: BlockConfig, weights: BlockWeights, plan: ShardPlan, ops,
-                 group=None, max_chunks: int = 4, attn_split: Optional[int] = None):
+                 group=None, max_chunks: int = 4, attn_split: Optional[int] = None,
+                 seq: Optional[SeqShards] = None):
         self.cfg, self.w, self.plan, self.ops, self.group = cfg, weights, plan, ops, group
-        self.max_chunks, self.attn_split = max_chunks, attn_split
+        self.max_chunks, self.attn_split, self.seq = max_chunks, attn_split, seq
+        if seq is not None:
+            if plan.world != 1:
+                raise ValueError("all-to-all sequence parallelism takes the one-rank plan")
+            if cfg.heads % seq.world:
+                raise ValueError(f"{cfg.heads} heads do not split evenly over {seq.world} ranks")
 
     # ----- collectives (identity on one rank)
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
@@ -536,6 +589,72 @@ class DiTBlock:
             out[:, (h - p.head0) * D:(h - p.head0) * D + buf.size(1)] = buf
         return out
 
+    def _heads_exchange(self, state):
+        """All-to-all of the prepared self-attention operands of this rank's
+        tokens (all heads) -> those of this rank's heads (all tokens): the
+        INT8 Q/K codes, their per-tile scales and V (KernelOps), or the fp32
+        Q/K/V (TorchOps).  Chunks are sent in token-shard order, so what
+        arrives is already in token order."""
+        seq, D = self.seq, self.cfg.head_dim
+        W, sizes, me = seq.world, seq.sizes, seq.rank
+        nh, L, Lr = self.cfg.heads // W, sum(seq.sizes), seq.sizes[seq.rank]
+        works = []
+
+        def tokens_nhd(t):  # [Lr, H, D] (any strides, unit channel stride) -> [L, nh, D]
+            send = t.reshape(Lr, W, nh, D).permute(1, 0, 2, 3).contiguous()
+            recv = torch.empty((L, nh, D), dtype=t.dtype, device=t.device)
+            works.append(dist.all_to_all_single(recv, send, sizes, [Lr] * W, group=seq.group,
+                                                async_op=True))
+            return recv
+
+        def tokens_hnd(t):  # [H, Lr, D] -> flat pieces of [nh, L_src, D]
+            send = t.reshape(W, nh * Lr * D).contiguous()
+            recv = torch.empty((nh * L * D,), dtype=t.dtype, device=t.device)
+            works.append(dist.all_to_all_single(recv, send.view(-1),
+                                                [nh * n * D for n in sizes], [nh * Lr * D] * W,
+                                                group=seq.group, async_op=True))
+            return recv
+
+        def tiles(sc, per_block):  # [1, H, n_me] per-tile scales -> list of [nh, n_src] pieces
+            counts = [(n + 63) // 64 * per_block for n in sizes]
+            assert sc.size(-1) == counts[me]
+            recv = torch.empty((nh * sum(counts),), dtype=sc.dtype, device=sc.device)
+            works.append(dist.all_to_all_single(recv, sc.contiguous().view(-1),
+                                                [nh * n for n in counts], [nh * counts[me]] * W,
+                                                group=seq.group, async_op=True))
+            return recv, counts
+
+        if isinstance(self.ops, KernelOps):
+            q8, qs, k8, ks, v = state
+            q_full, k_full, v_full = tokens_nhd(q8[0]), tokens_nhd(k8[0]), tokens_nhd(v[0])
+            (qr, qc), (kr, kc) = tiles(qs, 4), tiles(ks, 1)
+            self._wait(works)
+
+            def join(recv, counts):
+                parts = recv.split([nh * n for n in counts])
+                return torch.cat([p.view(nh, n) for p, n in zip(parts, counts)], dim=1)[None]
+
+            return (q_full[None], join(qr, qc), k_full[None], join(kr, kc), v_full[None])
+        qf, kf, vf = state
+        out = [tokens_hnd(t) for t in (qf, kf, vf)]
+        self._wait(works)
+
+        def join_hnd(recv):
+            parts = recv.split([nh * n * D for n in sizes])
+            return torch.cat([p.view(nh, n, D) for p, n in zip(parts, sizes)], dim=1)
+
+        return tuple(join_hnd(r) for r in out)
+
+    def _tokens_exchange(self, att: torch.Tensor) -> torch.Tensor:
+        """All-to-all of the self-attention output [L, nh * D] of this rank's
+        heads -> [Lr, H * D] of this rank's tokens (heads in rank order)."""
+        seq = self.seq
+        W, sizes, Lr = seq.world, seq.sizes, seq.sizes[seq.rank]
+        recv = torch.empty((W, Lr, att.size(1)), dtype=att.dtype, device=att.device)
+        dist.all_to_all_single(recv.view(W * Lr, -1), att.contiguous(), [Lr] * W, sizes,
+                               group=seq.group)
+        return recv.permute(1, 0, 2).reshape(Lr, W * att.size(1))
+
     def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
         """Row RRMS over the heads of every rank (None: one rank, the fused
         prologue computes it)."""
@@ -545,55 +664,90 @@ class DiTBlock:
         return torch.rsqrt(s / self.cfg.dim + self.cfg.eps)
 
     def forward(self, x_local: torch.Tensor, ctx: torch.Tensor, freqs: torch.Tensor,
-                L: Optional[int] = None) -> torch.Tensor:
-        """x_local: this rank's tokens of x (`local_rows`; all of x on one
-        rank), ctx [Lc, dim] (every rank), freqs [1, L, 1, head_dim/2, 2, 2].
-        Returns this rank's tokens of the block output."""
+                L: Optional[int] = None, branches=("self", "cross", "ffn"),
+                trace: Optional[list] = None) -> torch.Tensor:
+        """x_local: this rank's tokens of x (`local_rows`, or `seq.bounds`
+        with SeqShards; all of x on one rank), ctx [Lc, dim] (every rank),
+        freqs [1, L, 1, head_dim/2, 2, 2] (all tokens).  Returns this rank's
+        tokens of the block output.  `branches` names the residual branches
+        added to x (all by default; tests hold each branch alone to a bound)
+        and `trace`, when given, receives (branch, chunk, branch output)
+        before each residual add."""
         c, w, ops, N = self.cfg, self.w, self.ops, self.plan.world
         D, nh = c.head_dim, self.plan.nattn
-        L = x_local.size(0) * N if L is None else L
-        C = token_chunks(L, N, self.max_chunks)
-        rows, piece = L // C, L // (C * N)
+        seq = self.seq
+        if seq is None:
+            L = x_local.size(0) * N if L is None else L
+            Ll, fr = L, freqs      # tokens whose Q/K/V this rank computes
+        else:
+            L = seq.bounds[-1][1]
+            t0, t1 = seq.bounds[seq.rank]
+            if x_local.size(0) != t1 - t0:
+                raise ValueError("x_local must hold this rank's token shard")
+            Ll, fr = t1 - t0, freqs[:, t0:t1]
+        C = token_chunks(Ll, N, self.max_chunks)
+        rows, piece = Ll // C, Ll // (C * N)
         Lc = ctx.size(0)
         m = w.modulation
         x = x_local.clone()
         xs = [x[i * piece:(i + 1) * piece] for i in range(C)]      # views of x
         full_dtype = torch.bfloat16 if isinstance(ops, KernelOps) else torch.float32
 
+        def residual(name, i, y, gate):
+            if trace is not None:
+                trace.append((name, i, y.clone()))
+            if name in branches:
+                ops.gated_add_(xs[i], y, gate)
+
         # Q/K/V of the whole sequence: per chunk LayerNorm+AdaLN, quantize,
         # all-gather, GEMM into the chunk's rows.
-        gathered = [self._gather(ops.quantize(ops.ln_adaln(xi, m[1], m[0], c.eps))) for xi in xs]
-        qkv = torch.empty((L, 3 * nh * D), dtype=full_dtype, device=x.device)
-        for i, (act, works) in enumerate(gathered):
-            self._wait(works)
-            ops.linear_q(act, w.qkv, out=qkv[i * rows:(i + 1) * rows])
-        del gathered
-        qkv = qkv.view(L, 3, nh, D)
+        with PROFILER.phase("dit.norm_qkv"):
+            gathered = [self._gather(ops.quantize(ops.ln_adaln(xi, m[1], m[0], c.eps)))
+                        for xi in xs]
+            qkv = torch.empty((Ll, 3 * nh * D), dtype=full_dtype, device=x.device)
+            for i, (act, works) in enumerate(gathered):
+                self._wait(works)
+                ops.linear_q(act, w.qkv, out=qkv[i * rows:(i + 1) * rows])
+            del gathered
+        qkv = qkv.view(Ll, 3, nh, D)
         q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
-        state = ops.qk_prepare(q, k, v, w.norm_q, w.norm_k, freqs, D, self._rrms(q),
-                               self._rrms(k), c.eps)
+        with PROFILER.phase("dit.qk_prologue"):
+            state = ops.qk_prepare(q, k, v, w.norm_q, w.norm_k, fr, D, self._rrms(q),
+                                   self._rrms(k), c.eps)
+        nha = nh                   # heads of this rank's self-attention
+        if seq is not None:
+            with PROFILER.phase("dit.heads_all_to_all"):
+                state = self._heads_exchange(state)
+            nha = c.heads // seq.world
         # Self-attention in wave-aligned launches; every chunk whose rows are
         # done goes through O and starts its reduce-scatter while the next
-        # attention launch runs.
-        att = torch.empty((L, nh * D), dtype=full_dtype, device=x.device)
+        # attention launch runs (tensor parallel).  All-to-all: the output
+        # returns to the token owners after the last launch.
+        att = torch.empty((L, nha * D), dtype=full_dtype, device=x.device)
         pending, done = [], 0
-        for a0, a1 in attention_launches(L, split=self.attn_split):
-            ops.attend_rows(state, a0, a1, mark=a1 == L, out=att[a0:a1])
-            while done < C and (done + 1) * rows <= a1:
-                blk = att[done * rows:(done + 1) * rows]
-                pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(blk)),
-                                                          w.o)))
-                done += 1
+        with PROFILER.phase("dit.self_attention_o"):
+            for a0, a1 in attention_launches(L, split=self.attn_split):
+                ops.attend_rows(state, a0, a1, mark=a1 == L, out=att[a0:a1])
+                while seq is None and done < C and (done + 1) * rows <= a1:
+                    blk = att[done * rows:(done + 1) * rows]
+                    pending.append(self._scatter(
+                        ops.linear_q(ops.quantize(self._to_o_heads(blk)), w.o)))
+                    done += 1
+            if seq is not None:
+                pending.append(self._scatter(
+                    ops.linear_q(ops.quantize(self._tokens_exchange(att)), w.o)))
         del state, qkv, q, k, v, att
 
         # Cross-attention: the context's K/V once, then per chunk.
+        cross = PROFILER.phase("dit.cross_attention")
+        cross.__enter__()
         kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)
         k_rrms = self._rrms(kv[:, 0])
         gathered = []
         for i, (y, job) in enumerate(pending):
             if job is not None:
                 job[0].wait()
-            ops.gated_add_(xs[i], y, m[2])
+            residual("self", i, y, m[2])
             gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], w.cross_norm[1],
                                                                    w.cross_norm[0], c.eps))))
         # Q of every chunk first, so the cross-rank RMS of all chunks is one
@@ -613,13 +767,16 @@ class DiTBlock:
             att = ops.attend_rows(st, 0, rows)
             pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(att)), w.co)))
         del qcs
+        cross.__exit__(None, None, None)
 
         # Feed-forward per chunk.
+        ffn = PROFILER.phase("dit.ffn")
+        ffn.__enter__()
         gathered = []
         for i, (y, job) in enumerate(pending):
             if job is not None:
                 job[0].wait()
-            ops.gated_add_(xs[i], y, None)
+            residual("cross", i, y, None)
             gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], m[4], m[3], c.eps))))
         pending = []
         for i, (act, works) in enumerate(gathered):
@@ -629,7 +786,9 @@ class DiTBlock:
         for i, (y, job) in enumerate(pending):
             if job is not None:
                 job[0].wait()
-            ops.gated_add_(xs[i], y, m[5])
+            residual("ffn", i, y, m[5])
+        ffn.__exit__(None, None, None)
+        PROFILER.complete_attention((L, c.dim))
         return x
 
     def ops_count(self, L: int, Lc: int) -> float:
@@ -640,6 +799,57 @@ class DiTBlock:
             + 2 * 2 * L * d * f
         attn = 4 * H * L * L * D + 4 * H * L * Lc * D
         return float(lin + attn)
+
+
+@torch.no_grad()
+def reference_rows(cfg: BlockConfig, w: BlockWeights, x: torch.Tensor, ctx: torch.Tensor,
+                   freqs: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    """The fp32 reference block (TorchOps' arithmetic: dequantized weights,
+    unquantized activations) at token rows `idx` only, from one-rank weights
+    `w` and all tokens of x: K and V are computed for every token, Q and the
+    rest of the block for the sampled rows.  Equals
+    DiTBlock(cfg, w, plan, TorchOps()).forward(x, ctx, freqs)[idx] up to fp32
+    summation order; used to check multi-GPU outputs on a row sample."""
+    ops, m, eps = TorchOps(), w.modulation, cfg.eps
+    d, H, D = cfg.dim, cfg.heads, cfg.head_dim
+    x = x.float()
+    L, R = x.size(0), idx.numel()
+
+    def lin(a, layer, rows=None):
+        wt = ops._dense(layer) if rows is None else ops._dense(layer)[rows]
+        y = a @ wt.t()
+        if layer.bias is not None:
+            y = y + (layer.bias if rows is None else layer.bias[rows])
+        return y
+
+    def norm_rope(t, weight, f):  # t [n, H, D]; row RMSNorm over all heads, RoPE by f
+        rrms = torch.rsqrt(t.pow(2).sum(dim=(1, 2)) / d + eps)
+        n = t * rrms[:, None, None] * weight.float().view(1, H, D)
+        if f is not None:
+            pairs = n.view(n.size(0), H, D // 2, 2)
+            n = torch.einsum("lprc,lhpc->lhpr", f.float()[0, :, 0], pairs).reshape(n.shape)
+        return n
+
+    h = ops.ln_adaln(x, m[1], m[0], eps)
+    q = lin(h[idx], w.qkv, slice(0, d)).view(R, H, D)
+    k = lin(h, w.qkv, slice(d, 2 * d)).view(L, H, D)
+    v = lin(h, w.qkv, slice(2 * d, 3 * d)).view(L, H, D)
+    del h
+    q, k = norm_rope(q, w.norm_q, freqs[:, idx]), norm_rope(k, w.norm_k, freqs)
+    a = torch.nn.functional.scaled_dot_product_attention(q.transpose(0, 1), k.transpose(0, 1),
+                                                         v.transpose(0, 1))
+    del k, v
+    xr = x[idx] + lin(a.transpose(0, 1).reshape(R, d), w.o) * m[2].float()
+    hc = ops.ln_adaln(xr, w.cross_norm[1], w.cross_norm[0], eps)
+    qc = norm_rope(lin(hc, w.cq).view(R, H, D), w.cnorm_q, None)
+    kv = lin(ctx.float(), w.ckv).view(ctx.size(0), 2, H, D)
+    kc = norm_rope(kv[:, 0], w.cnorm_k, None)
+    a = torch.nn.functional.scaled_dot_product_attention(qc.transpose(0, 1), kc.transpose(0, 1),
+                                                         kv[:, 1].transpose(0, 1))
+    xr = xr + lin(a.transpose(0, 1).reshape(R, d), w.co)
+    hf = ops.ln_adaln(xr, m[4], m[3], eps)
+    u = torch.nn.functional.gelu(lin(hf, w.up), approximate="tanh")
+    return xr + lin(u, w.down) * m[5].float()
 
 
 def block_ops(cfg: BlockConfig, L: int, Lc: int) -> float:

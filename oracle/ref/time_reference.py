@@ -161,8 +161,31 @@ def linear(dev, Lib) -> None:
                                                        R.stream()), "int8 linear"))
     ours_ms = timed(lambda: _C.turing_int8_linear(xq, w, xs.view(M), w_s, bias))
     mine = _C.turing_int8_linear(xq, w, xs.view(M), w_s, bias)
+    torch.cuda.synchronize()
+    # Where the two outputs differ, which one the oracle's epilogue
+    # ((float(acc) * a_s) * w_s + bias, one bf16 rounding) agrees with, on
+    # 16 sampled rows.
+    import numpy as np
+
+    import oracle
+
+    differ = (mine != out)
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(3))[:16].numpy()
+    q_np = xq.cpu().numpy()
+    acc = oracle.int8_gemm_rows(q_np, w.cpu().numpy(), rows)
+    want = oracle.dequant_bf16(acc, xs.cpu().numpy()[rows], w_s.cpu().numpy(),
+                               bias.cpu().numpy())
+
+    def bits(t):
+        return t.cpu().view(torch.int16).numpy().view(np.uint16)[rows]
+
+    ulp = (mine.float() - out.float()).abs() / out.float().abs().clamp_min(1e-30)
     report("INT8 linear (turing_int8_linear)", ref_ms, ours_ms, 2.0 * M * N * K,
-           outputs_equal=bool(torch.equal(mine, out)))
+           outputs_equal=bool(torch.equal(mine, out)),
+           outputs_differing_frac=round(float(differ.float().mean()), 6),
+           max_rel_diff=float(ulp.max()),
+           ours_equal_oracle_rows=bool(np.array_equal(bits(mine), want)),
+           reference_equal_oracle_rows=bool(np.array_equal(bits(out), want)))
 
 
 def main() -> None:

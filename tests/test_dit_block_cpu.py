@@ -113,3 +113,132 @@ def test_tensor_parallel_block_equals_one_rank(tmp_path, world, moves):
     # scales over the shard's columns), so the two runs differ by weight
     # rounding only.
     assert rel < 0.02, rel
+
+
+def test_token_shards_are_whole_quantizer_blocks():
+    b = db.token_shards(75600, 8)
+    assert [t1 - t0 for t0, t1 in b] == [9472] * 6 + [9408, 9360]
+    assert b[0][0] == 0 and b[-1][1] == 75600
+    assert all(t0 % 64 == 0 for t0, _ in b) and all(b[i][1] == b[i + 1][0] for i in range(7))
+    assert db.token_shards(96, 2) == [(0, 64), (64, 96)]
+    assert db.token_shards(75600, 1) == [(0, 75600)]
+    with pytest.raises(ValueError):
+        db.token_shards(100, 4)
+
+
+def _a2a_out(world: int, rank: int, L: int, group=None):
+    """All-to-all sequence-parallel block (fp32 backend): this rank's tokens."""
+    cfg = SMALL
+    w = db.make_weights(cfg, db.shard_plan(cfg, 1, 0), seed=3)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn((L, cfg.dim), generator=g)
+    ctx = torch.randn((16, cfg.dim), generator=g)
+    freqs = db.rope_freqs(L, cfg.head_dim, seed=4, dtype=torch.float32)
+    seq = db.SeqShards.make(L, world, rank, group)
+    t0, t1 = seq.bounds[rank]
+    block = db.DiTBlock(cfg, w, db.shard_plan(cfg, 1, 0), db.TorchOps(), seq=seq)
+    return x, (t0, t1), block.forward(x[t0:t1], ctx, freqs)
+
+
+def _a2a_rank_main(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
+    sys.path.insert(0, str(ROOT / "comfyui-turing-utils_b200"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        _, bounds, out = _a2a_out(world, rank, L)
+        torch.save((bounds, out), Path(out_dir) / f"a2a{rank}.pt")
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("world,L", [(2, 96), (4, 200)])
+def test_all_to_all_block_equals_one_rank(tmp_path, world, L):
+    """Token shards for the linears, head shards for self-attention, two
+    all-to-alls: the same weights and arithmetic as one rank, so the rows
+    agree to fp32 summation order (uneven shards at L = 200: 64,64,64,8)."""
+    import torch.multiprocessing as mp
+
+    x, _, single = _block_out(1, 0, SMALL, L)
+    mp.start_processes(_a2a_rank_main, args=(world, _free_port(), str(tmp_path), L),
+                       nprocs=world, start_method="spawn", join=True)
+    full = torch.full_like(x, float("nan"))
+    for r in range(world):
+        (t0, t1), out = torch.load(tmp_path / f"a2a{r}.pt")
+        full[t0:t1] = out
+    assert not torch.isnan(full).any()
+    rel = ((full - x) - (single - x)).norm() / (single - x).norm()
+    assert rel < 1e-5, rel
+
+
+def test_branches_and_trace_one_rank():
+    """With one branch enabled only that residual is added; the trace holds
+    every branch output before its add."""
+    cfg = SMALL
+    plan = db.shard_plan(cfg, 1, 0)
+    w = db.make_weights(cfg, plan, seed=3)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn((64, cfg.dim), generator=g)
+    ctx = torch.randn((16, cfg.dim), generator=g)
+    freqs = db.rope_freqs(64, cfg.head_dim, seed=4, dtype=torch.float32)
+    block = db.DiTBlock(cfg, w, plan, db.TorchOps())
+    trace = []
+    out = block.forward(x, ctx, freqs, branches=("ffn",), trace=trace)
+    assert [t[0] for t in trace] == ["self", "cross", "ffn"]
+    y = trace[2][2]
+    assert torch.allclose(out, x + y * w.modulation[5].float(), atol=1e-5)
+
+
+def test_reference_rows_equal_fp32_block_rows():
+    cfg = SMALL
+    plan = db.shard_plan(cfg, 1, 0)
+    w = db.make_weights(cfg, plan, seed=3)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn((96, cfg.dim), generator=g)
+    ctx = torch.randn((16, cfg.dim), generator=g)
+    freqs = db.rope_freqs(96, cfg.head_dim, seed=4, dtype=torch.float32)
+    full = db.DiTBlock(cfg, w, plan, db.TorchOps()).forward(x, ctx, freqs)
+    idx = torch.tensor([0, 5, 17, 63, 64, 95])
+    rows = db.reference_rows(cfg, w, x, ctx, freqs, idx)
+    assert torch.allclose(rows, full[idx], rtol=1e-4, atol=1e-4), (rows - full[idx]).abs().max()
+
+
+def test_phase_profiler_window(monkeypatch, caplog):
+    """COMFYUI_TURING_UTILS_PROFILE_CALLS semantics (the plugin's
+    profiling.py:28-95): events per phase over the first N calls, one report,
+    then off; off by default."""
+    from comfyui_turing_utils_kernel import profiling
+
+    class FakeEvent:
+        clock = [0.0]
+
+        def record(self):
+            FakeEvent.clock[0] += 1.5
+            self.t = FakeEvent.clock[0]
+
+        def synchronize(self):
+            pass
+
+        def elapsed_time(self, other):
+            return other.t - self.t
+
+    assert not profiling.CudaPhaseProfiler(0).enabled
+    monkeypatch.setenv("COMFYUI_TURING_UTILS_PROFILE_CALLS", "2")
+    prof = profiling.CudaPhaseProfiler(profiling._profile_call_limit(), FakeEvent, nvtx=False)
+    monkeypatch.setattr(db, "PROFILER", prof)
+    cfg = SMALL
+    plan = db.shard_plan(cfg, 1, 0)
+    w = db.make_weights(cfg, plan, seed=3)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn((64, cfg.dim), generator=g)
+    ctx = torch.randn((16, cfg.dim), generator=g)
+    freqs = db.rope_freqs(64, cfg.head_dim, seed=4, dtype=torch.float32)
+    block = db.DiTBlock(cfg, w, plan, db.TorchOps())
+    with caplog.at_level("WARNING", logger="comfyui-turing-utils"):
+        for _ in range(3):
+            block.forward(x, ctx, freqs)
+    assert not prof.enabled and prof.calls == 2
+    assert set(prof.last_report) == {"dit.norm_qkv", "dit.qk_prologue", "dit.self_attention_o",
+                                     "dit.cross_attention", "dit.ffn"}
+    assert all(n == 2 for n, _ in prof.last_report.values())
+    assert sum("[Turing profile] attention_calls=2" in r.message for r in caplog.records) == 1

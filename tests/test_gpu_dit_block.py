@@ -13,8 +13,11 @@ import socket
 import sys
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
+
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -53,6 +56,79 @@ def test_block_matches_fp32_reference(cfg, L, Lc, split):
     ref = db.DiTBlock(cfg, w, plan, db.TorchOps()).forward(x.float(), ctx, freqs.float())
     rel, cos = _compare(out, ref, x)
     assert rel <= 3e-2 and cos >= 0.999, (rel, cos)
+    assert _lib.device_error() == 0
+
+
+class DequantOps(db.TorchOps):
+    """The block's dequantize-then-compute reference (the north star's
+    reference path, composed): every tensor the kernel path stores in bf16
+    is rounded to bf16, every activation the kernel path quantizes gets the
+    kernel's INT8 codes from the CPU oracle (ConvRot INT8 with and without
+    the fused tanh-GELU, the fused RMSNorm + RoPE Q/K prologue), and the
+    codes are dequantized and used in fp32 matmuls and fp32 attention."""
+
+    @staticmethod
+    def _bits(t):
+        return t.detach().to(torch.bfloat16).cpu().view(torch.int16).numpy().view(np.uint16)
+
+    def ln_adaln(self, x, scale, shift, eps):
+        return db.TorchOps.ln_adaln(x, scale, shift, eps).to(torch.bfloat16)
+
+    def _deq(self, codes, scales, device):
+        return torch.from_numpy(codes).to(device).float() * torch.from_numpy(scales).to(device)
+
+    def quantize(self, x):
+        return [self._deq(*oracle.convrot_quantize(self._bits(x)), x.device)]
+
+    def gelu_quantize(self, u):
+        return [self._deq(*oracle.convrot_quantize(self._bits(u), act="gelu"), u.device)]
+
+    def linear_q(self, act, layer, out=None):
+        y = act[0] @ (layer.weight.float() * layer.scale[:, None]).t()  # rotated basis
+        y = (y + layer.bias if layer.bias is not None else y).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+
+    def qk_prepare(self, q, k, v, qn, kn, freqs, rot_dim, q_rrms, k_rrms, eps):
+        def prep(t, norm, tile):
+            fb = None if not rot_dim else self._bits(freqs)
+            codes, sc = oracle.qk_rms_rope_int8(self._bits(t)[None], self._bits(norm), fb,
+                                                tile_tokens=tile, eps=eps, rot_dim=rot_dim,
+                                                layout="NHD", norm_scope="row")
+            c = torch.from_numpy(codes[0]).to(t.device).float().transpose(0, 1)  # [H, n, D]
+            s = torch.from_numpy(sc[0]).to(t.device).repeat_interleave(tile, dim=1)
+            return c * s[:, :t.size(0), None]
+        return prep(q, qn, 16), prep(k, kn, 64), v.float().transpose(0, 1)
+
+    def attend_rows(self, state, r0, r1, mark=False, out=None):
+        res = db.TorchOps.attend_rows(state, r0, r1).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+
+
+@pytest.mark.parametrize("L,Lc", [(1024, 512), (1000, 64)])
+def test_each_branch_within_north_star_bound_at_full_width(L, Lc):
+    """configs[4]'s width (dim 5120, 40 heads, FFN 13824): with no residual
+    adds every branch sees x, and each branch output (self-attention + O,
+    cross-attention + O, FFN up / GELU / down) of the kernel block is held
+    to the north-star bound against the dequantize-then-compute reference:
+    cosine >= 0.9995, relative L2 <= 1e-2."""
+    cfg = db.BlockConfig()
+    plan = db.shard_plan(cfg, 1, 0)
+    w = db.make_weights(cfg, plan, seed=3, device="cuda")
+    x, ctx, freqs = _inputs(cfg, L, Lc)
+    got, want = [], []
+    db.DiTBlock(cfg, w, plan, db.KernelOps()).forward(x, ctx, freqs, branches=(), trace=got)
+    db.DiTBlock(cfg, w, plan, DequantOps()).forward(x, ctx, freqs, branches=(), trace=want)
+    assert [t[0] for t in got] == [t[0] for t in want] == ["self", "cross", "ffn"]
+    for (name, _, yk), (_, _, yr) in zip(got, want):
+        met = oracle.metrics(yk.float().cpu(), yr.float().cpu())
+        assert met["cosine"] >= oracle.NORTH_STAR_COSINE, (name, met)
+        assert met["rel_l2"] <= oracle.NORTH_STAR_REL_L2, (name, met)
     assert _lib.device_error() == 0
 
 
@@ -102,3 +178,45 @@ def test_tensor_parallel_two_gpus(tmp_path):
     ref = db.DiTBlock(SMALL, w, plan, db.TorchOps()).forward(x.float(), ctx, freqs.float())
     rel, cos = _compare(full, ref, x)
     assert rel <= 3e-2 and cos >= 0.999, (rel, cos)
+
+
+def _a2a_rank(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
+    import datetime
+
+    sys.path.insert(0, str(ROOT / "comfyui-turing-utils_b200"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=120),
+                                         device_id=torch.device("cuda", rank))
+    try:
+        plan = db.shard_plan(SMALL, 1, 0)
+        w = db.make_weights(SMALL, plan, seed=3, device="cuda")
+        x, ctx, freqs = _inputs(SMALL, L, 40)
+        seq = db.SeqShards.make(L, world, rank, torch.distributed.group.WORLD)
+        t0, t1 = seq.bounds[rank]
+        out = db.DiTBlock(SMALL, w, plan, db.KernelOps(), seq=seq).forward(x[t0:t1], ctx, freqs)
+        torch.cuda.synchronize()
+        torch.save(((t0, t1), out.cpu()), Path(out_dir) / f"a2a{rank}.pt")
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("L", [300, 1000])
+def test_all_to_all_two_gpus_equals_one_gpu(tmp_path, L):
+    """Token shards of whole 64-token blocks (uneven at L = 300: 192 + 108)
+    through the linears, head shards through self-attention: every output
+    row equals the one-GPU block's bit for bit."""
+    import torch.multiprocessing as mp
+
+    mp.start_processes(_a2a_rank, args=(2, _free_port(), str(tmp_path), L), nprocs=2,
+                       start_method="spawn", join=True)
+    plan = db.shard_plan(SMALL, 1, 0)
+    w = db.make_weights(SMALL, plan, seed=3, device="cuda")
+    x, ctx, freqs = _inputs(SMALL, L, 40)
+    single = db.DiTBlock(SMALL, w, plan, db.KernelOps()).forward(x, ctx, freqs).cpu()
+    for r in range(2):
+        (t0, t1), out = torch.load(tmp_path / f"a2a{r}.pt")
+        assert torch.equal(out, single[t0:t1]), (r, (out.float() - single[t0:t1].float()).abs().max())
