@@ -784,6 +784,30 @@ class DiTBlockWorkload:
                 "max_abs_diff": float((one - rows).abs().max())}
         return res
 
+    def phases(self, calls: int):
+        """Per-phase device time of `calls` eager block forwards
+        (comfyui_turing_utils_kernel.profiling): ms per forward, max over
+        ranks (every rank runs the same forwards and collectives)."""
+        from comfyui_turing_utils_kernel import profiling
+
+        prof = profiling.CudaPhaseProfiler(calls)
+        saved, self.db.PROFILER = self.db.PROFILER, prof
+        try:
+            for _ in range(calls):
+                self.block.forward(self.x, self.ctx, self.freqs, L=self.L)
+            torch.cuda.synchronize()
+        finally:
+            self.db.PROFILER = saved
+        names = sorted(prof.last_report)
+        per = torch.tensor([prof.last_report[n][1] / calls for n in names], dtype=torch.float64,
+                           device=self.x.device)
+        if self.world > 1:
+            import torch.distributed as tdist
+
+            tdist.all_reduce(per, op=tdist.ReduceOp.MAX)
+        return {"eager_forwards": calls, "ms_per_forward_max_over_ranks":
+                {n: round(float(v), 4) for n, v in zip(names, per.tolist())}}
+
     def _capture(self):
         """Capture one block forward (kernels and NCCL collectives) in a CUDA
         graph; a step then replays it, without per-launch host work."""
@@ -1030,6 +1054,7 @@ def run_ours(args, world, rank, local):
         torch.cuda.synchronize()
         parity = wl.parity(out)
         barrier(world)
+    phases = wl.phases(args.phases) if args.phases and hasattr(wl, "phases") else None
     dev_err = _lib.device_error()
 
     peaks = load_peaks()
@@ -1073,6 +1098,7 @@ def run_ours(args, world, rank, local):
         "clocks": dict(sampler.summary(), region="timed+soak" if soak else "timed"),
         "device_error": dev_err,
         **({"parity": parity} if parity is not None else {}),
+        **({"phases": phases} if phases is not None else {}),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(wl, args)
@@ -1156,6 +1182,10 @@ def main():
                          "shards, head-sharded self-attention) or Megatron tensor parallel")
     ap.add_argument("--no-parity", action="store_true",
                     help="dit_block: skip the sampled-token check against the fp32 reference")
+    ap.add_argument("--phases", type=int, default=0,
+                    help="dit_block: after the timed region, time the block's phases (CUDA "
+                         "events on the compute stream, so a collective counts with its "
+                         "exposed time) over this many eager forwards; max over ranks")
     ap.add_argument("--heads", type=int, default=None,
                     help="attention heads (default: the config's 40); smaller cases for profiling")
     args = ap.parse_args()

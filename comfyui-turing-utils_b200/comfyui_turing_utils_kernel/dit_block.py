@@ -725,7 +725,7 @@ class DiTBlock:
         # returns to the token owners after the last launch.
         att = torch.empty((L, nha * D), dtype=full_dtype, device=x.device)
         pending, done = [], 0
-        with PROFILER.phase("dit.self_attention_o"):
+        with PROFILER.phase("dit.self_attention" if seq is not None else "dit.self_attention_o"):
             for a0, a1 in attention_launches(L, split=self.attn_split):
                 ops.attend_rows(state, a0, a1, mark=a1 == L, out=att[a0:a1])
                 while seq is None and done < C and (done + 1) * rows <= a1:
@@ -733,9 +733,11 @@ class DiTBlock:
                     pending.append(self._scatter(
                         ops.linear_q(ops.quantize(self._to_o_heads(blk)), w.o)))
                     done += 1
-            if seq is not None:
-                pending.append(self._scatter(
-                    ops.linear_q(ops.quantize(self._tokens_exchange(att)), w.o)))
+        if seq is not None:
+            with PROFILER.phase("dit.tokens_all_to_all"):
+                att = self._tokens_exchange(att)
+            with PROFILER.phase("dit.o_proj"):
+                pending.append(self._scatter(ops.linear_q(ops.quantize(att), w.o)))
         del state, qkv, q, k, v, att
 
         # Cross-attention: the context's K/V once, then per chunk.

@@ -75,14 +75,6 @@ constexpr uint32_t kPolyPairMask = TB_ATTN_POLY_MASK;
 #define TB_ATTN_SPLIT_LD 1
 #endif
 constexpr bool kSplitLd = TB_ATTN_SPLIT_LD != 0;
-// 1: the two softmax warps of a sub-partition (same TMEM lane quadrant, one
-// per query tile) take turns on the exponentials of a block, so one warp's
-// TMEM loads, P store and barrier hand-offs run while the other owns the
-// MUFU unit instead of both idling it at the same time.
-#ifndef TB_ATTN_PINGPONG
-#define TB_ATTN_PINGPONG 1
-#endif
-constexpr bool kPingPong = TB_ATTN_PINGPONG != 0;
 
 
 struct AttnParams {
@@ -117,7 +109,6 @@ struct __align__(8) AttnBarriers {
   uint64_t o_done[kQTiles];            // after each of the tile's last two PVs
   uint64_t o_final[kQTiles];           // after the tile's last PV
   uint64_t drain[kQTiles];
-  uint64_t turn[4][kQTiles];           // quadrant q's warp of tile t may take its exponentials
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -363,7 +354,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar->o_done[t], 1);
       mbar_init(&bar->o_final[t], 1);
       mbar_init(&bar->drain[t], 1);
-      for (int q = 0; q < 4; ++q) mbar_init(&bar->turn[q][t], 1);
     }
     bar->abort_flag = 0;
     fence_barrier_init();
@@ -512,13 +502,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;  // exponent reference point
     float dsum = 0.0f;        // row sum of p
     bool ok = n_kv > 0;
-    // Turns: tile 0's warp takes the exponentials of block j after the
-    // j-th completion of its turn barrier, then hands the turn to tile 1's
-    // warp of the same quadrant, which hands it back; tile 1 gives tile 0 its
-    // first turn.  Every wait is bounded.
-    uint64_t* my_turn = &bar->turn[quad][t];
-    uint64_t* other_turn = &bar->turn[quad][t ^ 1];
-    if (kPingPong && ok && t == 1 && lane == 0) mbar_arrive(other_turn);
     // Control flow stays warp-uniform: tcgen05.ld / st are .sync.aligned
     // warp-collective instructions, so every decision that guards one is
     // taken by a warp vote.
@@ -552,11 +535,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool done = false;
       bool need_rescale = false;  // some row of the warp moved its reference point
       float f = 1.0f;             // this row's rescale factor 2^(m_old - m_new)
-      if (kPingPong) {
-        ok = __all_sync(0xffffffffu, mbar_wait(my_turn, static_cast<uint32_t>(j) & 1u, abort_flag,
-                                               kDevWaitTimeoutSoftmax));
-        if (!ok) break;
-      }
       if (all_full && __all_sync(0xffffffffu, m_ref != -INFINITY)) {
         // Usual case: the reference point stands, so the exponentials need
         // not wait for the row max.  If any row's max moved past it (W8A8:
@@ -615,7 +593,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (all_full) exp_block<TV, false, W8A8>(v, cx2, bx2, valid, sum2);
         else exp_block<TV, true, W8A8>(v, cx2, bx2, valid, sum2);
       }
-      if (kPingPong && lane == 0) mbar_arrive(other_turn);
       tmem_st32(s_tmem, *reinterpret_cast<const uint32_t(*)[32]>(v));
       const uint64_t s01 = f2_add(sum2[0], sum2[1]);
       dsum += f2_lo(s01) + f2_hi(s01);

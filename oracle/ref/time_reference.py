@@ -170,7 +170,10 @@ def linear(dev, Lib) -> None:
     import oracle
 
     differ = (mine != out)
-    rows = torch.randperm(M, generator=torch.Generator().manual_seed(3))[:16].numpy()
+    # The sampled rows: 8 random ones plus up to 8 rows where the outputs differ.
+    diff_rows = torch.nonzero(differ.any(dim=1)).flatten()[:8].cpu()
+    rows = torch.cat([torch.randperm(M, generator=torch.Generator().manual_seed(3))[:8],
+                      diff_rows]).unique().numpy()
     q_np = xq.cpu().numpy()
     acc = oracle.int8_gemm_rows(q_np, w.cpu().numpy(), rows)
     want = oracle.dequant_bf16(acc, xs.cpu().numpy()[rows], w_s.cpu().numpy(),
@@ -184,8 +187,11 @@ def linear(dev, Lib) -> None:
            outputs_equal=bool(torch.equal(mine, out)),
            outputs_differing_frac=round(float(differ.float().mean()), 6),
            max_rel_diff=float(ulp.max()),
+           sampled_rows=int(rows.size), rows_with_differences=int(differ.any(dim=1).sum()),
            ours_equal_oracle_rows=bool(np.array_equal(bits(mine), want)),
-           reference_equal_oracle_rows=bool(np.array_equal(bits(out), want)))
+           reference_equal_oracle_rows=bool(np.array_equal(bits(out), want)),
+           reference_mismatches_vs_oracle=int((bits(out) != want).sum()),
+           ours_mismatches_vs_oracle=int((bits(mine) != want).sum()))
 
 
 def main() -> None:
