@@ -17,8 +17,8 @@ Ops, at BASELINE configs[0]'s and configs[1]'s shapes:
   `sol_sparse_online_w8a8_prequantized_attn` with force_dense=1
   (sol_sparse_cuda_sm75.cu:709-1394).
 
-Each op: 2 untimed calls, then 5 calls each bracketed by CUDA events on the
-current stream, with a 256 MB buffer written between calls (outside the
+After a 1 s warm-up of the GPU, each op: 2 untimed calls, then 5 calls each
+bracketed by CUDA events on the current stream, with a 256 MB buffer written between calls (outside the
 events) so no call finds the previous call's operands in the 126 MB L2.  The
 median is reported.  One JSON line per op on stdout:
 {"op", "reference_ms", "ours_ms", "speedup", ...}.
@@ -194,8 +194,21 @@ def linear(dev, Lib) -> None:
            ours_mismatches_vs_oracle=int((bits(mine) != want).sum()))
 
 
+def warm(dev, seconds: float = 1.0) -> None:
+    """Bring the GPU out of its idle clocks before the first timing."""
+    import time
+
+    a = torch.randn((4096, 4096), device=dev, dtype=torch.bfloat16)
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for _ in range(20):
+            a = torch.matmul(a, a) * 1e-2
+        torch.cuda.synchronize()
+
+
 def main() -> None:
     dev = torch.device("cuda:0")
+    warm(dev)
     linear(dev, R.linear())
     attention(dev, R.sage())
 
