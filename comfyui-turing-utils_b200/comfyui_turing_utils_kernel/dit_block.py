@@ -589,6 +589,15 @@ class DiTBlock:
             out[:, (h - p.head0) * D:(h - p.head0) * D + buf.size(1)] = buf
         return out
 
+    @staticmethod
+    def _all_to_all(recv, send, out_splits, in_splits, group, async_op=False):
+        """dist.all_to_all_single with NCCL's contract checked on every
+        backend: the split sizes count rows of dim 0 of each tensor."""
+        if recv.size(0) != sum(out_splits) or send.size(0) != sum(in_splits):
+            raise ValueError("all-to-all split sizes must sum to dim 0 of the tensors")
+        return dist.all_to_all_single(recv, send, out_splits, in_splits, group=group,
+                                      async_op=async_op)
+
     def _heads_exchange(self, state):
         """All-to-all of the prepared self-attention operands of this rank's
         tokens (all heads) -> those of this rank's heads (all tokens): the
@@ -601,27 +610,25 @@ class DiTBlock:
         works = []
 
         def tokens_nhd(t):  # [Lr, H, D] (any strides, unit channel stride) -> [L, nh, D]
-            send = t.reshape(Lr, W, nh, D).permute(1, 0, 2, 3).contiguous()
+            send = t.reshape(Lr, W, nh, D).permute(1, 0, 2, 3).reshape(W * Lr, nh, D)
             recv = torch.empty((L, nh, D), dtype=t.dtype, device=t.device)
-            works.append(dist.all_to_all_single(recv, send, sizes, [Lr] * W, group=seq.group,
-                                                async_op=True))
+            works.append(self._all_to_all(recv, send, sizes, [Lr] * W, seq.group, True))
             return recv
 
         def tokens_hnd(t):  # [H, Lr, D] -> flat pieces of [nh, L_src, D]
             send = t.reshape(W, nh * Lr * D).contiguous()
             recv = torch.empty((nh * L * D,), dtype=t.dtype, device=t.device)
-            works.append(dist.all_to_all_single(recv, send.view(-1),
-                                                [nh * n * D for n in sizes], [nh * Lr * D] * W,
-                                                group=seq.group, async_op=True))
+            works.append(self._all_to_all(recv, send.view(-1), [nh * n * D for n in sizes],
+                                          [nh * Lr * D] * W, seq.group, True))
             return recv
 
         def tiles(sc, per_block):  # [1, H, n_me] per-tile scales -> list of [nh, n_src] pieces
             counts = [(n + 63) // 64 * per_block for n in sizes]
             assert sc.size(-1) == counts[me]
             recv = torch.empty((nh * sum(counts),), dtype=sc.dtype, device=sc.device)
-            works.append(dist.all_to_all_single(recv, sc.contiguous().view(-1),
-                                                [nh * n for n in counts], [nh * counts[me]] * W,
-                                                group=seq.group, async_op=True))
+            works.append(self._all_to_all(recv, sc.contiguous().view(-1),
+                                          [nh * n for n in counts], [nh * counts[me]] * W,
+                                          seq.group, True))
             return recv, counts
 
         if isinstance(self.ops, KernelOps):
@@ -651,8 +658,7 @@ class DiTBlock:
         seq = self.seq
         W, sizes, Lr = seq.world, seq.sizes, seq.sizes[seq.rank]
         recv = torch.empty((W, Lr, att.size(1)), dtype=att.dtype, device=att.device)
-        dist.all_to_all_single(recv.view(W * Lr, -1), att.contiguous(), [Lr] * W, sizes,
-                               group=seq.group)
+        self._all_to_all(recv.view(W * Lr, -1), att.contiguous(), [Lr] * W, sizes, seq.group)
         return recv.permute(1, 0, 2).reshape(Lr, W * att.size(1))
 
     def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
