@@ -7,7 +7,11 @@ and distributions — the reference benchmarks on no public dataset):
   dit_block  configs[4] (default): one Wan2.1-14B-shaped DiT block, dim 5120,
              40 heads x 128, FFN 13824, L = 75600, 512 text tokens, W8A8
              ConvRot linears, Sage INT8 self- and cross-attention, AdaLN;
-             tensor + sequence parallel over the torchrun ranks (NCCL).
+             over the torchrun ranks either all-to-all sequence parallel
+             (--parallel a2a, default: token shards through every linear,
+             head shards for self-attention) or Megatron tensor + sequence
+             parallel (--parallel tp), over NCCL; a "parity" key checks 256
+             sampled output tokens against the fp32 reference block.
              Metric: block tokens/s (L / block time, max over ranks),
              strong scaling.
   attention  configs[1]: Sage INT8 attention B=1, H=40, L=32760, D=128, HND,
@@ -35,10 +39,10 @@ and distributions — the reference benchmarks on no public dataset):
 Metric of the other workloads: INT8 TOPS (whole job, all ranks) = algorithmic
 ops / device time.
 
-Multi-GPU (torchrun): dit_block splits one block over the ranks (strong
-scaling); every other workload runs an independent copy per rank (its own
-batch shard, no data-path collective, weak scaling).  Time = max over ranks of
-the per-rank device time.
+Multi-GPU (torchrun): every workload splits one config over the ranks
+(strong scaling): dit_block as above; the linears their tokens (rows of X,
+weights replicated), the attentions their 40 heads, with no data-path
+collective.  Time = max over ranks of the per-rank device time.
 
 --impl reference times the reference's CPU implementation of the same step
 (the torch fp32 dequantize-then-matmul / dequantize-then-attention path of
@@ -938,14 +942,51 @@ WORKLOADS = {"linear": LinearWorkload, "attention": AttentionWorkload,
              "codebook": CodebookWorkload, "w4a4_ffn": W4A4FFNWorkload}
 
 
+def _split(units: int, parts: int) -> list[int]:
+    base, extra = divmod(units, parts)
+    return [base + (1 if r < extra else 0) for r in range(parts)]
+
+
 def make_workload(args, device, seed, world=1, rank=0):
+    """The workload of this rank.  On several ranks the independent configs
+    are sharded with no collective: the linears split their
+    tokens (rows of X; the weights are replicated), the attentions their 40
+    heads; the reported value is the whole config's work over the max-over-
+    ranks step time ("scaling": "strong")."""
     if args.workload in ("attention", "attention_rope", "w8a8_attention"):
-        return WORKLOADS[args.workload](device, seed, heads=args.heads)
+        if world == 1 or args.heads is not None:
+            return WORKLOADS[args.workload](device, seed, heads=args.heads)
+        heads = AttentionWorkload.config["heads"]
+        if heads % world:
+            raise ValueError(f"{heads} heads do not split evenly over {world} ranks")
+        wl = WORKLOADS[args.workload](device, seed + rank, heads=heads // world)
+        wl.name = args.workload                      # the committed traffic is per head
+        wl.traffic_scale = 1.0 / world
+        wl.config = dict(WORKLOADS[args.workload].config, heads_per_rank=heads // world)
+        wl.work = wl.ops * world                     # whole config (wl.ops: this rank's heads)
+        wl.scaling = "strong"
+        wl.shard_desc = f"heads split over {world} ranks ({heads // world} each), no collective"
+        return wl
     if args.workload == "dit_block":
         return DiTBlockWorkload(device, world, rank, tokens=args.tokens,
                                 use_graph=not args.no_graph, max_chunks=args.chunks,
                                 parallel=args.parallel)
-    return WORKLOADS[args.workload](device, seed)
+    wl = WORKLOADS[args.workload](device, seed)
+    if world > 1:
+        m_full = wl.config["m"]
+        sizes = _split(m_full, world)
+        r0, m = sum(sizes[:rank]), sizes[rank]
+        wl.x = wl.x[r0:r0 + m].contiguous()
+        wl.x_host = wl.x_host[r0:r0 + m]
+        wl.out_host = wl.out_host[r0:r0 + m]
+        wl.dom_ops *= m / m_full                     # this rank's dominant kernel
+        wl.h2d_bytes = wl.x_host.numel() * 2
+        wl.d2h_bytes = wl.out_host.numel() * 2
+        wl.config = dict(wl.config, m_per_rank=m)    # wl.ops stays the whole config's
+        wl.scaling = "strong"
+        wl.shard_desc = (f"tokens (rows of X) split over {world} ranks ({m} here), weights "
+                         "replicated, no collective")
+    return wl
 
 
 def default_workload() -> str:
@@ -1086,7 +1127,7 @@ def run_ours(args, world, rank, local):
         "dtype": "int8",
         "data": "synthetic (seeded; BASELINE shapes and distributions)",
         "config": dict(wl.config, parallelism=wl.parallelism(world) if hasattr(wl, "parallelism")
-                       else f"independent shards x{world} (no collective)",
+                       else getattr(wl, "shard_desc", "1 GPU"),
                        l2="256 MB buffer written between steps; per-step CUDA events exclude it"),
         "impl": "ours",
         "roofline": roof,
