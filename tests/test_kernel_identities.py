@@ -70,3 +70,38 @@ def test_pv_partial_sums_are_exact():
     np.testing.assert_array_equal(acc.astype(np.int64), exact)
     # Every code is exact in fp16 (an fp16 integer needs <= 11 significant bits).
     assert (np.arange(-128, 256).astype(np.float16).astype(np.int64) == np.arange(-128, 256)).all()
+
+
+def _exp2_poly(x: np.ndarray) -> np.ndarray:
+    """sage_attn.cu exp2_poly_pair restated in float32: clamp at -120,
+    n = rint(x) through the 1.5 * 2^23 constant, f = x - n in [-0.5, 0.5],
+    2^f by the degree-3 minimax polynomial (Horner with fused multiply-adds,
+    emulated in float64 with one float32 rounding each), 2^n added to the
+    exponent field."""
+    x = np.maximum(x.astype(np.float32), np.float32(-120.0))
+    r2 = (x + MAGIC).astype(np.float32)
+    f = (x - (r2 - MAGIC).astype(np.float32)).astype(np.float32)
+
+    def fma(a, b, c):
+        return (a.astype(np.float64) * b.astype(np.float64) + np.float64(c)).astype(np.float32)
+
+    q = fma(f, np.full_like(f, np.float32(0.0551716685295105)), np.float32(0.2426111251115799))
+    q = fma(q, f, np.float32(0.6932609677314758))
+    q = fma(q, f, np.float32(0.9999280571937561))
+    n_bits = (r2.view(np.uint32).astype(np.uint64) << np.uint64(23)) & np.uint64(0xFFFFFFFF)
+    bits = (q.view(np.uint32).astype(np.uint64) + n_bits) & np.uint64(0xFFFFFFFF)
+    return bits.astype(np.uint32).view(np.float32)
+
+
+def test_fma_pipe_exp2_matches_exp2_within_the_p_rounding():
+    """The FMA-pipe 2^x that takes one pair of scores in sixteen off the MUFU
+    unit: relative error <= 8e-5 on every representable x in [-100, 8] at a
+    2^-12 step (the softmax arguments: at most 8 above the reference point),
+    far below the 2^-9 rounding of the 16-bit P it feeds."""
+    x = np.arange(-100.0, 8.0, 2.0 ** -12, dtype=np.float64).astype(np.float32)
+    got = _exp2_poly(x).astype(np.float64)
+    want = np.exp2(x.astype(np.float64))
+    rel = np.abs(got - want) / want
+    assert rel.max() <= 8e-5, rel.max()
+    # Below the clamp the result is 2^-120 (0 for every later use of p).
+    assert _exp2_poly(np.array([-300.0, -121.0], np.float32)).max() <= np.float32(2.0 ** -119)
