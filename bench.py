@@ -873,14 +873,66 @@ class DiTBlockWorkload:
             ev[3].record()
         return out
 
+    def e2e_begin(self):
+        """Starts a streaming run of step_e2e (graph mode): the first step's
+        tokens go up on the input copy stream; later steps' inputs are copied
+        in, and earlier steps' outputs copied out, on two copy streams while
+        the block computes, through two device staging buffers each way."""
+        if self.graph is None:
+            return
+        cur = torch.cuda.current_stream()
+        if not hasattr(self, "_h2d"):
+            self._h2d, self._d2h = torch.cuda.Stream(), torch.cuda.Stream()
+            self._stage = [(torch.empty_like(self.x), torch.empty_like(self.ctx)) for _ in range(2)]
+            self._outbuf = [torch.empty_like(self.graph_out) for _ in range(2)]
+            self._ev = {k: [torch.cuda.Event() for _ in range(2)]
+                        for k in ("in", "free", "out", "done")}
+        for b in range(2):            # nothing pending on either buffer
+            self._ev["free"][b].record(cur)
+            self._ev["done"][b].record(cur)
+        self._h2d.wait_stream(cur)
+        with torch.cuda.stream(self._h2d):
+            self._stage[0][0].copy_(self.host[0], non_blocking=True)
+            self._stage[0][1].copy_(self.host[1], non_blocking=True)
+            self._ev["in"][0].record()
+        self._i = 0
+
+    def e2e_finish(self):
+        """The compute stream waits for the last copies (they are timed)."""
+        if self.graph is None:
+            return
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self._h2d)
+        cur.wait_stream(self._d2h)
+
     def step_e2e(self):
         """Host tokens in, host tokens out, through the same block call (the
-        captured graph reads its static input buffers)."""
+        captured graph reads its static input buffers).  Between e2e_begin
+        and e2e_finish the copies of neighbouring steps overlap this step's
+        compute (a serving loop's double buffering); every step still moves
+        its whole input from pinned host memory and its whole output back."""
         if self.graph is not None:
-            self.x.copy_(self.host[0], non_blocking=True)
-            self.ctx.copy_(self.host[1], non_blocking=True)
+            cur = torch.cuda.current_stream()
+            ev, b, nb = self._ev, self._i % 2, (self._i + 1) % 2
+            with torch.cuda.stream(self._h2d):      # the next step's input
+                self._h2d.wait_event(ev["free"][nb])
+                self._stage[nb][0].copy_(self.host[0], non_blocking=True)
+                self._stage[nb][1].copy_(self.host[1], non_blocking=True)
+                ev["in"][nb].record()
+            cur.wait_event(ev["in"][b])
+            self.x.copy_(self._stage[b][0])
+            self.ctx.copy_(self._stage[b][1])
+            ev["free"][b].record(cur)
             self.graph.replay()
-            out = self.graph_out
+            cur.wait_event(ev["done"][b])
+            self._outbuf[b].copy_(self.graph_out)
+            ev["out"][b].record(cur)
+            with torch.cuda.stream(self._d2h):      # this step's output
+                self._d2h.wait_event(ev["out"][b])
+                self.out_host.copy_(self._outbuf[b], non_blocking=True)
+                ev["done"][b].record()
+            self._i += 1
+            return self._outbuf[b]
         else:
             dev = self.x.device
             x, ctx = (t.to(dev, non_blocking=True) for t in self.host)
@@ -1077,14 +1129,19 @@ def run_ours(args, world, rank, local):
     dom_avg = sum(dom_ms) / len(dom_ms)
 
     # End to end through the public API with host buffers.
+    begin, finish = (getattr(wl, "e2e_begin", lambda: None), getattr(wl, "e2e_finish", lambda: None))
+    begin()
     for _ in range(max(1, args.warmup // 2)):
         wl.step_e2e()
+    finish()
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    begin()
     for _ in range(args.steps):
         wl.step_e2e()
+    finish()
     e1.record()
     torch.cuda.synchronize()
     barrier(world)
@@ -1133,7 +1190,13 @@ def run_ours(args, world, rank, local):
         "roofline": roof,
         "e2e": {"value": round(job / (e2e_ms * 1e-3) / scale, 2), "unit": unit,
                 "h2d_bytes_per_step": wl.h2d_bytes, "d2h_bytes_per_step": wl.d2h_bytes,
-                "ms_per_step": round(e2e_ms, 4)},
+                "ms_per_step": round(e2e_ms, 4),
+                **({"copies": "each step's input up from and output back to pinned host "
+                              "memory on two copy streams, overlapping the neighbouring "
+                              "steps' compute (double-buffered); first input and last "
+                              "output inside the timed region"}
+                   if hasattr(wl, "e2e_begin") and getattr(wl, "graph", None) is not None
+                   else {})},
         "gpu_launches": wl.launches_per_step * args.steps,
         **({"block_tops": round(wl.ops / (ms * 1e-3) / 1e12, 1)} if wl.name == "dit_block" else {}),
         "clocks": dict(sampler.summary(), region="timed+soak" if soak else "timed"),
