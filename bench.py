@@ -216,6 +216,17 @@ class LinearWorkload:
 
     cpu_sample_desc = "rows of X, full N and K (ConvRot oracle + torch fp32 dequantize-then-matmul)"
 
+    def aux_roofline(self, pro_ms, peaks):
+        """The ConvRot prologue (event 0 -> 1 of a step) against HBM:
+        2 B read + 1 B code written per element + a 4 B scale per row."""
+        m, k = self.x.size(0), self.x.size(1)
+        bytes_ = 3 * m * k + 4 * m
+        achieved = bytes_ / (pro_ms * 1e-3) / 1e9
+        return {"prologue": {"kernel": "convrot_rowbuffer", "bound": "hbm",
+                             "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                             "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                             "algorithmic_bytes": bytes_, "ms": round(pro_ms, 4)}}
+
     def roofline(self, dom_ms, peaks):
         int8_peak = 2.0 * peaks["bf16_tflops"]
         achieved = self.dom_ops / (dom_ms * 1e-3) / 1e12

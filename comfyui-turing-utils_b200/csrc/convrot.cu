@@ -135,6 +135,11 @@ __device__ __forceinline__ uint64_t psub(uint64_t a, uint64_t b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t pmul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ uint64_t phalf(uint64_t a) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(0x3F0000003F000000ull));
@@ -255,6 +260,22 @@ __device__ __forceinline__ float row_scale_from_amax(float amax) {
   }
 }
 
+// Both halves of a T pair clamped to [-128, 127] with the 16-bit max / min
+// (a NaN operand loses, as in fmaxf / fminf, so NaN gives -128); -128 and 127
+// are exact in bf16 and fp16, so this equals clamping the widened values.
+template <typename T>
+__device__ __forceinline__ uint32_t clamp_pair_i8(uint32_t d2) {
+  uint32_t r;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("{\n\t.reg .b32 t;\n\tmax.bf16x2 t, %1, %2;\n\tmin.bf16x2 %0, t, %3;\n\t}"
+        : "=r"(r) : "r"(d2), "r"(0xC300C300u), "r"(0x42FE42FEu));
+  } else {
+    asm("{\n\t.reg .b32 t;\n\tmax.f16x2 t, %1, %2;\n\tmin.f16x2 %0, t, %3;\n\t}"
+        : "=r"(r) : "r"(d2), "r"(0xD800D800u), "r"(0x57F057F0u));
+  }
+  return r;
+}
+
 // Quantizes 16 consecutive rotated elements (bits in `h`) and stores them.
 // INT8: the reference divides by the T-rounded scale,
 // rint(T(v / T(scale))); here v is multiplied by rcp_rounded =
@@ -286,15 +307,20 @@ __device__ __forceinline__ void quantize16_store(const uint32_t (&h)[8], float r
     // to -128, as the reference's fminf(127, fmaxf(-128, NaN)) does), and
     // adding 1.5 * 2^23 rounds to the nearest integer, ties to even, exactly
     // as __float2int_rn, leaving the code two's-complement in the low byte.
+    // Packed: both multiplies in one mul.rn.f32x2 and both rounding adds in
+    // one add.rn.f32x2 (each lane rounds as the scalar form), the clamp on the
+    // T pair.
     uint32_t cb[16];
+    const uint64_t rcp2 = pk(rcp_rounded, rcp_rounded);
+    const uint64_t magic2 = pk(12582912.0f, 12582912.0f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const uint32_t d2 = pack2_elem<T>(__fmul_rn(elem_to_f32<T>(h[i] & 0xffffu), rcp_rounded),
-                                        __fmul_rn(elem_to_f32<T>(h[i] >> 16), rcp_rounded));
-      cb[2 * i] = __float_as_uint(__fadd_rn(
-          fminf(127.0f, fmaxf(-128.0f, elem_to_f32<T>(d2 & 0xffffu))), 12582912.0f));
-      cb[2 * i + 1] = __float_as_uint(__fadd_rn(
-          fminf(127.0f, fmaxf(-128.0f, elem_to_f32<T>(d2 >> 16))), 12582912.0f));
+      float lo, hi;
+      unpk(pmul(pk(elem_to_f32<T>(h[i] & 0xffffu), elem_to_f32<T>(h[i] >> 16)), rcp2), lo, hi);
+      const uint32_t d2 = clamp_pair_i8<T>(pack2_elem<T>(lo, hi));
+      unpk(padd(pk(elem_to_f32<T>(d2 & 0xffffu), elem_to_f32<T>(d2 >> 16)), magic2), lo, hi);
+      cb[2 * i] = __float_as_uint(lo);
+      cb[2 * i + 1] = __float_as_uint(hi);
     }
     uint32_t out[4];
 #pragma unroll
@@ -336,11 +362,23 @@ __global__ void __launch_bounds__(512) convrot_rowbuffer_kernel(RowQuantParams p
   // run the same number of iterations (the transpose and the shuffles below
   // are warp-collective); an odd last item leaves one half-warp idle.
   const int items = rows_here * groups;
+  // (row, group) of this half-warp's item, advanced by `halfwarps` items per
+  // iteration without a division.
+  int ir = 0, ig = 2 * (hw >> 1) + (hw & 1);
+  while (ig >= groups) {
+    ig -= groups;
+    ++ir;
+  }
   for (int base = 2 * (hw >> 1); base < items; base += halfwarps) {
     const int item = base + (hw & 1);
     const bool active = item < items;
-    const int r = active ? item / groups : 0;
-    const int g = active ? item - r * groups : 0;
+    const int r = active ? ir : 0;
+    const int g = active ? ig : 0;
+    ig += halfwarps;
+    while (ig >= groups) {
+      ig -= groups;
+      ++ir;
+    }
     const T* row_in = in + static_cast<int64_t>(row0 + r) * in_width;
     float v[16];
     load16<T, ACT>(row_in, k, g * kGroup + 16 * l, v);
@@ -362,24 +400,40 @@ __global__ void __launch_bounds__(512) convrot_rowbuffer_kernel(RowQuantParams p
     if (active && l == 0) atomicMax(&row_amax[r], __float_as_uint(amax));
   }
   __syncthreads();
+  // Per-row constants once per row: scale, RN(1 / T(scale)) and RN(1 / scale),
+  // over the row's absmax words (which this overwrites: nothing reads them
+  // after the barrier below).
+  float* row_rcp = reinterpret_cast<float*>(row_amax);
+  for (int r = tid; r < rows_here; r += blockDim.x) {
+    const float scale = row_scale_from_amax<T, INT4, STAGED_SCALE>(__uint_as_float(row_amax[r]));
+    p.scales[row0 + r] = scale;
+    row_rcp[r] = INT4 ? __frcp_rn(scale) : __frcp_rn(round_to_elem<T>(scale));
+  }
+  __syncthreads();
 
   // Phase 2: quantize the buffered rows with coalesced 16-element chunks.
   const int chunks_per_row = k / 16;
   const int chunks = rows_here * chunks_per_row;
+  int cr = 0, cc = tid;  // (row, chunk in row) of chunk `c`, advanced without a division
+  while (cc >= chunks_per_row) {
+    cc -= chunks_per_row;
+    ++cr;
+  }
   for (int c = tid; c < chunks; c += blockDim.x) {
-    const int r = c / chunks_per_row;
-    const int col = (c - r * chunks_per_row) * 16;
-    const float amax = __uint_as_float(row_amax[r]);
-    const float scale = row_scale_from_amax<T, INT4, STAGED_SCALE>(amax);
-    const float rcp_rounded = __frcp_rn(round_to_elem<T>(scale));
-    const float inv_scale = __frcp_rn(scale);
+    const int r = cr;
+    const int col = cc * 16;
+    cc += blockDim.x;
+    while (cc >= chunks_per_row) {
+      cc -= chunks_per_row;
+      ++cr;
+    }
+    const float rcp = row_rcp[r];
     const uint4* src = reinterpret_cast<const uint4*>(rowbuf + static_cast<size_t>(r) * k + col);
     uint4 a = src[0], b = src[1];
     uint32_t h[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     const int64_t row = row0 + r;
     int8_t* dst = INT4 ? p.output + row * (k / 2) + col / 2 : p.output + row * k + col;
-    quantize16_store<T, INT4>(h, rcp_rounded, inv_scale, dst);
-    if (col == 0) p.scales[row] = scale;
+    quantize16_store<T, INT4>(h, rcp, rcp, dst);
   }
 }
 
