@@ -747,55 +747,52 @@ class DiTBlock:
         del state, qkv, q, k, v, att
 
         # Cross-attention: the context's K/V once, then per chunk.
-        cross = PROFILER.phase("dit.cross_attention")
-        cross.__enter__()
-        kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)
-        k_rrms = self._rrms(kv[:, 0])
-        gathered = []
-        for i, (y, job) in enumerate(pending):
-            if job is not None:
-                job[0].wait()
-            residual("self", i, y, m[2])
-            gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], w.cross_norm[1],
-                                                                   w.cross_norm[0], c.eps))))
-        # Q of every chunk first, so the cross-rank RMS of all chunks is one
-        # all-reduce (a collective queues behind the chunks' gathers).
-        qcs = []
-        for i, (act, works) in enumerate(gathered):
-            self._wait(works)
-            qcs.append(ops.linear_q(act, w.cq).view(rows, nh, D))
-        q_rrms = [None] * C
-        if N > 1 or not isinstance(ops, KernelOps):
-            sums = self._all_reduce(torch.cat([ops.sum_squares(qc).float() for qc in qcs]))
-            q_rrms = list(torch.rsqrt(sums / c.dim + c.eps).split(rows))
-        pending = []
-        for i, qc in enumerate(qcs):
-            st = ops.qk_prepare(qc, kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0,
-                                q_rrms[i], k_rrms, c.eps)
-            att = ops.attend_rows(st, 0, rows)
-            pending.append(self._scatter(ops.linear_q(ops.quantize(self._to_o_heads(att)), w.co)))
-        del qcs
-        cross.__exit__(None, None, None)
+        with PROFILER.phase("dit.cross_attention"):
+            kv = ops.linear_q(ops.quantize(ctx), w.ckv).view(Lc, 2, nh, D)
+            k_rrms = self._rrms(kv[:, 0])
+            gathered = []
+            for i, (y, job) in enumerate(pending):
+                if job is not None:
+                    job[0].wait()
+                residual("self", i, y, m[2])
+                gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], w.cross_norm[1],
+                                                                       w.cross_norm[0], c.eps))))
+            # Q of every chunk first, so the cross-rank RMS of all chunks is one
+            # all-reduce (a collective queues behind the chunks' gathers).
+            qcs = []
+            for i, (act, works) in enumerate(gathered):
+                self._wait(works)
+                qcs.append(ops.linear_q(act, w.cq).view(rows, nh, D))
+            q_rrms = [None] * C
+            if N > 1 or not isinstance(ops, KernelOps):
+                sums = self._all_reduce(torch.cat([ops.sum_squares(qc).float() for qc in qcs]))
+                q_rrms = list(torch.rsqrt(sums / c.dim + c.eps).split(rows))
+            pending = []
+            for i, qc in enumerate(qcs):
+                st = ops.qk_prepare(qc, kv[:, 0], kv[:, 1], w.cnorm_q, w.cnorm_k, None, 0,
+                                    q_rrms[i], k_rrms, c.eps)
+                att = ops.attend_rows(st, 0, rows)
+                pending.append(self._scatter(
+                    ops.linear_q(ops.quantize(self._to_o_heads(att)), w.co)))
+            del qcs
 
         # Feed-forward per chunk.
-        ffn = PROFILER.phase("dit.ffn")
-        ffn.__enter__()
-        gathered = []
-        for i, (y, job) in enumerate(pending):
-            if job is not None:
-                job[0].wait()
-            residual("cross", i, y, None)
-            gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], m[4], m[3], c.eps))))
-        pending = []
-        for i, (act, works) in enumerate(gathered):
-            self._wait(works)
-            u = ops.linear_q(act, w.up)
-            pending.append(self._scatter(ops.linear_q(ops.gelu_quantize(u), w.down)))
-        for i, (y, job) in enumerate(pending):
-            if job is not None:
-                job[0].wait()
-            residual("ffn", i, y, m[5])
-        ffn.__exit__(None, None, None)
+        with PROFILER.phase("dit.ffn"):
+            gathered = []
+            for i, (y, job) in enumerate(pending):
+                if job is not None:
+                    job[0].wait()
+                residual("cross", i, y, None)
+                gathered.append(self._gather(ops.quantize(ops.ln_adaln(xs[i], m[4], m[3], c.eps))))
+            pending = []
+            for i, (act, works) in enumerate(gathered):
+                self._wait(works)
+                u = ops.linear_q(act, w.up)
+                pending.append(self._scatter(ops.linear_q(ops.gelu_quantize(u), w.down)))
+            for i, (y, job) in enumerate(pending):
+                if job is not None:
+                    job[0].wait()
+                residual("ffn", i, y, m[5])
         PROFILER.complete_attention((L, c.dim))
         return x
 
