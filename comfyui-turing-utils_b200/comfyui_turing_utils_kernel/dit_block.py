@@ -513,7 +513,9 @@ class DiTBlock:
     the full weights) the block runs all-to-all sequence parallel instead:
     this rank's tokens go through every norm, linear and the cross-attention
     as on one GPU, and the self-attention of its heads over all tokens sits
-    between two all-to-alls (`_heads_exchange`, `_tokens_exchange`).  Every
+    between two all-to-alls (`_heads_exchange`; `_tokens_exchange_start`, one
+    per attention launch so a launch's rows travel under the next launch, and
+    `_tokens_exchange_finish`).  Every
     output row is then the one-rank block's row bit for bit.
     """
 
@@ -652,14 +654,34 @@ class DiTBlock:
 
         return tuple(join_hnd(r) for r in out)
 
-    def _tokens_exchange(self, att: torch.Tensor) -> torch.Tensor:
-        """All-to-all of the self-attention output [L, nh * D] of this rank's
-        heads -> [Lr, H * D] of this rank's tokens (heads in rank order)."""
+    def _tokens_exchange_start(self, att: torch.Tensor, a0: int, a1: int):
+        """Starts the all-to-all that returns rows [a0, a1) of the
+        self-attention output [L, nh * D] of this rank's heads to the ranks
+        owning those tokens (async: it runs under the next attention launch).
+        Returns (work, received rows, this rank's row range inside its shard)."""
         seq = self.seq
-        W, sizes, Lr = seq.world, seq.sizes, seq.sizes[seq.rank]
-        recv = torch.empty((W, Lr, att.size(1)), dtype=att.dtype, device=att.device)
-        self._all_to_all(recv.view(W * Lr, -1), att.contiguous(), [Lr] * W, sizes, seq.group)
-        return recv.permute(1, 0, 2).reshape(Lr, W * att.size(1))
+        W, me = seq.world, seq.rank
+        send = [max(0, min(a1, t1) - max(a0, t0)) for t0, t1 in seq.bounds]
+        t0, t1 = seq.bounds[me]
+        r0, r1 = max(a0, t0), min(a1, t1)
+        m = max(0, r1 - r0)
+        recv = torch.empty((W * m, att.size(1)), dtype=att.dtype, device=att.device)
+        work = self._all_to_all(recv, att[a0:a1], [m] * W, send, seq.group, async_op=True)
+        return work, recv, (r0 - t0, r0 - t0 + m)
+
+    def _tokens_exchange_finish(self, parts, width: int) -> torch.Tensor:
+        """Waits for the exchanges of _tokens_exchange_start and assembles
+        this rank's [Lr, H * D] attention output (heads in rank order)."""
+        seq = self.seq
+        W, Lr = seq.world, seq.sizes[seq.rank]
+        out = None
+        for work, recv, (r0, r1) in parts:
+            work.wait()
+            if out is None:
+                out = torch.empty((Lr, W, width), dtype=recv.dtype, device=recv.device)
+            if r1 > r0:
+                out[r0:r1] = recv.view(W, r1 - r0, width).permute(1, 0, 2)
+        return out.view(Lr, W * width)
 
     def _rrms(self, t: torch.Tensor) -> Optional[torch.Tensor]:
         """Row RRMS over the heads of every rank (None: one rank, the fused
@@ -731,9 +753,12 @@ class DiTBlock:
         # returns to the token owners after the last launch.
         att = torch.empty((L, nha * D), dtype=full_dtype, device=x.device)
         pending, done = [], 0
+        exchanges = []
         with PROFILER.phase("dit.self_attention" if seq is not None else "dit.self_attention_o"):
             for a0, a1 in attention_launches(L, split=self.attn_split):
                 ops.attend_rows(state, a0, a1, mark=a1 == L, out=att[a0:a1])
+                if seq is not None:  # these rows go home under the next launch
+                    exchanges.append(self._tokens_exchange_start(att, a0, a1))
                 while seq is None and done < C and (done + 1) * rows <= a1:
                     blk = att[done * rows:(done + 1) * rows]
                     pending.append(self._scatter(
@@ -741,7 +766,7 @@ class DiTBlock:
                     done += 1
         if seq is not None:
             with PROFILER.phase("dit.tokens_all_to_all"):
-                att = self._tokens_exchange(att)
+                att = self._tokens_exchange_finish(exchanges, nha * D)
             with PROFILER.phase("dit.o_proj"):
                 pending.append(self._scatter(ops.linear_q(ops.quantize(att), w.o)))
         del state, qkv, q, k, v, att

@@ -126,8 +126,10 @@ def test_token_shards_are_whole_quantizer_blocks():
         db.token_shards(100, 4)
 
 
-def _a2a_out(world: int, rank: int, L: int, group=None):
-    """All-to-all sequence-parallel block (fp32 backend): this rank's tokens."""
+def _a2a_out(world: int, rank: int, L: int, group=None, split=None):
+    """All-to-all sequence-parallel block (fp32 backend): this rank's tokens;
+    `split` makes self-attention two launches, each returning its rows in its
+    own all-to-all."""
     cfg = SMALL
     w = db.make_weights(cfg, db.shard_plan(cfg, 1, 0), seed=3)
     g = torch.Generator().manual_seed(9)
@@ -136,31 +138,35 @@ def _a2a_out(world: int, rank: int, L: int, group=None):
     freqs = db.rope_freqs(L, cfg.head_dim, seed=4, dtype=torch.float32)
     seq = db.SeqShards.make(L, world, rank, group)
     t0, t1 = seq.bounds[rank]
-    block = db.DiTBlock(cfg, w, db.shard_plan(cfg, 1, 0), db.TorchOps(), seq=seq)
+    block = db.DiTBlock(cfg, w, db.shard_plan(cfg, 1, 0), db.TorchOps(), seq=seq,
+                        attn_split=split)
     return x, (t0, t1), block.forward(x[t0:t1], ctx, freqs)
 
 
-def _a2a_rank_main(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
+def _a2a_rank_main(rank: int, world: int, port: int, out_dir: str, L: int, split) -> None:
     sys.path.insert(0, str(ROOT / "comfyui-turing-utils_b200"))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        _, bounds, out = _a2a_out(world, rank, L)
+        _, bounds, out = _a2a_out(world, rank, L, split=split)
         torch.save((bounds, out), Path(out_dir) / f"a2a{rank}.pt")
     finally:
         torch.distributed.destroy_process_group()
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("world,L", [(2, 96), (4, 200)])
-def test_all_to_all_block_equals_one_rank(tmp_path, world, L):
-    """Token shards for the linears, head shards for self-attention, two
-    all-to-alls: the same weights and arithmetic as one rank, so the rows
-    agree to fp32 summation order (uneven shards at L = 200: 64,64,64,8)."""
+@pytest.mark.parametrize("world,L,split", [(2, 96, None), (4, 200, None), (4, 200, 100),
+                                           (2, 96, 80)])
+def test_all_to_all_block_equals_one_rank(tmp_path, world, L, split):
+    """Token shards for the linears, head shards for self-attention, the
+    all-to-alls around it: the same weights and arithmetic as one rank, so the
+    rows agree to fp32 summation order (uneven shards at L = 200: 64,64,64,8;
+    with `split` the attention output returns in two all-to-alls whose row
+    ranges cut through shards)."""
     import torch.multiprocessing as mp
 
     x, _, single = _block_out(1, 0, SMALL, L)
-    mp.start_processes(_a2a_rank_main, args=(world, _free_port(), str(tmp_path), L),
+    mp.start_processes(_a2a_rank_main, args=(world, _free_port(), str(tmp_path), L, split),
                        nprocs=world, start_method="spawn", join=True)
     full = torch.full_like(x, float("nan"))
     for r in range(world):

@@ -211,7 +211,7 @@ def test_tensor_parallel_two_gpus(tmp_path):
     assert rel <= 3e-2 and cos >= 0.999, (rel, cos)
 
 
-def _a2a_rank(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
+def _a2a_rank(rank: int, world: int, port: int, out_dir: str, L: int, split) -> None:
     import datetime
 
     sys.path.insert(0, str(ROOT / "comfyui-turing-utils_b200"))
@@ -226,7 +226,8 @@ def _a2a_rank(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
         x, ctx, freqs = _inputs(SMALL, L, 40)
         seq = db.SeqShards.make(L, world, rank, torch.distributed.group.WORLD)
         t0, t1 = seq.bounds[rank]
-        out = db.DiTBlock(SMALL, w, plan, db.KernelOps(), seq=seq).forward(x[t0:t1], ctx, freqs)
+        out = db.DiTBlock(SMALL, w, plan, db.KernelOps(), seq=seq,
+                          attn_split=split).forward(x[t0:t1], ctx, freqs)
         torch.cuda.synchronize()
         torch.save(((t0, t1), out.cpu()), Path(out_dir) / f"a2a{rank}.pt")
     finally:
@@ -235,14 +236,16 @@ def _a2a_rank(rank: int, world: int, port: int, out_dir: str, L: int) -> None:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("L", [300, 1000])
-def test_all_to_all_two_gpus_equals_one_gpu(tmp_path, L):
+@pytest.mark.parametrize("L,split", [(300, None), (1000, None), (1000, 384)])
+def test_all_to_all_two_gpus_equals_one_gpu(tmp_path, L, split):
     """Token shards of whole 64-token blocks (uneven at L = 300: 192 + 108)
     through the linears, head shards through self-attention: every output
-    row equals the one-GPU block's bit for bit."""
+    row equals the one-GPU block's bit for bit.  With `split` the attention
+    runs as two launches and each returns its rows in its own all-to-all,
+    the first under the second launch."""
     import torch.multiprocessing as mp
 
-    mp.start_processes(_a2a_rank, args=(2, _free_port(), str(tmp_path), L), nprocs=2,
+    mp.start_processes(_a2a_rank, args=(2, _free_port(), str(tmp_path), L, split), nprocs=2,
                        start_method="spawn", join=True)
     plan = db.shard_plan(SMALL, 1, 0)
     w = db.make_weights(SMALL, plan, seed=3, device="cuda")
