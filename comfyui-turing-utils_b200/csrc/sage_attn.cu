@@ -30,10 +30,11 @@
 // thread's barrier wait drains the tensor pipe (it is ordered after the
 // shared-memory operand reads of the MMAs before it), so each tile has its
 // own issuer and one issuer's waits overlap the other's MMAs.
-// For a full block with an established reference point the softmax takes
-// the exponentials first and the row max in the same pass (the reference
-// rarely moves); a block whose max does move is read again from TMEM and
-// redone after the rescale.
+// For a full block with an established reference point the Sage softmax
+// takes the exponentials first and the row max in the same pass (the lazy
+// reference rarely moves); a block whose max does move is read again from
+// TMEM and redone after the rescale.  W8A8, whose exact running max moves
+// often, always takes the row max first.
 // TMEM columns: O0 [0,128) O1 [128,256) and S(t, b) at 256 + 128 t + 64 b;
 // P_t(j) is written as packed 16-bit pairs over the first 32 columns of its
 // S buffer.
@@ -535,12 +536,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool done = false;
       bool need_rescale = false;  // some row of the warp moved its reference point
       float f = 1.0f;             // this row's rescale factor 2^(m_old - m_new)
-      if (all_full && __all_sync(0xffffffffu, m_ref != -INFINITY)) {
+      // Sage only: W8A8's exact running max moves in about a quarter of the
+      // warp-blocks (any of 32 rows finding a new maximum), and redoing those
+      // blocks costs more than taking the row max first every time
+      // (configs[1]: 20.7 against 23.4 ms).
+      if (!W8A8 && all_full && __all_sync(0xffffffffu, m_ref != -INFINITY)) {
         // Usual case: the reference point stands, so the exponentials need
-        // not wait for the row max.  If any row's max moved past it (W8A8:
-        // past the exact running max, so P stays <= 255 and the codes are
-        // the reference's), the scores are read again and the block takes
-        // the general path.
+        // not wait for the row max.  If any row's max moved past it, the
+        // scores are read again and the block takes the general path.
         const float bb = W8A8 ? -m_ref : fmaf(-12582912.0f, c, -m_ref);
         const int mx = exp_block_max<TV, kSplitLd, W8A8>(v, cx2, f2_pack(bb, bb), sum2);
         hi_pending = false;
