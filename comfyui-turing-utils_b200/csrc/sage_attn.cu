@@ -557,24 +557,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!done) {
-        if (hi_pending) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
-        if (!all_full) {
-          // Ragged last block or causal diagonal: masked keys never win the
-          // max and get p = 0 below.
-#pragma unroll
-          for (int i = 0; i < kBlockN; ++i)
-            if (i >= valid) v[i] = static_cast<uint32_t>(INT32_MIN);
-        }
-        // Row max (integer max, then one multiply).
-        int a[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        // Row max (integer max, then one multiply), over 16 columns at a
+        // time; on a full block the first 32 columns while the last 32 load.
+        auto max16 = [&](int q) {
           const uint32_t* w = v + 16 * q;
           int m = static_cast<int>(w[0]);
 #pragma unroll
           for (int i = 1; i < 15; i += 2)
             m = __vimax3_s32(m, static_cast<int>(w[i]), static_cast<int>(w[i + 1]));
-          a[q] = max(m, static_cast<int>(w[15]));
+          return max(m, static_cast<int>(w[15]));
+        };
+        int a[4];
+        if (all_full) {
+          a[0] = max16(0);
+          a[1] = max16(1);
+          if (hi_pending) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          a[2] = max16(2);
+          a[3] = max16(3);
+        } else {
+          if (hi_pending) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
+          // Ragged last block or causal diagonal: masked keys never win the
+          // max and get p = 0 below.
+#pragma unroll
+          for (int i = 0; i < kBlockN; ++i)
+            if (i >= valid) v[i] = static_cast<uint32_t>(INT32_MIN);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) a[q] = max16(q);
         }
         const int mx = max(__vimax3_s32(a[0], a[1], a[2]), a[3]);
         // W8A8 keeps the reference's offset point fma(max, c, -log2 255).
