@@ -25,6 +25,13 @@
 // holds elements l + 16 j; stages S=16 and S=64 then also run in registers.
 // The rotated row is kept as bf16 in shared memory (never in HBM) until the
 // row scale is known; the quantized codes leave as 16-byte coalesced stores.
+// The single-pass form processes rows in pairs (convrot_rowpair_kernel): each
+// fp32 value of row A shares a 64-bit register with the same column of row B,
+// so every packed f32x2 add / sub / mul does one butterfly step for both rows.
+// The 256-point transform is then bound by the FP32 pipe: 14 operations per
+// element (four radix-4 stages of 2 + 4 x 3 adds / subs and 4 halvings per 4
+// values), which a packed instruction issues in one slot but occupies for two
+// pipe cycles.
 #include <mutex>
 
 #include "tb_capi_internal.h"
@@ -437,6 +444,292 @@ __global__ void __launch_bounds__(512) convrot_rowbuffer_kernel(RowQuantParams p
   }
 }
 
+// ---------------------------------------------------------------------------
+// Row-pair form of the single-pass kernel: the same arithmetic, two rows per
+// packed register.  Every fp32 value lives in a 64-bit register pair whose
+// low half is row A's element and whose high half is row B's element at the
+// same column, so each add.rn / sub.rn / mul.rn.f32x2 performs one butterfly
+// operation for both rows and the pairing never changes between stages (no
+// register moves to re-pair values).  A half-warp owns one 256-group of both
+// rows; the two half-warps of a warp own neighbouring groups.
+//
+// Shared layout: the rotated row pair as bf16x2 words (word x = column x,
+// low half row A, high half row B), 16-byte chunks XOR-swizzled inside each
+// 128-byte line so that the phase-1 word stores and the phase-2 16-byte reads
+// are both free of bank conflicts; then one 2 KB transpose buffer per
+// half-warp (16 x 16 eight-byte units, chunks swizzled); then the per-row
+// absmax words.
+
+// Word index -> swizzled word index of the row-pair buffer.  Inside a
+// 128-byte line (32 words, 8 chunks) chunk c is stored at c ^ f(line), with
+// f taking line bits 0-1 (spreads four consecutive lines read by eight
+// consecutive phase-2 threads) and line bit 3 (separates the two half-warps,
+// whose groups are 8 lines apart).
+__device__ __forceinline__ int pair_swizzle(int x) {
+  const int line = x >> 5;
+  const int f = (line & 3) | ((line >> 1) & 4);
+  return (line << 5) | ((((x >> 2) & 7) ^ f) << 2) | (x & 3);
+}
+
+__device__ __forceinline__ void bfly4_pair(uint64_t& x0, uint64_t& x1, uint64_t& x2,
+                                           uint64_t& x3) {
+  const uint64_t s01 = padd(x0, x1);
+  const uint64_t d01 = psub(x0, x1);
+  const uint64_t y0 = phalf(psub(padd(s01, x2), x3));
+  const uint64_t y1 = phalf(padd(psub(s01, x2), x3));
+  const uint64_t y2 = phalf(padd(padd(d01, x2), x3));
+  const uint64_t y3 = phalf(padd(psub(x2, d01), x3));
+  x0 = y0;
+  x1 = y1;
+  x2 = y2;
+  x3 = y3;
+}
+
+// Full 256-point rotation of one group of both rows.  On entry lane l holds
+// elements 16 l + j in v[j]; on exit it holds elements l + 16 j.
+__device__ __forceinline__ void rotate_group_pair(uint64_t (&v)[16], uint64_t* __restrict__ tb,
+                                                  int l) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) bfly4_pair(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) bfly4_pair(v[p], v[p + 4], v[p + 8], v[p + 12]);
+  // Transpose: row l of the 16 x 16 unit matrix is written as 8 chunks of 16
+  // bytes, chunk c at c ^ (l & 7) (eight lanes of a 16-byte store phase hit
+  // eight different chunks); column l is read back unit by unit (sixteen
+  // lanes read one whole 128-byte row).
+  uint4* row = reinterpret_cast<uint4*>(tb + 16 * l);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t a0, a1, b0, b1;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(a0), "=r"(a1) : "l"(v[2 * c]));
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(b0), "=r"(b1) : "l"(v[2 * c + 1]));
+    row[c ^ (l & 7)] = make_uint4(a0, a1, b0, b1);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = tb[16 * j + 2 * ((l >> 1) ^ (j & 7)) + (l & 1)];
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) bfly4_pair(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) bfly4_pair(v[p], v[p + 4], v[p + 8], v[p + 12]);
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// Both 16-bit halves of d2 widened to fp32 and added to 1.5 * 2^23 in one
+// mixed-precision add each (add.rn.f32.{bf16,f16}: the exact widening, then
+// the fp32 round-to-nearest add), equal to widening first and adding after.
+template <typename T>
+__device__ __forceinline__ void add_magic_pair(uint32_t d2, float& lo, float& hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.bf16 %0, l, %3;\n\tadd.rn.f32.bf16 %1, h, %3;\n\t}"
+        : "=f"(lo), "=f"(hi) : "r"(d2), "f"(12582912.0f));
+  } else {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+        : "=f"(lo), "=f"(hi) : "r"(d2), "f"(12582912.0f));
+  }
+}
+
+// Four consecutive columns of a row pair (h[i] = column i, low half row A)
+// quantized to INT8: row A's four codes in `a`, row B's in `b`.  The
+// arithmetic per value is quantize16_store's INT8 branch: T(v * rcp), the
+// 16-bit pair clamp to [-128, 127], then the 1.5 * 2^23 rounding add.
+template <typename T>
+__device__ __forceinline__ void quantize4_pair_i8(const uint4& h4, uint64_t rcp2, uint32_t& a,
+                                                  uint32_t& b) {
+  const uint32_t h[4] = {h4.x, h4.y, h4.z, h4.w};
+  uint32_t ca[4], cb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lo, hi;
+    unpk(pmul(pk(elem_to_f32<T>(h[i] & 0xffffu), elem_to_f32<T>(h[i] >> 16)), rcp2), lo, hi);
+    const uint32_t d2 = clamp_pair_i8<T>(pack2_elem<T>(lo, hi));
+    add_magic_pair<T>(d2, lo, hi);
+    ca[i] = __float_as_uint(lo);
+    cb[i] = __float_as_uint(hi);
+  }
+  a = __byte_perm(__byte_perm(ca[0], ca[1], 0x0040), __byte_perm(ca[2], ca[3], 0x0040), 0x5410);
+  b = __byte_perm(__byte_perm(cb[0], cb[1], 0x0040), __byte_perm(cb[2], cb[3], 0x0040), 0x5410);
+}
+
+// INT4 form: clamp(rint(v * (1 / scale)), -7, 7) per value as
+// quantize16_store's INT4 branch; four nibbles per row (low nibble = even
+// column) in the low 16 bits of `a` and `b`.
+template <typename T>
+__device__ __forceinline__ void quantize4_pair_i4(const uint4& h4, uint64_t inv2, uint32_t& a,
+                                                  uint32_t& b) {
+  const uint32_t h[4] = {h4.x, h4.y, h4.z, h4.w};
+  a = 0u;
+  b = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float lo, hi;
+    unpk(pmul(pk(elem_to_f32<T>(h[i] & 0xffffu), elem_to_f32<T>(h[i] >> 16)), inv2), lo, hi);
+    const int qa = __float2int_rn(fminf(7.0f, fmaxf(-7.0f, lo)));
+    const int qb = __float2int_rn(fminf(7.0f, fmaxf(-7.0f, hi)));
+    a |= (static_cast<uint32_t>(qa) & 0xfu) << (4 * i);
+    b |= (static_cast<uint32_t>(qb) & 0xfu) << (4 * i);
+  }
+}
+
+// rows_per_cta = 2 * row pairs.  Warp items are (row pair, group pair); the
+// odd last row of the tensor is paired with itself and its B half dropped.
+template <typename T, int ACT, bool INT4, bool STAGED_SCALE>
+__global__ void __launch_bounds__(512, 2)
+    convrot_rowpair_kernel(RowQuantParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int R = p.rows_per_cta;
+  const int k = p.k;
+  const int groups = k / kGroup;
+  const int gpairs = (groups + 1) >> 1;
+  const int warps = blockDim.x >> 5;
+  uint32_t* rowbuf = reinterpret_cast<uint32_t*>(smem);
+  uint64_t* tb_all = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(R / 2) * k * 4);
+  unsigned int* row_amax = reinterpret_cast<unsigned int*>(tb_all + warps * 2 * 256);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int half = (tid >> 4) & 1;
+  const int l = tid & 15;
+  const int row0 = blockIdx.x * R;
+  const int rows_here = min(R, p.rows - row0);
+  const int pairs_here = (rows_here + 1) >> 1;
+  const int in_width = ACT == kActSwiGLU ? 2 * k : k;
+  const T* in = static_cast<const T*>(p.input);
+  uint64_t* tb = tb_all + (warp * 2 + half) * 256;
+  int lane_sw[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) lane_sw[c] = 4 * ((l >> 2) ^ c) + (l & 3);
+
+  for (int r = tid; r < R; r += blockDim.x) row_amax[r] = 0u;
+  __syncthreads();
+
+  // (row pair, group pair) of this warp's item, advanced by `warps` items per
+  // iteration without a division.
+  const int items = pairs_here * gpairs;
+  int ip = 0, igp = warp;
+  while (igp >= gpairs) {
+    igp -= gpairs;
+    ++ip;
+  }
+  for (int item = warp; item < items; item += warps) {
+    const int rp = ip;
+    const int g = 2 * igp + half;
+    igp += warps;
+    while (igp >= gpairs) {
+      igp -= gpairs;
+      ++ip;
+    }
+    const bool active = g < groups;
+    const bool has_b = 2 * rp + 1 < rows_here;
+    const int gl = active ? g : groups - 1;
+    const T* row_a = in + static_cast<int64_t>(row0 + 2 * rp) * in_width;
+    const T* row_b = has_b ? row_a + in_width : row_a;
+    const int col = gl * kGroup + 16 * l;
+    float fa[16], fb[16];
+    load16<T, ACT>(row_a, k, col, fa);
+    load16<T, ACT>(row_b, k, col, fb);
+    uint64_t v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = pk(fa[j], fb[j]);
+    rotate_group_pair(v, tb, l);
+    float am_a = 0.0f, am_b = 0.0f;
+    // pair_swizzle(rp * k + g * 256 + l + 16 j), spelled out: the group
+    // starts on line L0 (a multiple of 8), element l + 16 j sits on line
+    // L0 + j / 2 in chunk l / 4 + 4 (j % 2), and f(line) = (j / 2) % 4 plus 4
+    // times bit 3 of L0.  So the word is L0 * 32 + 32 (j / 2) + lane_sw[(j / 2)
+    // % 4] + 16 ((j % 2) ^ b3), with lane_sw[c] = 4 ((l / 4) ^ c) + l % 4.
+    const int line0 = (rp * k + g * kGroup) >> 5;
+    const int b3 = (line0 >> 3) & 1;
+    uint32_t* dst_even = rowbuf + line0 * 32 + 16 * b3;
+    uint32_t* dst_odd = rowbuf + line0 * 32 + 16 * (b3 ^ 1);
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      float a0, b0, a1, b1;
+      unpk(v[j], a0, b0);
+      unpk(v[j + 1], a1, b1);
+      am_a = max3f(am_a, fabsf(a0), fabsf(a1));
+      am_b = max3f(am_b, fabsf(b0), fabsf(b1));
+      if (active) {
+        const int off = 32 * (j >> 1) + lane_sw[(j >> 1) & 3];
+        dst_even[off] = pack2_elem<T>(a0, b0);
+        dst_odd[off] = pack2_elem<T>(a1, b1);
+      }
+    }
+    // Non-negative floats order like their bit patterns; both half-warps
+    // hold the same row pair, so one warp-wide maximum serves both.
+    const uint32_t wa = warp_max_u32(active ? __float_as_uint(am_a) : 0u);
+    const uint32_t wb = warp_max_u32(active ? __float_as_uint(am_b) : 0u);
+    if (tid % 32 == 0) {
+      atomicMax(&row_amax[2 * rp], wa);
+      if (has_b) atomicMax(&row_amax[2 * rp + 1], wb);
+    }
+  }
+  __syncthreads();
+  float* row_rcp = reinterpret_cast<float*>(row_amax);
+  for (int r = tid; r < rows_here; r += blockDim.x) {
+    const float scale = row_scale_from_amax<T, INT4, STAGED_SCALE>(__uint_as_float(row_amax[r]));
+    p.scales[row0 + r] = scale;
+    row_rcp[r] = INT4 ? __frcp_rn(scale) : __frcp_rn(round_to_elem<T>(scale));
+  }
+  __syncthreads();
+
+  // Phase 2: sixteen columns of one row pair per thread per iteration.
+  const int cpr = k / 16;
+  const int chunks = pairs_here * cpr;
+  int cr = 0, cc = tid;
+  while (cc >= cpr) {
+    cc -= cpr;
+    ++cr;
+  }
+  for (int c = tid; c < chunks; c += blockDim.x) {
+    const int rp = cr;
+    const int col = cc * 16;
+    cc += blockDim.x;
+    while (cc >= cpr) {
+      cc -= cpr;
+      ++cr;
+    }
+    const bool has_b = 2 * rp + 1 < rows_here;
+    const float rcp_a = row_rcp[2 * rp];
+    const float rcp_b = has_b ? row_rcp[2 * rp + 1] : rcp_a;
+    const int xb = rp * k + col;
+    const uint64_t rcp2 = pk(rcp_a, rcp_b);
+    const int64_t row_a = row0 + 2 * rp;
+    uint32_t oa[4], ob[4];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint4 q = *reinterpret_cast<const uint4*>(rowbuf + pair_swizzle(xb + 4 * s));
+      if constexpr (INT4) quantize4_pair_i4<T>(q, rcp2, oa[s], ob[s]);
+      else quantize4_pair_i8<T>(q, rcp2, oa[s], ob[s]);
+    }
+    if constexpr (INT4) {
+      const uint2 a = make_uint2(oa[0] | (oa[1] << 16), oa[2] | (oa[3] << 16));
+      const uint2 b = make_uint2(ob[0] | (ob[1] << 16), ob[2] | (ob[3] << 16));
+      int8_t* dst = p.output + row_a * (k / 2) + col / 2;
+      *reinterpret_cast<uint2*>(dst) = a;
+      if (has_b) *reinterpret_cast<uint2*>(dst + k / 2) = b;
+    } else {
+      int8_t* dst = p.output + row_a * k + col;
+      *reinterpret_cast<uint4*>(dst) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+      if (has_b) *reinterpret_cast<uint4*>(dst + k) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+    }
+  }
+}
+
 // Staged form, pass 1: rotate, write the rotated T values to the global
 // scratch and one fp32 absmax per (row, group) (convrot_quant.cu:158-211).
 template <typename T, int ACT>
@@ -527,9 +820,51 @@ RowbufferLaunch plan_rowbuffer(int k) {
   return L;
 }
 
+// Row-pair kernel plan: enough row pairs per CTA for about max_warps warp
+// items, warps balanced over the items, shared memory = the bf16x2 row-pair
+// buffer + 4 KB of transpose buffers per warp + the row absmax words.
+// Returns false when that does not fit in one CTA's shared memory.  The plain
+// rotation runs best with up to 8 warps per CTA (more, smaller CTAs per SM
+// overlap one CTA's loads with another's arithmetic: 380 vs 407 us at
+// 75600 x 5120 on a B200); the fused activations, whose tanhf / expf make
+// them arithmetic-bound, with up to 16.
+bool plan_rowpair(int k, RowbufferLaunch& L, int max_warps) {
+  const int groups = k / kGroup;
+  const int gpairs = (groups + 1) / 2;
+  int pairs = gpairs >= max_warps ? 1 : max_warps / gpairs;
+  while (pairs > 1 && static_cast<size_t>(pairs) * k * 4 > 64 * 1024) pairs >>= 1;
+  const int items = pairs * gpairs;
+  const int iters = (items + max_warps - 1) / max_warps;
+  const int warps = (items + iters - 1) / iters;
+  L.rows_per_cta = 2 * pairs;
+  L.threads = warps * 32;
+  L.smem = static_cast<size_t>(pairs) * k * 4 + static_cast<size_t>(warps) * 4096 +
+           static_cast<size_t>(2 * pairs) * 4;
+  return L.smem <= 200 * 1024;
+}
+
 template <typename T, int ACT, bool INT4, bool STAGED_SCALE>
 void launch_rowbuffer_t(const void* input, int rows, int k, int8_t* out, float* scales,
                         cudaStream_t stream) {
+  RowbufferLaunch P;
+  if (plan_rowpair(k, P, ACT == kActNone ? 8 : 16)) {
+    RowQuantParams p{};
+    p.input = input;
+    p.output = out;
+    p.scales = scales;
+    p.rows = rows;
+    p.k = k;
+    p.rows_per_cta = P.rows_per_cta;
+    auto kernel = convrot_rowpair_kernel<T, ACT, INT4, STAGED_SCALE>;
+    if (P.smem > 48 * 1024) {
+      TB_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(P.smem)));
+    }
+    const int grid = (rows + P.rows_per_cta - 1) / P.rows_per_cta;
+    kernel<<<grid, P.threads, P.smem, stream>>>(p);
+    TB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   RowbufferLaunch L = plan_rowbuffer(k);
   RowQuantParams p{};
   p.input = input;

@@ -126,3 +126,56 @@ def test_no_watchdog_errors():
     from comfyui_turing_utils_kernel import _lib
 
     assert _lib.device_error() == 0
+
+
+GOLDEN = __import__("pathlib").Path(__file__).parent / "golden"
+
+
+def _fixture(name):
+    path = GOLDEN / f"{name}.npz"
+    if not path.exists():
+        pytest.skip(f"golden fixture {name} not present")
+    return dict(np.load(path))
+
+
+@pytest.mark.parametrize("name", ["plain_5120", "plain_256", "edge_512"])
+def test_plain_matches_reference_kernel_outputs(name):
+    """Codes and scale bits equal the reference kernel's own outputs
+    (convrot_quant.cu:350-444 run on a B200 by tests/golden/make_golden.py)."""
+    from conftest import from_bits
+
+    f = _fixture(f"convrot_{name}")
+    x = from_bits(f["x"]).cuda()
+    for int4, tag in ((False, "8"), (True, "4")):
+        fn = kernel.turing_bf16_int4_convrot_quantize if int4 else kernel.turing_bf16_int8_convrot_quantize
+        q, s = fn(x)
+        assert np.array_equal(q.cpu().numpy(), f[f"q{tag}"])
+        assert np.array_equal(s.cpu().numpy().reshape(-1).view(np.uint32),
+                              f[f"s{tag}"].reshape(-1).view(np.uint32))
+
+
+@pytest.mark.parametrize("name,act", [("gelu_13824", "gelu"), ("swiglu_5376", "swiglu")])
+def test_fused_activation_matches_reference_kernel_outputs(name, act):
+    """Row-buffer, staged and staged-fp16 forms with the fused activation:
+    codes and scale bits equal the reference kernel's outputs, since both call
+    CUDA's expf / tanhf on the same operation tree (convrot_quant.cu:137-291)."""
+    from conftest import from_bits
+
+    f = _fixture(f"convrot_{name}")
+    x = from_bits(f["x"]).cuda()
+    x16 = x.float().to(torch.float16)
+    for int4, tag in ((False, "8"), (True, "4")):
+        if act == "gelu":
+            row = kernel.turing_bf16_gelu_int4_convrot_quantize if int4 else kernel.turing_bf16_gelu_int8_convrot_quantize
+            staged = kernel.turing_gelu_int4_convrot_quantize if int4 else kernel.turing_gelu_int8_convrot_quantize
+            row_out = row(x)
+        else:
+            row = kernel.turing_bf16_int4_convrot_quantize if int4 else kernel.turing_bf16_int8_convrot_quantize
+            staged = kernel.turing_swiglu_int4_convrot_quantize if int4 else kernel.turing_swiglu_int8_convrot_quantize
+            row_out = row(x, 256, swiglu=True)
+        for (q, s), key in ((row_out, ""), (staged(x), f"_staged_{tag}"), (staged(x16), f"_staged16_{tag}")):
+            qk = f"q{tag}" if key == "" else f"q{key}"
+            sk = f"s{tag}" if key == "" else f"s{key}"
+            assert np.array_equal(q.cpu().numpy(), f[qk]), (qk, int(np.sum(q.cpu().numpy() != f[qk])))
+            assert np.array_equal(s.cpu().numpy().reshape(-1).view(np.uint32),
+                                  f[sk].reshape(-1).view(np.uint32)), sk
