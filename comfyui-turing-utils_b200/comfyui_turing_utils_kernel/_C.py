@@ -344,6 +344,26 @@ def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, out
     return out
 
 
+def gated_residual_add_(x, y, gate=None):
+    """x = bf16(x + y * gate) in place (gate [cols] or None), fp32 arithmetic
+    with one rounding per operation: the DiT block's residual, which the model
+    code around the plugin runs as ``x.addcmul_(y, gate)``.  Not a reference
+    binding; x and y are bf16 row blocks with unit column stride."""
+    _check(x.is_cuda and y.is_cuda, "gated_residual_add_: x and y must be CUDA tensors")
+    _check(x.dtype == torch.bfloat16 and y.dtype == torch.bfloat16,
+           "gated_residual_add_: x and y must be bfloat16")
+    _check(x.dim() == 2 and x.shape == y.shape, "gated_residual_add_: x and y must be 2D, same shape")
+    _check(x.stride(1) == 1 and y.stride(1) == 1, "gated_residual_add_: unit column stride required")
+    if gate is not None:
+        _check(gate.dtype == torch.bfloat16 and gate.numel() == x.size(1),
+               "gated_residual_add_: gate must be bfloat16 with one value per column")
+        gate = gate.reshape(-1).contiguous()
+    with torch.cuda.device(x.device):
+        call("tb_gated_residual_add", ptr(x), x.stride(0), ptr(y), y.stride(0), ptr(gate),
+             x.size(0), x.size(1), stream_of(x))
+    return x
+
+
 # ---------------------------------------------------------- ConvRot quantizers
 
 def _rowbuffer(input, group_size, swiglu, int4, gelu, forced_threads=0):

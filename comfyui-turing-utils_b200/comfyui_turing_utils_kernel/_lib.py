@@ -58,6 +58,7 @@ SIGNATURES: dict[str, list] = {
                                 _int, _int, _p],
     "tb_int8_gemm_s32": [_p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "tb_dequantize_int8_bf16": [_p, _i64, _p, _p, _i64, _p, _i64, _i64, _p],
+    "tb_gated_residual_add": [_p, _i64, _p, _i64, _p, _i64, _i64, _p],
     "tb_quant_per_block_int8": [_p, _int, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int,
                                 _int, _p, _p],
     "tb_quant_per_warp_int8": [_p, _int, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _int,

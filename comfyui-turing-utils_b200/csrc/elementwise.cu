@@ -4,7 +4,10 @@
 //   * grouped-codebook W4 -> INT8 decode (kernel/csrc/turing/w4a8.cu:907-973):
 //       w8 = clamp(rint(codebook[idx] * e4m3(group_scale)), -127, 127);
 //   * signed 4-bit -> INT8 unpack for the W4A8 and W4A4 linears
-//     (w4a8.cu:34-72): low nibble = even column, two's-complement nibbles.
+//     (w4a8.cu:34-72): low nibble = even column, two's-complement nibbles;
+//   * the DiT block's gated residual add, x = bf16(x + y * gate[col]) in
+//     fp32 with one rounding per operation (what `x.addcmul_(y, gate)` on
+//     bf16 tensors computes), in place.
 // All move 16-byte vectors per thread with grid-stride loops sized to the SM
 // count.
 #include <cuda_fp8.h>
@@ -139,6 +142,44 @@ __global__ void __launch_bounds__(256) unpack_s4_kernel(const uint2* __restrict_
   }
 }
 
+// x[r, c] = bf16_rn(fp32(x) + fp32(y) * fp32(gate[c])) (product and sum each
+// rounded to fp32), or bf16_rn(fp32(x) + fp32(y)) without a gate; 8 columns
+// (16 bytes) per thread and step.
+template <bool GATED>
+__global__ void __launch_bounds__(256) gated_residual_kernel(uint16_t* __restrict__ x,
+                                                             int64_t x_stride,
+                                                             const uint16_t* __restrict__ y,
+                                                             int64_t y_stride,
+                                                             const uint16_t* __restrict__ gate,
+                                                             unsigned int rows,
+                                                             unsigned int vpr) {
+  const unsigned int total = rows * vpr;
+  for (unsigned int v = blockIdx.x * blockDim.x + threadIdx.x; v < total;
+       v += gridDim.x * blockDim.x) {
+    const unsigned int row = v / vpr;
+    const unsigned int col = (v - row * vpr) * 8;
+    uint4* px = reinterpret_cast<uint4*>(x + row * x_stride + col);
+    const uint4 a = *px;
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(y + row * y_stride + col));
+    uint4 g = make_uint4(0u, 0u, 0u, 0u);
+    if (GATED) g = __ldg(reinterpret_cast<const uint4*>(gate + col));
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+    const uint32_t wg[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float lo = bf16_bits_to_f32(wb[i] & 0xffffu), hi = bf16_bits_to_f32(wb[i] >> 16);
+      if (GATED) {
+        lo = __fmul_rn(lo, bf16_bits_to_f32(wg[i] & 0xffffu));
+        hi = __fmul_rn(hi, bf16_bits_to_f32(wg[i] >> 16));
+      }
+      o[i] = pack_bf16x2(__fadd_rn(bf16_bits_to_f32(wa[i] & 0xffffu), lo),
+                         __fadd_rn(bf16_bits_to_f32(wa[i] >> 16), hi));
+    }
+    *px = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 int grid_for(int64_t work_items, int threads) {
   int64_t blocks = (work_items + threads - 1) / threads;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * 16;
@@ -181,6 +222,32 @@ void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
   const int grid = grid_for(static_cast<int64_t>(rows) * (k / 16), 256);
   codebook_decode_kernel<<<grid, 256, 0, stream>>>(packed, group_scale, codebook, out, rows, k,
                                                    group_size);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+void gated_residual_launch(void* x, int64_t x_stride, const void* y, int64_t y_stride,
+                           const void* gate, int64_t rows, int64_t cols, cudaStream_t stream) {
+  TB_REQUIRE(cols % 8 == 0 && x_stride % 8 == 0 && y_stride % 8 == 0,
+             "gated residual add needs columns and row strides divisible by 8");
+  TB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(y) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(gate) & 15u) == 0,
+             "gated residual add needs 16-byte aligned x, y and gate");
+  TB_REQUIRE(rows * (cols / 8) <= INT32_MAX, "gated residual add exceeds the kernel range");
+  const int64_t n_vec = rows * (cols / 8);
+  if (n_vec == 0) return;
+  const int grid = grid_for(n_vec, 256);
+  auto* xb = static_cast<uint16_t*>(x);
+  auto* yb = static_cast<const uint16_t*>(y);
+  auto* gb = static_cast<const uint16_t*>(gate);
+  if (gate != nullptr)
+    gated_residual_kernel<true><<<grid, 256, 0, stream>>>(xb, x_stride, yb, y_stride, gb,
+                                                          static_cast<unsigned int>(rows),
+                                                          static_cast<unsigned int>(cols / 8));
+  else
+    gated_residual_kernel<false><<<grid, 256, 0, stream>>>(xb, x_stride, yb, y_stride, gb,
+                                                           static_cast<unsigned int>(rows),
+                                                           static_cast<unsigned int>(cols / 8));
   TB_CUDA_CHECK(cudaGetLastError());
 }
 

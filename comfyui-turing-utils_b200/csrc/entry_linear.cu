@@ -14,6 +14,8 @@ void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
                             cudaStream_t stream);
 void unpack_s4_launch(const int8_t* packed, int8_t* out, int64_t rows, int64_t k,
                       cudaStream_t stream);
+void gated_residual_launch(void* x, int64_t x_stride, const void* y, int64_t y_stride,
+                           const void* gate, int64_t rows, int64_t cols, cudaStream_t stream);
 void sage_quant_launch(const void* input, int dtype, int8_t* out, float* scale, int64_t B,
                        int64_t H, int64_t L, int64_t D, int64_t sb, int64_t sh, int64_t sl,
                        int tile, int64_t num_tiles, int layout, const void* mean,
@@ -71,6 +73,19 @@ int tb_dequantize_int8_bf16(const int32_t* accumulator, int64_t acc_stride,
     tb::dequant_launch(accumulator, acc_stride, activation_scale, weight_scale,
                        weight_scale_numel == 1, output, static_cast<int>(rows),
                        static_cast<int>(cols), static_cast<cudaStream_t>(stream));
+  });
+}
+
+int tb_gated_residual_add(void* x, int64_t x_stride, const void* y, int64_t y_stride,
+                          const void* gate, int64_t rows, int64_t cols, tb_stream_t stream) {
+  return guarded([&] {
+    TB_REQUIRE(x && y, "gated residual add: x and y must be CUDA tensors");
+    TB_REQUIRE(rows >= 0 && cols >= 0 && x_stride >= cols && y_stride >= cols,
+               "gated residual add: invalid shape or strides");
+    if (rows == 0 || cols == 0) return;
+    tb::require_sm100();
+    tb::gated_residual_launch(x, x_stride, y, y_stride, gate, rows, cols,
+                              static_cast<cudaStream_t>(stream));
   });
 }
 

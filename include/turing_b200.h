@@ -257,6 +257,16 @@ TB_API int tb_layer_norm_adaln(const void *input, const void *scale, const void 
 TB_API int tb_int8_gemm_s32(const int8_t *activation, const int8_t *weight, int32_t *accumulator,
                      int64_t m, int64_t n, int64_t k, int64_t acc_stride, tb_stream_t stream);
 
+/* Gated residual add of the DiT block, in place on bf16 rows:
+ * x[r, c] = bf16(x[r, c] + y[r, c] * gate[c]) with the product and the sum
+ * each rounded to fp32 (gate == NULL: x[r, c] = bf16(x + y)).  x, y and gate
+ * 16-byte aligned, cols and both row strides (elements) multiples of 8.  No
+ * reference counterpart: the model code around the plugin runs this as
+ * torch's `x.addcmul_(y, gate)` on bf16 tensors. */
+TB_API int tb_gated_residual_add(void *x, int64_t x_stride, const void *y, int64_t y_stride,
+                                 const void *gate, int64_t rows, int64_t cols,
+                                 tb_stream_t stream);
+
 /* INT32 -> BF16 dequant epilogue: out[r, c] = bf16((acc[r, c] * a_s[r]) * w_s[c])
  * (w_s scalar when weight_scale_numel == 1).  Replaces kernel_api.h:37-40
  * turing_dequantize_int8_bf16 (bf16_epilogue.cu:147-218). */

@@ -254,3 +254,26 @@ def test_all_to_all_two_gpus_equals_one_gpu(tmp_path, L, split):
     for r in range(2):
         (t0, t1), out = torch.load(tmp_path / f"a2a{r}.pt")
         assert torch.equal(out, single[t0:t1]), (r, (out.float() - single[t0:t1].float()).abs().max())
+
+
+@pytest.mark.parametrize("gated", [True, False])
+def test_gated_residual_add_kernel(gated):
+    """tb_gated_residual_add on a row block of a larger tensor: equal bit for
+    bit to bf16(x + y * gate) with fp32 product and sum, each rounded once."""
+    from comfyui_turing_utils_kernel import _C
+
+    g = torch.Generator(device="cuda").manual_seed(77)
+    big = torch.randn((700, 5120), generator=g, device="cuda").to(torch.bfloat16)
+    x = big[100:400]
+    y = (torch.randn((300, 5120), generator=g, device="cuda") * 3).to(torch.bfloat16)
+    gate = torch.randn((5120,), generator=g, device="cuda").to(torch.bfloat16) if gated else None
+    want = (x.float() + (y.float() * gate.float() if gated else y.float())).to(torch.bfloat16)
+    untouched = big[:100].clone(), big[400:].clone()
+    torch_form = x.clone().addcmul_(y, gate) if gated else x.clone().add_(y)
+    _C.gated_residual_add_(x, y, gate)
+    torch.cuda.synchronize()
+    assert torch.equal(x, want)
+    assert torch.equal(big[:100], untouched[0]) and torch.equal(big[400:], untouched[1])
+    # torch's own addcmul_ may contract the multiply-add; it agrees on all but
+    # a few last-bit cases.
+    assert (x != torch_form).float().mean().item() <= 1e-3
