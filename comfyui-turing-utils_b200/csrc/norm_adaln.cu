@@ -10,7 +10,9 @@
 //     groups of ceil(sequence / steps) tokens),
 //       n = T((x - mean) * rsqrt(var + eps)),  mult = T(1 + scale),
 //       out = T(float(n) * float(mult) + shift).
-// Statistics are fp32.  One CTA per row: the row is read from HBM once into
+// Statistics are fp32.  LayerNorm rows of 256 * NV 16-bit values (NV <= 24)
+// are handled one per warp (layer_norm_adaln_warp_kernel).  Otherwise
+// one CTA per row: the row is read from HBM once into
 // shared memory (16-byte vectors when the pointers and width allow), reduced
 // by warp shuffles, and the output is formed from the staged copy, so each
 // element crosses HBM once in each direction.  LayerNorm takes its mean and
@@ -168,9 +170,161 @@ __global__ void __launch_bounds__(kNormThreads) layer_norm_adaln_kernel(
   }
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Warp-per-row form for 16-bit rows of hidden = 256 * NV: lane l loads the
+// 16-byte chunks l, l + 32, ... of the row (all in flight at once) and parks
+// them in its warp's slice of shared memory, so the row crosses HBM once in
+// each direction with no CTA barrier; statistics by warp butterflies.  Same formula as
+// layer_norm_adaln_kernel (two fp32 passes, then
+// out = T(float(T((x - mean) * inv_std)) * float(T(1 + scale)) + shift)); only
+// the summation order of the mean and variance differs.
+template <typename T>
+__device__ __forceinline__ float half_bits_to_f32(uint32_t bits16) {
+  return ld_f(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+template <>
+__device__ __forceinline__ float half_bits_to_f32<__nv_bfloat16>(uint32_t bits16) {
+  return __uint_as_float(bits16 << 16);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = half_bits_to_f32<T>(w[i] & 0xffffu);
+    f[2 * i + 1] = half_bits_to_f32<T>(w[i] >> 16);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t bits_of(T v) {
+  return static_cast<uint32_t>(*reinterpret_cast<const unsigned short*>(&v));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+constexpr int kWarpRowsPerCta = 8;
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpRowsPerCta * 32, 2) layer_norm_adaln_warp_kernel(
+    const T* __restrict__ x, const T* __restrict__ scale, const T* __restrict__ shift,
+    T* __restrict__ out, int rows, int sequence, int hidden, int steps, float eps) {
+  extern __shared__ __align__(16) unsigned char norm_smem[];
+  const int w = threadIdx.x >> 5;
+  const int row = blockIdx.x * kWarpRowsPerCta + w;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // warp-uniform
+  const int batch = row / sequence;
+  const int token = row - batch * sequence;
+  int mod_token = 0;
+  if (steps > 1) {
+    const int per = (sequence + steps - 1) / steps;
+    mod_token = min(token / max(per, 1), steps - 1);
+  }
+  // The warp's row: all NV loads of a lane in flight at once, then parked in
+  // this warp's slice of shared memory (lane-owned chunks, no other lane
+  // reads them, so no barrier beyond the warp's own program order).
+  uint4* srow = reinterpret_cast<uint4*>(norm_smem) + static_cast<size_t>(w) * NV * 32;
+  {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * hidden);
+    uint4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __ldg(xr + lane + 32 * i);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) srow[lane + 32 * i] = v[i];
+  }
+  float s = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < NV; ++i) {
+    float f[8];
+    unpack8<T>(srow[lane + 32 * i], f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += f[k];
+  }
+  const float mean = warp_sum(s) / static_cast<float>(hidden);
+  float q = 0.0f;
+#pragma unroll 4
+  for (int i = 0; i < NV; ++i) {
+    float f[8];
+    unpack8<T>(srow[lane + 32 * i], f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float d = f[k] - mean;
+      q += d * d;
+    }
+  }
+  const float var = warp_sum(q) / static_cast<float>(hidden);
+  const float inv_std = rsqrtf(var + eps);
+  const int64_t mod = (static_cast<int64_t>(batch) * steps + mod_token) * hidden;
+  const uint4* scr = reinterpret_cast<const uint4*>(scale + mod);
+  const uint4* shr = reinterpret_cast<const uint4*>(shift + mod);
+  uint4* orow = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * hidden);
+#pragma unroll 4
+  for (int i = 0; i < NV; ++i) {
+    float f[8], sc[8], sh[8];
+    unpack8<T>(srow[lane + 32 * i], f);
+    unpack8<T>(__ldg(scr + lane + 32 * i), sc);
+    unpack8<T>(__ldg(shr + lane + 32 * i), sh);
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      uint32_t pair = 0u;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const T n = st_f<T>((f[k + e] - mean) * inv_std);
+        const T mult = st_f<T>(1.0f + sc[k + e]);
+        const float result = ld_f(n) * ld_f(mult) + sh[k + e];
+        pair |= bits_of(st_f<T>(result)) << (16 * e);
+      }
+      o[k / 2] = pair;
+    }
+    orow[lane + 32 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <typename T, int NV>
+void launch_ln_warp(const void* x, const void* scale, const void* shift, void* out, int rows,
+                    int seq, int hidden, int steps, float eps, cudaStream_t stream) {
+  const int grid = (rows + kWarpRowsPerCta - 1) / kWarpRowsPerCta;
+  const size_t smem = static_cast<size_t>(kWarpRowsPerCta) * NV * 32 * 16;
+  auto kern = layer_norm_adaln_warp_kernel<T, NV>;
+  if (smem > 48 * 1024)
+    TB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem)));
+  kern<<<grid, kWarpRowsPerCta * 32, smem, stream>>>(
+      static_cast<const T*>(x), static_cast<const T*>(scale), static_cast<const T*>(shift),
+      static_cast<T*>(out), rows, seq, hidden, steps, eps);
+  TB_CUDA_CHECK(cudaGetLastError());
+}
+
+// The warp-per-row form for hidden = 256 * NV, NV in {4, 8, 12, 16, 20,
+// 24} (1024 ... 6144 columns), 16-bit types and 16-byte aligned tensors;
+// false when it does not apply.
+template <typename T>
+bool try_ln_warp(const void* x, const void* scale, const void* shift, void* out, int rows,
+                 int seq, int hidden, int steps, float eps, cudaStream_t stream) {
+  if (hidden % 256 != 0 || !aligned16(x) || !aligned16(scale) || !aligned16(shift) ||
+      !aligned16(out))
+    return false;
+  switch (hidden / 256) {
+    case 4: launch_ln_warp<T, 4>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    case 8: launch_ln_warp<T, 8>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    case 12: launch_ln_warp<T, 12>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    case 16: launch_ln_warp<T, 16>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    case 20: launch_ln_warp<T, 20>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    case 24: launch_ln_warp<T, 24>(x, scale, shift, out, rows, seq, hidden, steps, eps, stream); return true;
+    default: return false;
+  }
+}
+
 int elem_bytes(int dtype) { return dtype == TB_DTYPE_F32 ? 4 : 2; }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 template <typename T, typename K, typename... Args>
 void launch_with_smem(K kern, int rows, size_t smem, cudaStream_t stream, Args... args) {
@@ -262,6 +416,13 @@ extern "C" int tb_layer_norm_adaln(const void* input, const void* scale, const v
     const int rows = static_cast<int>(batch * sequence);
     const int seq = static_cast<int>(sequence), hd = static_cast<int>(hidden);
     const int steps = static_cast<int>(modulation_steps);
+    if (dtype == TB_DTYPE_BF16 &&
+        tb::try_ln_warp<__nv_bfloat16>(input, scale, shift, output, rows, seq, hd, steps,
+                                       epsilon, s))
+      return;
+    if (dtype == TB_DTYPE_F16 &&
+        tb::try_ln_warp<__half>(input, scale, shift, output, rows, seq, hd, steps, epsilon, s))
+      return;
     if (dtype == TB_DTYPE_BF16) {
       using T = __nv_bfloat16;
       tb::launch_with_smem<T>(tb::layer_norm_adaln_kernel<T>, rows, smem, s,
