@@ -123,7 +123,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 // One bounded probe of a barrier phase.  The suspend-time hint lets the
 // hardware park the waiting warp (it wakes when the phase completes or after
 // at most kSuspendHintNs), so waiting warps do not spin on the issue slots the
-// working warps need.
+// working warps need.  A translation unit that defines TB_TRY_WAIT_NO_HINT
+// before including this header probes without the hint (the attention kernel,
+// whose waiting warps resume sooner that way).
 constexpr uint32_t kSuspendHintNs = 1000000;  // 1 ms per probe
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
