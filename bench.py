@@ -256,6 +256,13 @@ class LinearWorkload:
         self.bias_cpu = self.bias.cpu().float()
 
 
+def _chunks(n, k):
+    """Weight chunks (decode + GEMM rounds) of a staged W4 linear."""
+    from comfyui_turing_utils_kernel._C import _weight_chunk_rows
+
+    return -(-n // _weight_chunk_rows(n, k))
+
+
 class CodebookWorkload:
     """grouped-codebook W4A8 linear.  The reference's fast
     path stores symmetric codebook weights (packed 4-bit indices, 16-entry fp32
@@ -296,7 +303,8 @@ class CodebookWorkload:
         self.codebook = (torch.arange(16, dtype=torch.float32) - 8.0).to(device)
         self.out_host = torch.empty((m, n), dtype=torch.bfloat16,
                                     pin_memory=device.type == "cuda")
-        self.launches_per_step = 1 + 2 * ((n + 4095) // 4096)
+        # quantize, then (decode, GEMM) per weight chunk
+        self.launches_per_step = 1 + 2 * _chunks(n, k)
         self.dominant = "gemm_i8"
         self.h2d_bytes = self.x_host.numel() * 2
         self.d2h_bytes = self.out_host.numel() * 2
@@ -394,9 +402,9 @@ class W4A4FFNWorkload:
         self.b_down = (torch.randn((d,), generator=g) * 0.02).to(device)
         self.out_host = torch.empty((m, d), dtype=torch.bfloat16,
                                     pin_memory=device.type == "cuda")
-        # quantize, W4A4 up (activation unpack + 4 chunks x (unpack, GEMM)), GELU
-        # quantize, W4A4 down (activation unpack + 2 chunks x (unpack, GEMM)).
-        self.launches_per_step = 1 + (1 + 2 * ((f + 4095) // 4096)) + 1 + (1 + 2 * ((d + 4095) // 4096))
+        # quantize, W4A4 up (activation unpack + (unpack, GEMM) per weight chunk),
+        # GELU quantize, W4A4 down (the same).
+        self.launches_per_step = 1 + (1 + 2 * _chunks(f, d)) + 1 + (1 + 2 * _chunks(d, f))
         self.dominant = "gemm_i8"
         self.h2d_bytes = self.x_host.numel() * 2
         self.d2h_bytes = self.out_host.numel() * 2

@@ -98,6 +98,25 @@ def _pad_k16(activation, weight_packed):
             torch.nn.functional.pad(weight_packed, (0, pad // 2)))
 
 
+# Largest expanded int8 weight chunk (bytes) a staged W4 linear decodes before
+# its GEMM.  One chunk covers every N x K of the configs (13824 x 5120 = 67.5
+# MiB), so the GEMM runs once over all N-blocks instead of ending each chunk
+# on a partial wave of tiles.
+_WEIGHT_CHUNK_BYTES = 128 << 20
+
+
+def _weight_chunk_rows(n, k):
+    """Rows of the expanded weight per decode + GEMM round: all N when N x K
+    int8 fits _WEIGHT_CHUNK_BYTES, else equal chunks rounded up to the GEMM's
+    256-column tile.  Each output column depends only on its own weight row,
+    so the chunking changes no result."""
+    if n * k <= _WEIGHT_CHUNK_BYTES:
+        return n
+    chunks = -(-(n * k) // _WEIGHT_CHUNK_BYTES)
+    rows = -(-n // chunks)
+    return min(n, -(-rows // 256) * 256)
+
+
 def _n_tail_linear(m, n, dev, run):
     """N-tail handling of bindings.cpp:205-259: the first N - N % 8 channels in
     one call, the last N % 8 channels padded with zero rows to 8 in a second,
@@ -161,7 +180,7 @@ def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=
                 w = torch.nn.functional.pad(w, (0, 0, 0, width - count))
                 ws = torch.nn.functional.pad(ws, (0, width - count))
                 b = None if b is None else torch.nn.functional.pad(b, (0, width - count))
-            rows = min(width, 4096)
+            rows = _weight_chunk_rows(width, k)
             workspace = torch.empty((rows, k), dtype=torch.int8, device=dev)
             call("tb_w4a8_linear", ptr(activation), ptr(w.contiguous()), ptr(activation_scale),
                  ptr(ws.contiguous()), ptr(None if b is None else b.contiguous()), ptr(workspace),
@@ -221,7 +240,7 @@ def turing_int4_linear(activation, weight, activation_scale, weight_scale, bias=
                 w = torch.nn.functional.pad(w, (0, 0, 0, width - count))
                 ws = torch.nn.functional.pad(ws, (0, width - count))
                 b = None if b is None else torch.nn.functional.pad(b, (0, width - count))
-            rows = min(width, 4096)
+            rows = _weight_chunk_rows(width, k)
             workspace = torch.empty((rows, k), dtype=torch.int8, device=dev)
             call("tb_int4_linear", ptr(activation), ptr(w.contiguous()), ptr(activation_scale),
                  ptr(ws.contiguous()), ptr(None if b is None else b.contiguous()),
@@ -299,7 +318,7 @@ def turing_codebook_w4a8_linear(activation, weight, activation_scale, group_scal
     _check(chunk_rows != -1 or inline_eligible,
            "forced inline codebook W4A8 requires group_size=16 and M>8192")
     if chunk_rows <= 0:
-        chunk_rows = min(n, 4096)
+        chunk_rows = _weight_chunk_rows(n, k)
     else:
         _check(chunk_rows % 8 == 0, "chunk_rows must be divisible by 8")
         chunk_rows = min(n, chunk_rows)

@@ -115,6 +115,30 @@ def test_int4_linear_on_convrot_int4_codes(oracle):
     assert np.array_equal(bf16_bits(out), _expected(oracle, a, w, s.reshape(-1).cpu(), w_s, None))
 
 
+def test_w4_linears_across_weight_chunks(oracle, monkeypatch):
+    """A chunk cap far below N x K splits the expanded weight into several
+    decode + GEMM rounds (the last one short); W4A8 and W4A4 outputs stay
+    bit-exact against the oracle."""
+    from comfyui_turing_utils_kernel import _C
+
+    monkeypatch.setattr(_C, "_WEIGHT_CHUNK_BYTES", 300 * 512)
+    m, n, k = 130, 1000, 512
+    assert _C._weight_chunk_rows(n, k) == 256
+    g = torch.Generator().manual_seed(91)
+    a = torch.randint(-7, 8, (m, k), generator=g, dtype=torch.int8)
+    w = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.5 + 0.01
+    w_s = torch.rand((n,), generator=g) * 0.03 + 0.001
+    b = (torch.randn((n,), generator=g) * 0.1).to(torch.bfloat16)
+    want = _expected(oracle, a, w, a_s, w_s, b)
+    w_p = torch.from_numpy(oracle.pack_int4(w.numpy())).cuda()
+    out = kernel.turing_w4a8_linear(a.cuda(), w_p, a_s.cuda(), w_s.cuda(), b.cuda())
+    assert np.array_equal(bf16_bits(out), want)
+    a_p = torch.from_numpy(oracle.pack_int4(a.numpy())).cuda()
+    out = kernel.turing_int4_linear(a_p, w_p, a_s.cuda(), w_s.cuda(), b.cuda())
+    assert np.array_equal(bf16_bits(out), want)
+
+
 def test_no_watchdog_errors():
     from comfyui_turing_utils_kernel import _lib
 

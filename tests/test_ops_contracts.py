@@ -273,3 +273,16 @@ def test_w8a8_attention_is_a_fullgraph_leaf():
         backend="eager", fullgraph=True)
     out = compiled(q, k, k)
     assert out.shape == q.shape and out.dtype == q.dtype
+
+
+def test_staged_w4_weight_chunks():
+    """One decode + GEMM round for every configs shape; above the cap, equal
+    chunks on the GEMM's 256-column tile that cover N."""
+    from comfyui_turing_utils_kernel._C import _WEIGHT_CHUNK_BYTES, _weight_chunk_rows
+
+    for n, k in ((5120, 5120), (13824, 5120), (5120, 13824), (8, 16)):
+        assert _weight_chunk_rows(n, k) == n
+    for n, k in ((65536, 5120), (40000, 8192), (1 << 20, 4096)):
+        rows = _weight_chunk_rows(n, k)
+        assert rows % 256 == 0 and rows * k <= _WEIGHT_CHUNK_BYTES + 256 * k
+        assert -(-n // rows) == -(-(n * k) // _WEIGHT_CHUNK_BYTES)
