@@ -585,11 +585,49 @@ __device__ __forceinline__ void quantize4_pair_i4(const uint4& h4, uint64_t inv2
   }
 }
 
+// The 16 input elements of lane l in both rows of an item, as raw 16-bit
+// pairs (two 16-byte loads per row), and their fp32 values.
+struct RawPair {
+  uint4 a0, a1, b0, b1;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_raw_pair(const T* row_a, const T* row_b, int col, RawPair& r) {
+  const uint4* pa = reinterpret_cast<const uint4*>(row_a + col);
+  const uint4* pb = reinterpret_cast<const uint4*>(row_b + col);
+  r.a0 = __ldg(pa);
+  r.a1 = __ldg(pa + 1);
+  r.b0 = __ldg(pb);
+  r.b1 = __ldg(pb + 1);
+}
+
+template <typename T>
+__device__ __forceinline__ void widen16(const uint4& lo, const uint4& hi, float (&v)[16]) {
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[2 * i] = elem_to_f32<T>(w[i] & 0xffffu);
+    v[2 * i + 1] = elem_to_f32<T>(w[i] >> 16);
+  }
+}
+
+// Launch bounds of the row-pair kernel.  The plain form runs at most 8 warps
+// per CTA and keeps the next item's loads in flight (80 registers, 3+ CTAs
+// per SM); the fused activations run up to 16 warps at 64 registers.
+template <int ACT>
+struct RowpairBounds {
+  static constexpr int kThreads = ACT == 0 ? 256 : 512;
+  static constexpr int kMinBlocks = ACT == 0 ? 3 : 2;
+};
+
 // rows_per_cta = 2 * row pairs.  Warp items are (row pair, group pair); the
 // odd last row of the tensor is paired with itself and its B half dropped.
+// Plain form: each warp loads its next item before it rotates the current
+// one, so every warp keeps one item's loads in flight behind its arithmetic.
 template <typename T, int ACT, bool INT4, bool STAGED_SCALE>
-__global__ void __launch_bounds__(512, 2)
+__global__ void __launch_bounds__(RowpairBounds<ACT>::kThreads, RowpairBounds<ACT>::kMinBlocks)
     convrot_rowpair_kernel(RowQuantParams p) {
+  constexpr bool kPrefetch = ACT == kActNone;
   extern __shared__ __align__(16) unsigned char smem[];
   const int R = p.rows_per_cta;
   const int k = p.k;
@@ -625,9 +663,30 @@ __global__ void __launch_bounds__(512, 2)
     igp -= gpairs;
     ++ip;
   }
+  // Source of item (row pair ip_, group pair igp_) for this half-warp; an
+  // inactive half (odd group count) re-reads the last group, an odd last row
+  // its own row.
+  auto item_src = [&](int ip_, int igp_, const T*& ra, const T*& rb, int& col_) {
+    const int g_ = 2 * igp_ + half;
+    ra = in + static_cast<int64_t>(row0 + 2 * ip_) * in_width;
+    rb = 2 * ip_ + 1 < rows_here ? ra + in_width : ra;
+    col_ = (g_ < groups ? g_ : groups - 1) * kGroup + 16 * l;
+  };
+  RawPair nxt;
+  if (kPrefetch && warp < items) {
+    const T* ra;
+    const T* rb;
+    int c;
+    item_src(ip, igp, ra, rb, c);
+    load_raw_pair(ra, rb, c, nxt);
+  }
   for (int item = warp; item < items; item += warps) {
     const int rp = ip;
     const int g = 2 * igp + half;
+    const T* row_a;
+    const T* row_b;
+    int col;
+    item_src(ip, igp, row_a, row_b, col);
     igp += warps;
     while (igp >= gpairs) {
       igp -= gpairs;
@@ -635,13 +694,22 @@ __global__ void __launch_bounds__(512, 2)
     }
     const bool active = g < groups;
     const bool has_b = 2 * rp + 1 < rows_here;
-    const int gl = active ? g : groups - 1;
-    const T* row_a = in + static_cast<int64_t>(row0 + 2 * rp) * in_width;
-    const T* row_b = has_b ? row_a + in_width : row_a;
-    const int col = gl * kGroup + 16 * l;
     float fa[16], fb[16];
-    load16<T, ACT>(row_a, k, col, fa);
-    load16<T, ACT>(row_b, k, col, fb);
+    if constexpr (kPrefetch) {
+      const RawPair cur = nxt;
+      if (item + warps < items) {  // warp-uniform
+        const T* ra;
+        const T* rb;
+        int c;
+        item_src(ip, igp, ra, rb, c);
+        load_raw_pair(ra, rb, c, nxt);
+      }
+      widen16<T>(cur.a0, cur.a1, fa);
+      widen16<T>(cur.b0, cur.b1, fb);
+    } else {
+      load16<T, ACT>(row_a, k, col, fa);
+      load16<T, ACT>(row_b, k, col, fb);
+    }
     uint64_t v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = pk(fa[j], fb[j]);
