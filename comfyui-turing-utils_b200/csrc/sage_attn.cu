@@ -252,13 +252,27 @@ __device__ __forceinline__ uint32_t pack_pair(uint64_t p2) {
   return r;
 }
 
-// W8A8 P code of a pair: rni_sat_u8(p) as exact fp16 values (p reaches 255.5
-// only when |m| >= 2^16).
+// W8A8 P code of a pair: rni_sat_u8(p) as exact fp16 values.  Adding and
+// subtracting 1.5 * 2^23 rounds p to the nearest integer (ties to even, as
+// rni); the saturation at 255 (p reaches 255.5 only when |m| >= 2^16) is one
+// packed fp16 min after the exact conversion of the integers <= 256.
 __device__ __forceinline__ uint32_t u8_code_pair(uint64_t p2) {
   const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
-  const uint64_t r2 = f2_add(p2, rnd2);
-  const uint64_t c2 = f2_pack(fminf(f2_lo(r2), 12583167.0f), fminf(f2_hi(r2), 12583167.0f));
-  return pack_pair<__half>(f2_sub(c2, rnd2));
+  uint32_t r = pack_pair<__half>(f2_sub(f2_add(p2, rnd2), rnd2));
+  asm("min.f16x2 %0, %0, %1;" : "+r"(r) : "r"(0x5BF85BF8u));  // 255 in both halves
+  return r;
+}
+
+// Exact floats of a pair of int32 scores (W8A8's fma(s, c, -m) needs s itself).
+__device__ __forceinline__ uint64_t score_pair_f32(uint32_t s0, uint32_t s1) {
+  uint64_t r;
+  asm("{\n\t.reg .f32 a, b;\n\t"
+      "cvt.rn.f32.s32 a, %1;\n\t"
+      "cvt.rn.f32.s32 b, %2;\n\t"
+      "mov.b64 %0, {a, b};\n\t}"
+      : "=l"(r)
+      : "r"(s0), "r"(s1));
+  return r;
 }
 
 // The fast path of a full block: p = exp2(s * c - m_ref) against the current
@@ -268,7 +282,6 @@ __device__ __forceinline__ uint32_t u8_code_pair(uint64_t p2) {
 template <typename TV, bool WAIT_HI, bool W8A8>
 __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
                                              uint64_t (&sum2)[2]) {
-  const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
   int m[4] = {INT32_MIN, INT32_MIN, INT32_MIN, INT32_MIN};
 #pragma unroll
   for (int i = 0; i < kBlockN / 2; ++i) {
@@ -277,7 +290,7 @@ __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx
     if (WAIT_HI && i == kBlockN / 4) tmem_wait_ld_regs(*reinterpret_cast<uint32_t(*)[32]>(v + 32));
     m[i & 3] = __vimax3_s32(m[i & 3], static_cast<int>(v[2 * i]), static_cast<int>(v[2 * i + 1]));
     uint64_t x2;
-    if constexpr (W8A8) x2 = f2_fma(f2_sub(magic_pair(v[2 * i], v[2 * i + 1]), rnd2), cx2, bx2);
+    if constexpr (W8A8) x2 = f2_fma(score_pair_f32(v[2 * i], v[2 * i + 1]), cx2, bx2);
     else x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
     const uint64_t p2 =
         (!W8A8 && ((kPolyPairMask >> (i & 15)) & 1u)) ? exp2_poly_pair(x2) : ex2_pair(x2);
@@ -302,11 +315,10 @@ __device__ __forceinline__ int exp_block_max(uint32_t (&v)[kBlockN], uint64_t cx
 template <typename TV, bool MASKED, bool W8A8>
 __device__ __forceinline__ void exp_block(uint32_t (&v)[kBlockN], uint64_t cx2, uint64_t bx2,
                                           int valid, uint64_t (&sum2)[2]) {
-  const uint64_t rnd2 = f2_pack(12582912.0f, 12582912.0f);
 #pragma unroll
   for (int i = 0; i < kBlockN / 2; ++i) {
     uint64_t x2;
-    if constexpr (W8A8) x2 = f2_fma(f2_sub(magic_pair(v[2 * i], v[2 * i + 1]), rnd2), cx2, bx2);
+    if constexpr (W8A8) x2 = f2_fma(score_pair_f32(v[2 * i], v[2 * i + 1]), cx2, bx2);
     else x2 = f2_fma(magic_pair(v[2 * i], v[2 * i + 1]), cx2, bx2);
     uint64_t p2 = (!W8A8 && ((kPolyPairMask >> (i & 15)) & 1u)) ? exp2_poly_pair(x2) : ex2_pair(x2);
     if constexpr (MASKED) {
