@@ -115,6 +115,51 @@ __global__ void __launch_bounds__(256) codebook_decode_kernel(
   }
 }
 
+// Four codes (nibbles 0..3 of w) looked up in a 16-byte table held in four
+// words: two byte permutes pick entries code & 7 from the low and the high
+// eight entries, a third takes each byte from the high pick where code >= 8.
+__device__ __forceinline__ uint32_t lut16_lookup4(uint32_t w, const uint32_t (&lut)[4]) {
+  const uint32_t sel = w & 0x7777u;
+  const uint32_t lo = __byte_perm(lut[0], lut[1], sel);
+  const uint32_t hi = __byte_perm(lut[2], lut[3], sel);
+  return __byte_perm(lo, hi, 0x3210u | ((w >> 1) & 0x4444u));
+}
+
+// Codebook decode for group sizes that are multiples of 128: one thread per
+// 128 columns of one row, all inside one group, so the group's 16 decoded
+// values (decode_byte of each codebook entry with the group scale, the same
+// bytes as codebook_decode_kernel) are built once and every nibble is a table
+// lookup.
+__global__ void __launch_bounds__(256) codebook_decode_lut_kernel(
+    const int8_t* __restrict__ packed, const uint8_t* __restrict__ group_scale,
+    const float* __restrict__ codebook, int8_t* __restrict__ out, int rows, int k,
+    int group_size) {
+  __shared__ float cb[16];
+  if (threadIdx.x < 16) cb[threadIdx.x] = codebook[threadIdx.x];
+  __syncthreads();
+  const int cpr = k / 128;
+  const int gpr = k / group_size;
+  const int64_t total = static_cast<int64_t>(rows) * cpr;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(v / cpr);
+    const int col = static_cast<int>(v - static_cast<int64_t>(row) * cpr) * 128;
+    const float s = e4m3_to_f32(__ldg(group_scale + static_cast<int64_t>(row) * gpr + col / group_size));
+    uint32_t lut[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int c = 0; c < 16; ++c) lut[c >> 2] |= decode_byte(cb[c], s) << (8 * (c & 3));
+    // Packed rows are k / 2 bytes (8-byte aligned for k % 16 == 0).
+    const uint2* src = reinterpret_cast<const uint2*>(packed + static_cast<int64_t>(row) * (k / 2) + col / 2);
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * k + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint2 w = __ldg(src + q);
+      dst[q] = make_uint4(lut16_lookup4(w.x, lut), lut16_lookup4(w.x >> 16, lut),
+                          lut16_lookup4(w.y, lut), lut16_lookup4(w.y >> 16, lut));
+    }
+  }
+}
+
 // Eight packed nibbles (one 32-bit word, columns 0..7) -> eight int8 values.
 // Per byte, (b ^ 8) - 8 sign-extends a nibble b in [0, 15]; __vsub4 keeps the
 // four byte lanes independent.  Two byte permutes interleave the even-column
@@ -219,6 +264,13 @@ void dequant_launch(const int32_t* acc, int64_t acc_stride, const float* a_s, co
 void codebook_decode_launch(const int8_t* packed, const uint8_t* group_scale,
                             const float* codebook, int8_t* out, int rows, int k, int group_size,
                             cudaStream_t stream) {
+  if (group_size % 128 == 0 && k % 128 == 0) {
+    const int grid = grid_for(static_cast<int64_t>(rows) * (k / 128), 256);
+    codebook_decode_lut_kernel<<<grid, 256, 0, stream>>>(packed, group_scale, codebook, out, rows,
+                                                         k, group_size);
+    TB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int grid = grid_for(static_cast<int64_t>(rows) * (k / 16), 256);
   codebook_decode_kernel<<<grid, 256, 0, stream>>>(packed, group_scale, codebook, out, rows, k,
                                                    group_size);

@@ -2,8 +2,9 @@
 checked exhaustively (or on dense grids) in numpy float32 on the CPU.
 
 * Scores: an INT32 score s with |s| < 2^22 becomes the float 1.5 * 2^23 + s by
-  an integer add to the bits of 1.5 * 2^23 (sage_attn.cu magic_pair), and
-  subtracting 1.5 * 2^23 back gives float(s) exactly, so the W8A8 softmax's
+  an integer add to the bits of 1.5 * 2^23 (sage_attn.cu magic_pair, the Sage
+  softmax), and subtracting 1.5 * 2^23 back gives float(s) exactly (the W8A8
+  softmax takes float(s) with cvt.rn.f32.s32, exact for |s| < 2^24), so its
   fma(s, c, -m) is the reference's fmaf of the exact score.
 * Rounding: v + 1.5 * 2^23 rounds v to the nearest integer, ties to even, for
   |v| < 2^22 (w8a8_quant.cu / convrot.cu code_bits, the W8A8 u8 codes of P),
@@ -11,7 +12,10 @@ checked exhaustively (or on dense grids) in numpy float32 on the CPU.
 * INT8 code -> fp16: the bits 0x6400 | (c ^ 0x80) are the fp16 1024 + (c + 128);
   minus 1152 gives c exactly (w8a8_quant.cu v_codes_kernel).
 * u8 saturation: min(p + 1.5 * 2^23, 1.5 * 2^23 + 255) - 1.5 * 2^23 is
-  rni_sat_u8(p) for p in [0, 2^22) (sage_attn.cu u8_code_pair).
+  rni_sat_u8(p) for p in [0, 2^22); sage_attn.cu u8_code_pair takes the same
+  codes as min(fp16(rni(p)), 255), rni(p) <= 256 being exact in fp16.
+* Codebook table lookup: three byte permutes of a 16-byte table map four
+  4-bit codes to their bytes (elementwise.cu codebook_decode_lut_kernel).
 * PV on the fp16 tensor path: every u8 x s8 product and every sum of 16 of
   them is an integer below 2^24, exact in fp32 and in fp16 operands.
 """
@@ -105,3 +109,38 @@ def test_fma_pipe_exp2_matches_exp2_within_the_p_rounding():
     assert rel.max() <= 8e-5, rel.max()
     # Below the clamp the result is 2^-120 (0 for every later use of p).
     assert _exp2_poly(np.array([-300.0, -121.0], np.float32)).max() <= np.float32(2.0 ** -119)
+
+
+def _byte_perm(x, y, s):
+    """CUDA __byte_perm: byte i of the result is byte (s >> 4i) & 7 of y:x,
+    or that byte's sign replicated when bit 3 of the selector nibble is set."""
+    b = [(x >> (8 * i)) & 0xFF for i in range(4)] + [(y >> (8 * i)) & 0xFF for i in range(4)]
+    r = 0
+    for i in range(4):
+        sel = (s >> (4 * i)) & 0xF
+        v = b[sel & 7]
+        if sel & 8:
+            v = 0xFF if v & 0x80 else 0
+        r |= v << (8 * i)
+    return r
+
+
+def test_codebook_lut_lookup_by_byte_permutes():
+    """codebook_decode_lut_kernel (elementwise.cu) maps four 4-bit codes to
+    their decoded bytes with three byte permutes of a 16-byte table: entries
+    code & 7 of the low and the high halves, then the high pick where code >= 8.
+    Equal to a direct table lookup for random tables and codes."""
+    import random
+
+    rng = random.Random(7)
+    for _ in range(5000):
+        table = [rng.randrange(256) for _ in range(16)]
+        lut = [sum(table[4 * j + i] << (8 * i) for i in range(4)) for j in range(4)]
+        w = rng.getrandbits(32)
+        for part in (w, w >> 16):
+            sel = part & 0x7777
+            lo = _byte_perm(lut[0], lut[1], sel)
+            hi = _byte_perm(lut[2], lut[3], sel)
+            got = _byte_perm(lo, hi, 0x3210 | ((part >> 1) & 0x4444))
+            want = sum(table[(part >> (4 * i)) & 0xF] << (8 * i) for i in range(4))
+            assert got == want
