@@ -537,7 +537,7 @@ int pair_kernel_max_clusters(int epi) {
   TB_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kGemmSmem2)));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * 74, 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(device_sm_count() / 2 * 2), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kGemmSmem2;
   cudaLaunchAttribute attr;
