@@ -145,15 +145,28 @@ __global__ void __launch_bounds__(1024) token_mean_kernel(MeanParams p) {
   const int stripe = t / kTPR;
   const T* in = static_cast<const T*>(p.in) + b * p.sb + h * p.sh;
   double acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int tok = stripe; tok < p.L; tok += kStripes) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(in + static_cast<int64_t>(tok) * p.sl + c8));
+  auto add_row = [&](const uint4& v) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       acc[2 * i] += static_cast<double>(to_f32<T>(w[i] & 0xffffu));
       acc[2 * i + 1] += static_cast<double>(to_f32<T>(w[i] >> 16));
     }
+  };
+  // Four of this thread's token rows are loaded before any is added (one CTA
+  // per head keeps only a few CTAs on the GPU, so each thread keeps several
+  // loads in flight); the rows are still added in increasing token order.
+  int tok = stripe;
+  for (; tok + 3 * kStripes < p.L; tok += 4 * kStripes) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      v[u] = __ldg(reinterpret_cast<const uint4*>(in + static_cast<int64_t>(tok + u * kStripes) * p.sl + c8));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) add_row(v[u]);
   }
+  for (; tok < p.L; tok += kStripes)
+    add_row(__ldg(reinterpret_cast<const uint4*>(in + static_cast<int64_t>(tok) * p.sl + c8)));
   // Fold the stripes that share a warp, then the warps, in a fixed order.
 #pragma unroll
   for (int o = kTPR; o < 32; o <<= 1) {
