@@ -51,6 +51,23 @@ def test_int8_linear_bit_exact_epilogue(oracle, index, case):
     assert np.array_equal(bf16_bits(out), want)
 
 
+@pytest.mark.parametrize("index,case", list(enumerate(CASES)))
+def test_single_cta_form_bit_exact(oracle, monkeypatch, index, case):
+    """TB_GEMM_PAIR=0 selects the single-CTA kernel (the default runs CTA
+    pairs); its accumulators and epilogue are the oracle's too."""
+    monkeypatch.setenv("TB_GEMM_PAIR", "0")
+    m, n, k = case
+    a, w, a_s, w_s, b = _inputs(m, n, k, 4500 + index, bias=index % 2 == 1)
+    acc = kernel.turing_int8_gemm_s32(a.cuda(), w.cuda()).cpu().numpy()
+    want_acc = oracle.int8_gemm_rows(a.numpy(), w.numpy())
+    assert np.array_equal(acc, want_acc)
+    out = kernel.turing_int8_linear(a.cuda(), w.cuda(), a_s.cuda(), w_s.cuda(),
+                                    None if b is None else b.cuda())
+    want = oracle.dequant_bf16(want_acc, a_s.numpy(), w_s.numpy(),
+                               None if b is None else b.float().numpy())
+    assert np.array_equal(bf16_bits(out), want)
+
+
 def test_dequantize_epilogue_bit_exact(oracle):
     g = torch.Generator().manual_seed(2)
     acc = torch.randint(-2 ** 24, 2 ** 24, (37, 80), generator=g, dtype=torch.int32)
